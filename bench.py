@@ -1,0 +1,419 @@
+"""Benchmark: batched square QR (geqrf) throughput on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config C2] [--impl fastqr|reference]
+
+One step = one batched geqrf over the configuration's batch (per GPU), inputs
+resident in HBM, L2 flushed (256 MiB write) before every step.  The headline
+configuration is C2 (256 x 256^2, graded columns): BASELINE.json's configs[1].
+Multi-GPU (torchrun, one process per GPU): weak scaling, each rank factors a
+full configuration batch of its own (contiguous shard of a global batch of
+batch x N), no collective on the data path; time = max over ranks.
+
+Prints ONE JSON line on rank 0.  ``--impl reference`` times the reference's
+own CPU implementation of the path -- torch.geqrf on the host (its
+``ref_kernel``, official/reference.py:125-127, and baseline submission,
+submissions/baseline_geqrf.py:5-6) -- on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path[:0] = [str(ROOT), str(ROOT / "fast-qr_b200")]
+
+import torch  # noqa: E402
+
+from fastqr import inputs  # noqa: E402
+from fastqr.shard import all_ranks_ok, dist_env, max_over_ranks, rank_inputs  # noqa: E402
+
+HBM_FALLBACK_GBS = 6650.0
+BF16_FALLBACK_TFLOPS = 1590.0
+L2_FLUSH_BYTES = 256 << 20
+DEFAULT_STEPS = {"C1": 400, "C2": 200, "C3": 20, "C4": 10, "C5": 3}
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "source": "measured (MEASURED_PEAKS.json)"}
+    return {"hbm_gbs": HBM_FALLBACK_GBS, "bf16_tflops": BF16_FALLBACK_TFLOPS,
+            "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def flops_per_matrix(n: int) -> float:
+    return 4.0 * n ** 3 / 3.0
+
+
+def bytes_per_matrix(n: int) -> float:
+    return 4.0 * (2 * n * n + n)
+
+
+def trailing_flops(n: int, b: int = 32) -> float:
+    """Algorithmic flops of all trailing updates of one matrix:
+    per panel k: 4 (n-k) b (n-k-b) + b^2 (n-k-b)."""
+    tot = 0.0
+    for k in range(0, n, b):
+        m, nc = n - k, n - k - b
+        if nc > 0:
+            tot += 4.0 * m * b * nc + b * b * nc
+    return tot
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.idx)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc is not None:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out = ""
+
+    def summary(self) -> dict:
+        rows = []
+        for line in (self.out or "").strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                rows.append((float(f[1]), float(f[2]), float(f[3]), f[4], f[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        maxmhz = max(r[1] for r in rows)
+        loaded = [r for r in rows if r[2] > 200.0] or rows
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in loaded for i, v in enumerate(r[4]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": maxmhz,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def cpu_reference(cfg_name: str, seed: int, budget_s: float, reps_min: int = 3) -> dict:
+    """torch.geqrf on the host cores over a bounded sample of the workload."""
+    cfg = inputs.CONFIGS[cfg_name]
+    n, batch = cfg["n"], cfg["batch"]
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    # sample size: the whole batch when it is cheap, else fewer matrices
+    probe = inputs.baseline_input(cfg_name, seed=seed, device="cpu", batch=1)
+    t0 = time.perf_counter()
+    torch.geqrf(probe)
+    one = max(time.perf_counter() - t0, 1e-6)
+    sample = int(max(1, min(batch, (budget_s / reps_min) / one)))
+    a = inputs.baseline_input(cfg_name, seed=seed, device="cpu", batch=sample)
+    torch.geqrf(a)  # warm-up
+    times = []
+    start = time.perf_counter()
+    while len(times) < reps_min or (time.perf_counter() - start) < budget_s * 0.5:
+        t0 = time.perf_counter()
+        torch.geqrf(a)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - start > budget_s:
+            break
+    per = statistics.median(times)
+    return {"value": sample / per, "unit": "matrices/s", "cores": threads, "kind": "reference",
+            "sample": f"torch.geqrf (host LAPACK) on {sample} of the {batch} {n}x{n} matrices, "
+                      f"median of {len(times)} reps",
+            "tflops": sample * flops_per_matrix(n) / per / 1e12,
+            "cpu_model": _cpu_model()}
+
+
+def _cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def run_reference(args) -> int:
+    """The reference arm: torch.geqrf on the host cores (rank 0 only).  Each
+    step factors a bounded sample of the configuration's batch, sized so the
+    whole W + K run stays within a few minutes."""
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    cfg = inputs.CONFIGS[args.config]
+    n, batch = cfg["n"], cfg["batch"]
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    probe = inputs.baseline_input(args.config, seed=args.seed, device="cpu", batch=1)
+    torch.geqrf(probe)
+    t0 = time.perf_counter()
+    torch.geqrf(probe)
+    one = max(time.perf_counter() - t0, 1e-6)
+    per_step_budget = min(2.0, 150.0 / (args.warmup + args.steps))
+    sample = int(max(1, min(batch, per_step_budget / one)))
+    a = inputs.baseline_input(args.config, seed=args.seed, device="cpu", batch=sample)
+    for _ in range(args.warmup):
+        torch.geqrf(a)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        torch.geqrf(a)
+        times.append(time.perf_counter() - t0)
+    value = sample * len(times) / sum(times)
+    desc = (f"torch.geqrf (host LAPACK, {threads} threads) on {sample} of the {batch} "
+            f"{n}x{n} matrices per step")
+    line = {
+        "impl": "reference", "metric": f"matrices/s ({args.config} geqrf)", "value": value,
+        "unit": "matrices/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * batch / value, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": _config_block(args, world),
+        "tflops": value * flops_per_matrix(n) / 1e12,
+        "cpu_baseline": {"value": value, "unit": "matrices/s", "cores": threads,
+                         "kind": "reference", "sample": desc},
+        "e2e": {"value": value, "unit": "matrices/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "cpu_model": _cpu_model(),
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def _config_block(args, world) -> dict:
+    cfg = inputs.CONFIGS[args.config]
+    return {"workload": f"{args.config}: {cfg['desc']}", "batch_per_gpu": cfg["batch"], "n": cfg["n"],
+            "global_batch": cfg["batch"] * world, "l2": "flushed before every step (256 MiB write)",
+            "parallelism": f"batch-sharded x{world}, no collective"}
+
+
+def run_fastqr(args) -> int:
+    import torch.distributed as dist
+
+    import fastqr
+
+    rank, world, local = dist_env()
+    if world > 1:
+        torch.cuda.set_device(local)
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local if world > 1 else 0)
+    torch.cuda.set_device(dev)
+    cfg = inputs.CONFIGS[args.config]
+    n, batch = cfg["n"], cfg["batch"]
+    steps = args.steps
+
+    a, first = rank_inputs(args.config, args.seed, world, rank, dev, weak=True)
+    h, tau = fastqr.empty_outputs(batch, n, dev)
+    ws = torch.empty(max(1, fastqr.workspace_bytes(batch, n)), dtype=torch.uint8, device=dev)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        fastqr.geqrf(a, out=(h, tau), workspace=ws)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+
+    # correctness of this rank's output (untimed)
+    sys.path.insert(0, str(ROOT / "tests"))
+    from gpu_gates import gates
+    chk = min(batch, 16)
+    g = gates(a[:chk], h[:chk], tau[:chk], chunk=chk)
+    ok = all_ranks_ok(bool(g["ok"]), dev)
+
+    # timed region: K steps, L2 flush before each (outside the events)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(dev.index) as clk:
+        for i in range(steps):
+            flush.fill_(float(i))
+            starts[i].record(stream)
+            step()
+            ends[i].record(stream)
+        torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    total_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    total_ms = max_over_ranks(total_ms, dev)
+    ms = total_ms / steps
+    value = world * batch / (ms / 1e3)
+
+    # per-kernel times for the roofline: same steps again, kernels timed alone
+    roof = kernel_roofline(args.config, a, h, tau, ws, flush, steps, dev)
+
+    # end to end through the public API with host buffers
+    e2e = end_to_end(a, n, batch, dev, max(3, min(steps, 50)))
+    e2e_value = max_over_ranks(e2e["ms"], dev)
+    e2e_mps = world * batch / (e2e_value / 1e3)
+
+    cpu = None
+    if world == 1 and rank == 0 and not args.no_cpu:
+        budget = {"C1": 10.0, "C2": 10.0, "C3": 20.0, "C4": 20.0, "C5": 30.0}[args.config]
+        r = cpu_reference(args.config, args.seed, budget)
+        cpu = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        cpu["cpu_model"] = r["cpu_model"]
+
+    if rank == 0:
+        line = {
+            "metric": f"matrices/s ({args.config} geqrf)", "value": value, "unit": "matrices/s",
+            "n_gpus": world, "steps": steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded, the reference generator's distributions)",
+            "config": _config_block(args, world),
+            "tflops": value * flops_per_matrix(n) / 1e12,
+            "hbm_gbs_alg": value * bytes_per_matrix(n) / 1e9,
+            "verified": bool(ok),
+            "gate": {k: g[k] for k in ("factor_scaled", "orth_scaled", "recon_rel_f", "orth_rel_f")},
+            "roofline": roof,
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_mps, "unit": "matrices/s", "h2d_bytes_per_step": e2e["h2d"],
+                    "d2h_bytes_per_step": e2e["d2h"]},
+            "gpu_launches": steps * fastqr.launch_count(batch, n),
+            "plan": fastqr.plan(batch, n),
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def kernel_roofline(cfg_name, a, h, tau, ws, flush, steps, dev) -> dict:
+    """Dominant-kernel roofline from per-kernel CUDA events.
+
+    The same K steps are run again through ``fqr_geqrf_f32_profile``, which
+    records an event pair on the launch stream around every kernel; the
+    kernel class with the largest summed time is the dominant one and its
+    algorithmic work per step over its time per step is ``achieved``.
+    """
+    import fastqr
+
+    n = a.shape[-1]
+    batch = a.shape[0]
+    pk = peaks()
+    tot = {}
+    for i in range(steps):
+        flush.fill_(float(i))
+        st = fastqr.geqrf_profile(a, (h, tau), ws)
+        for kname, v in st.items():
+            tot[kname] = tot.get(kname, 0.0) + v
+    per_step_ms = {kname: v / steps for kname, v in tot.items()}
+    dom = max(per_step_ms, key=per_step_ms.get)
+    t = per_step_ms[dom] / 1e3
+    traffic = _traffic_from_profiles(cfg_name)
+    share = {kname: round(v / max(sum(per_step_ms.values()), 1e-12), 4) for kname, v in per_step_ms.items()}
+    base = {"kernel": dom, "stage_ms_per_step": per_step_ms, "stage_share": share,
+            "traffic": traffic, "peak_source": pk["source"]}
+    if dom in ("small", "copy_in"):
+        alg = batch * bytes_per_matrix(n) if dom == "small" else batch * 8.0 * n * n
+        ach = alg / t / 1e9
+        base.update({"bound": "hbm", "achieved": ach, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": ach / pk["hbm_gbs"], "alg_bytes_per_step": alg})
+        return base
+    tf32 = pk["bf16_tflops"] / 2.0
+    if dom == "trailing":
+        alg = batch * trailing_flops(n)
+    else:
+        alg = batch * (flops_per_matrix(n) - trailing_flops(n))
+    ach = alg / t / 1e12
+    base.update({"bound": "tensor", "achieved": ach, "peak": tf32, "unit": "TFLOP/s",
+                 "frac": ach / tf32, "alg_flops_per_step": alg,
+                 "peak_source": pk["source"] + "; TF32 dense peak taken as measured bf16 / 2"})
+    return base
+
+
+def _traffic_from_profiles(cfg_name):
+    p = ROOT / "profiles" / f"traffic_{cfg_name}.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("dram_bytes_per_launch"):
+            return float(line.split()[1])
+    return None
+
+
+def end_to_end(a, n, batch, dev, steps) -> dict:
+    """Same call through the public API with pinned host buffers: H2D of A,
+    geqrf, D2H of H and tau, all inside the events."""
+    import fastqr
+
+    stream = torch.cuda.current_stream(dev)
+    a_host = a.cpu().pin_memory()
+    # host outputs share the device layout, so each D2H is one flat copy
+    h_host = torch.empty_strided((batch, n, n), (n * n, 1, n), dtype=torch.float32, pin_memory=True)
+    t_host = torch.empty((batch, n), dtype=torch.float32, pin_memory=True)
+    a_dev = torch.empty_like(a)
+
+    def one():
+        a_dev.copy_(a_host, non_blocking=True)
+        hh, tt = fastqr.geqrf(a_dev)
+        h_host.copy_(hh, non_blocking=True)
+        t_host.copy_(tt, non_blocking=True)
+
+    for _ in range(2):
+        one()
+    torch.cuda.synchronize(dev)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for _ in range(steps):
+        one()
+    e.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = s.elapsed_time(e) / steps
+    return {"ms": ms, "h2d": batch * n * n * 4, "d2h": batch * (n * n + n) * 4}
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", default="C2", choices=sorted(inputs.CONFIGS))
+    ap.add_argument("--impl", default="fastqr", choices=["fastqr", "reference"])
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    if args.steps is None:
+        args.steps = DEFAULT_STEPS[args.config]
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_fastqr(args)
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

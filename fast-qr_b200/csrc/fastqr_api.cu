@@ -1,0 +1,201 @@
+// C ABI of libfastqr.so (declared in include/fastqr.h).
+//
+// Static dispatch on (batch, n) only:
+//   n <= 64  : one warp per matrix, registers (qr_small.cu)
+//   n >  64  : blocked compact-WY: copy-in, then per 32-column panel a panel
+//              kernel and a trailing-update kernel (qr_blocked.cu)
+// No path inspects matrix values and there is no CPU fallback: a failed
+// launch is reported as a status code.
+#include <cuda_runtime.h>
+#include <stdio.h>
+#include <string.h>
+
+#include "../../include/fastqr.h"
+#include "internal.h"
+
+namespace {
+
+constexpr size_t kWsAlign = 256;
+
+size_t align_up(size_t v) { return (v + kWsAlign - 1) / kWsAlign * kWsAlign; }
+
+bool small_path(int64_t n) { return n <= 64; }
+
+int status_from(cudaError_t e)
+{
+    if (e == cudaSuccess) return FQR_OK;
+    if (e == cudaErrorInvalidValue || e == cudaErrorInvalidConfiguration) return FQR_ELAUNCH;
+    return FQR_ELAUNCH;
+}
+
+}  // namespace
+
+extern "C" {
+
+int fqr_version(void) { return 100; }
+
+const char *fqr_status_string(int status)
+{
+    switch (status) {
+    case FQR_OK: return "ok";
+    case FQR_EINVAL: return "invalid argument (null pointer, negative size or bad stride)";
+    case FQR_EUNSUPPORTED: return "unsupported size (n outside the dispatch table)";
+    case FQR_ELAUNCH: return "kernel launch failed";
+    case FQR_ETIMEOUT: return "device-side bounded wait timed out";
+    case FQR_EWORKSPACE: return "workspace missing or too small";
+    case FQR_ECUDA: return "CUDA runtime error";
+    default: return "unknown status";
+    }
+}
+
+size_t fqr_workspace_bytes(int64_t batch, int64_t n)
+{
+    if (batch <= 0 || n <= 0 || n > FQR_MAX_N || small_path(n)) return 0;
+    // one 32 x 32 T factor per matrix
+    return align_up((size_t)batch * fqr::kPanel * fqr::kPanel * sizeof(float));
+}
+
+int fqr_launch_count(int64_t batch, int64_t n)
+{
+    if (batch <= 0 || n <= 0) return 0;
+    if (n > FQR_MAX_N) return -1;
+    if (small_path(n)) return 1;
+    const int64_t panels = (n + fqr::kPanel - 1) / fqr::kPanel;
+    const int64_t chunks = (batch + 65534) / 65535;
+    // copy-in + per panel (panel + trailing), the last panel has no trailing
+    return (int)(1 + panels + (panels - 1) * chunks);
+}
+
+int fqr_plan_describe(int64_t batch, int64_t n, char *buf, size_t len)
+{
+    if (!buf || len == 0) return FQR_EINVAL;
+    if (n > FQR_MAX_N || n < 0 || batch < 0) {
+        snprintf(buf, len, "unsupported");
+        return FQR_EUNSUPPORTED;
+    }
+    if (small_path(n)) {
+        snprintf(buf, len, "small: warp-per-matrix registers, n<=%d, %lld warps, 1 launch",
+                 n <= 32 ? 32 : 64, (long long)batch);
+    } else {
+        const fqr::PanelShape s = fqr::panel_shape((int)n);
+        snprintf(buf, len,
+                 "blocked: panel %d cols (first panel %d warps x %d row blocks, cluster %d), "
+                 "trailing simt, %d launches",
+                 fqr::kPanel, s.warps, s.rows_per_thread_blocks, s.cluster,
+                 fqr_launch_count(batch, n));
+    }
+    return FQR_OK;
+}
+
+}  // extern "C"
+
+namespace {
+
+// Optional per-stage timing: CUDA events recorded on the launch stream around
+// every kernel, summed per stage after a final stream synchronize.
+struct StageTimer {
+    cudaStream_t st;
+    cudaEvent_t ev[2 * 1024];
+    int stage[1024];
+    int count = 0;
+    bool ok = true;
+    void begin(int s)
+    {
+        if (count >= 1024) { ok = false; return; }
+        if (cudaEventCreate(&ev[2 * count]) != cudaSuccess ||
+            cudaEventCreate(&ev[2 * count + 1]) != cudaSuccess) { ok = false; return; }
+        stage[count] = s;
+        cudaEventRecord(ev[2 * count], st);
+    }
+    void end()
+    {
+        if (!ok) return;
+        cudaEventRecord(ev[2 * count + 1], st);
+        ++count;
+    }
+    int finish(float *ms, int nstages)
+    {
+        cudaError_t e = cudaStreamSynchronize(st);
+        for (int i = 0; i < nstages; ++i) ms[i] = 0.0f;
+        for (int i = 0; i < count; ++i) {
+            float t = 0.0f;
+            if (e == cudaSuccess) cudaEventElapsedTime(&t, ev[2 * i], ev[2 * i + 1]);
+            if (stage[i] < nstages) ms[stage[i]] += t;
+            cudaEventDestroy(ev[2 * i]);
+            cudaEventDestroy(ev[2 * i + 1]);
+        }
+        if (e != cudaSuccess) return FQR_ECUDA;
+        return ok ? FQR_OK : FQR_ELAUNCH;
+    }
+};
+
+int run_geqrf(const float *A, int64_t batch, int64_t n, int64_t a_bstride, int64_t a_rstride,
+              int64_t a_cstride, float *H, float *tau, void *workspace, size_t workspace_bytes,
+              cudaStream_t st, StageTimer *tm)
+{
+    if (batch < 0 || n < 0) return FQR_EINVAL;
+    if (batch == 0 || n == 0) return FQR_OK;
+    if (n > FQR_MAX_N) return FQR_EUNSUPPORTED;
+    if (!A || !H || !tau) return FQR_EINVAL;
+    if (a_rstride == 0 || a_cstride == 0 || (batch > 1 && a_bstride == 0)) return FQR_EINVAL;
+    const int ni = (int)n;
+    cudaError_t e;
+
+    if (small_path(n)) {
+        if (tm) tm->begin(FQR_STAGE_SMALL);
+        e = fqr::launch_small(A, batch, ni, a_bstride, a_rstride, a_cstride, H, tau, st);
+        if (tm) tm->end();
+        return status_from(e);
+    }
+
+    const size_t need = fqr_workspace_bytes(batch, n);
+    if (!workspace || workspace_bytes < need) return FQR_EWORKSPACE;
+    if (((uintptr_t)workspace) % kWsAlign) return FQR_EINVAL;
+    float *Tws = (float *)workspace;
+
+    if (tm) tm->begin(FQR_STAGE_COPY_IN);
+    e = fqr::launch_copy_in(A, batch, ni, a_bstride, a_rstride, a_cstride, H, st);
+    if (tm) tm->end();
+    if (e != cudaSuccess) return status_from(e);
+    for (int k = 0; k < ni; k += fqr::kPanel) {
+        if (tm) tm->begin(FQR_STAGE_PANEL);
+        e = fqr::launch_panel(H, tau, Tws, batch, ni, k, st);
+        if (tm) tm->end();
+        if (e != cudaSuccess) return status_from(e);
+        if (k + fqr::kPanel < ni) {
+            if (tm) tm->begin(FQR_STAGE_TRAILING);
+            e = fqr::launch_trailing(H, Tws, batch, ni, k, st);
+            if (tm) tm->end();
+            if (e != cudaSuccess) return status_from(e);
+        }
+    }
+    return FQR_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int fqr_geqrf_f32(const float *A, int64_t batch, int64_t n, int64_t a_bstride, int64_t a_rstride,
+                  int64_t a_cstride, float *H, float *tau, void *workspace, size_t workspace_bytes,
+                  void *stream)
+{
+    return run_geqrf(A, batch, n, a_bstride, a_rstride, a_cstride, H, tau, workspace,
+                     workspace_bytes, (cudaStream_t)stream, nullptr);
+}
+
+int fqr_geqrf_f32_profile(const float *A, int64_t batch, int64_t n, int64_t a_bstride,
+                          int64_t a_rstride, int64_t a_cstride, float *H, float *tau,
+                          void *workspace, size_t workspace_bytes, void *stream, float *stage_ms)
+{
+    if (!stage_ms) return FQR_EINVAL;
+    StageTimer *tm = new StageTimer();
+    tm->st = (cudaStream_t)stream;
+    int rc = run_geqrf(A, batch, n, a_bstride, a_rstride, a_cstride, H, tau, workspace,
+                       workspace_bytes, (cudaStream_t)stream, tm);
+    int rc2 = tm->finish(stage_ms, FQR_NUM_STAGES);
+    delete tm;
+    return rc != FQR_OK ? rc : rc2;
+}
+
+}  // extern "C"

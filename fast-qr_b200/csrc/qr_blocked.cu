@@ -1,0 +1,526 @@
+// Blocked compact-WY Householder QR for n > 64: copy-in, panel and SIMT
+// trailing-update kernels.
+//
+// Algorithm (tools/blocked_qr_reference.py:98-122,192-262 of the reference,
+// "compact-wy" mode): for each panel of kPanel columns starting at k,
+//   1. factor the (n-k) x 32 panel (unblocked Householder, LAPACK xGEQR2
+//      semantics) and form the 32 x 32 upper-triangular T with
+//      Q_panel = I - V T V^T;
+//   2. update the trailing columns C = H[k:, k+32:] as
+//      C := C - V (T^T (V^T C)).
+// The reference runs the same two steps as panel_factor_kernel /
+// trailing_update_kernel (submissions/candidate.py:2404-2505, :2507-2716), but
+// recomputes T redundantly in every trailing CTA and applies reflectors one
+// by one by default; here the panel kernel forms T once and the trailing
+// update is a blocked product.
+//
+// Working storage is H itself, column-major (column j of matrix b is
+// contiguous): the copy-in kernel transposes the row-major input once.
+#include <cooperative_groups.h>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace cg = cooperative_groups;
+
+namespace fqr {
+
+// ---------------------------------------------------------------------------
+// Copy-in: H(i, j) = A(i, j), column-major H from any-strided A.
+// ---------------------------------------------------------------------------
+
+// Row-major contiguous rows (a_cstride == 1): 32x32 tiles through shared
+// memory so both the reads (rows) and the writes (columns) are coalesced.
+__global__ void __launch_bounds__(256)
+copy_in_rowmajor_kernel(const float *__restrict__ A, int64_t batch, int n, int64_t bs, int64_t rs,
+                        float *__restrict__ H)
+{
+    __shared__ float tile[32][33];
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+    const int j0 = blockIdx.x * 32, i0 = blockIdx.y * 32;
+    for (int64_t b = blockIdx.z; b < batch; b += gridDim.z) {
+        const float *Am = A + b * bs;
+        float *Hm = H + b * (int64_t)n * n;
+#pragma unroll
+        for (int r = ty; r < 32; r += 8) {
+            const int i = i0 + r, j = j0 + tx;
+            tile[r][tx] = (i < n && j < n) ? __ldg(Am + (int64_t)i * rs + j) : 0.0f;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int r = ty; r < 32; r += 8) {
+            const int j = j0 + r, i = i0 + tx;
+            if (i < n && j < n) Hm[(int64_t)j * n + i] = tile[tx][r];
+        }
+        __syncthreads();
+    }
+}
+
+// Any other strides (column-major input included): one thread per element,
+// writes coalesced along columns of H.
+__global__ void __launch_bounds__(256)
+copy_in_strided_kernel(const float *__restrict__ A, int64_t batch, int n, int64_t bs, int64_t rs,
+                       int64_t cs, float *__restrict__ H)
+{
+    const int64_t nn = (int64_t)n * n;
+    const int64_t total = batch * nn;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t b = e / nn;
+        const int64_t r = e - b * nn;
+        const int64_t j = r / n, i = r - j * n;
+        H[e] = __ldg(A + b * bs + i * rs + j * cs);
+    }
+}
+
+cudaError_t launch_copy_in(const float *A, int64_t batch, int n, int64_t bs, int64_t rs, int64_t cs,
+                           float *H, cudaStream_t st)
+{
+    if (cs == 1) {
+        const unsigned t = (unsigned)((n + 31) / 32);
+        dim3 grid(t, t, (unsigned)(batch < 65535 ? batch : 65535));
+        copy_in_rowmajor_kernel<<<grid, 256, 0, st>>>(A, batch, n, bs, rs, H);
+    } else {
+        const int64_t total = batch * (int64_t)n * n;
+        int64_t blocks = (total + 255) / 256;
+        if (blocks > 148 * 64) blocks = 148 * 64;
+        copy_in_strided_kernel<<<(unsigned)blocks, 256, 0, st>>>(A, batch, n, bs, rs, cs, H);
+    }
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Panel kernel.
+//
+// Thread layout: a warp covers blocks of 32 panel rows x 32 columns; lane =
+// cg + 4*rg owns columns 8cg..8cg+7 of rows 4rg..4rg+3 of each block, in
+// registers.  Per column c:
+//   * the 4 x-values of the lane's rows are fetched from the lane of the same
+//     row group that owns column c (4 shuffles per block);
+//   * sigma and the 8 partial dots d_j = x^T a_j are reduced over the 8 row
+//     groups (3 + 7 shuffles: a reduce-scatter leaves column 8cg+rg in lane
+//     (cg, rg)), then over warps through shared memory, then -- for tall
+//     panels split over a thread-block cluster -- over CTAs through
+//     distributed shared memory;
+//   * warp 0 forms the reflector (identical arithmetic in every CTA of the
+//     cluster), w_j = a(c, j) + scale * d_j and tau * w_j, and the T-factor
+//     inputs y_i = v_i^T v_c = w_i for i < c;
+//   * every thread applies the rank-1 update to its 4R x 8 tile.
+// Two CTA barriers per column (plus one cluster barrier when split).
+// T is formed at the end from y and tau:
+//   T(c, c) = tau_c,  T(0:c, c) = -tau_c T(0:c, 0:c) y(0:c, c).
+// ---------------------------------------------------------------------------
+template <int NW, int R, bool CLUSTER>
+__global__ void __launch_bounds__(NW * 32)
+panel_kernel(float *__restrict__ H, float *__restrict__ tau, float *__restrict__ Tws, int n, int k)
+{
+    constexpr int ROWS = NW * 32 * R;  // panel rows held by one CTA
+    constexpr int NR = 4 * R;          // rows per thread
+    __shared__ float red[NW][32];
+    __shared__ float sig_part[NW];
+    __shared__ double sigd_part[NW];
+    __shared__ float rowc[32];
+    __shared__ __align__(16) float tw_s[32];
+    __shared__ float par_f[4];   // beta, tau, scale, robust flag
+    __shared__ double par_d[1];  // scale in double
+    __shared__ int par_wide;
+    __shared__ float Ysm[32][33];
+    __shared__ float tau_s[32];
+    __shared__ float xch[CLUSTER ? 2 : 1][CLUSTER ? 8 : 1][72];
+    __shared__ double xchd[CLUSTER ? 8 : 1];
+
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int cgp = lane & 3, rg = lane >> 2;
+    int crank = 0, ncl = 1;
+    if constexpr (CLUSTER) {
+        cg::cluster_group cl = cg::this_cluster();
+        crank = (int)cl.block_rank();
+        ncl = (int)cl.num_blocks();
+    }
+    const int64_t mat = blockIdx.x / ncl;
+    const int m = n - k;
+    const int w = m < kPanel ? m : kPanel;
+    float *Hm = H + mat * (int64_t)n * n;
+
+    int row[NR];
+    float p[NR][8];
+#pragma unroll
+    for (int q = 0; q < NR; ++q) {
+        row[q] = crank * ROWS + (q >> 2) * (NW * 32) + wid * 32 + 4 * rg + (q & 3);
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) {
+            const int col = 8 * cgp + jj;
+            p[q][jj] = (row[q] < m && col < w) ? Hm[(int64_t)(k + col) * n + k + row[q]] : 0.0f;
+        }
+    }
+
+#pragma unroll 1
+    for (int cb = 0; cb < 4; ++cb) {
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+            const int c = cb * 8 + cc;
+            if (c >= w) break;
+            const int par = c & 1;
+
+            // (1) x for my rows, from lane (cb, rg)
+            float x[NR];
+            float s = 0.0f;
+#pragma unroll
+            for (int q = 0; q < NR; ++q) {
+                // p[q][cc] holds column 8*cgp+cc; the source lane has cgp == cb
+                x[q] = __shfl_sync(kFull, p[q][cc], cb + 4 * rg);
+                const float xm = row[q] > c ? x[q] : 0.0f;
+                s = fmaf(xm, xm, s);
+            }
+            // (2) partial dots over rows > c for my 8 columns
+            float d[8];
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj) {
+                float acc = 0.0f;
+#pragma unroll
+                for (int q = 0; q < NR; ++q) acc = fmaf(row[q] > c ? x[q] : 0.0f, p[q][jj], acc);
+                d[jj] = acc;
+            }
+            // sigma over the 8 row groups (lane bits 2..4)
+            s += __shfl_xor_sync(kFull, s, 4);
+            s += __shfl_xor_sync(kFull, s, 8);
+            s += __shfl_xor_sync(kFull, s, 16);
+            // reduce-scatter of d over row groups: lane (cg, rg) keeps column 8cg+rg
+            {
+                const bool up4 = rg & 4;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float send = up4 ? d[i] : d[i + 4];
+                    const float keep = up4 ? d[i + 4] : d[i];
+                    d[i] = keep + __shfl_xor_sync(kFull, send, 16);
+                }
+                const bool up2 = rg & 2;
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                    const float send = up2 ? d[i] : d[i + 2];
+                    const float keep = up2 ? d[i + 2] : d[i];
+                    d[i] = keep + __shfl_xor_sync(kFull, send, 8);
+                }
+                const bool up1 = rg & 1;
+                const float send = up1 ? d[0] : d[1];
+                const float keep = up1 ? d[1] : d[0];
+                d[0] = keep + __shfl_xor_sync(kFull, send, 4);
+            }
+            red[wid][8 * cgp + rg] = d[0];
+            if (lane == 0) sig_part[wid] = s;
+#pragma unroll
+            for (int q = 0; q < NR; ++q)
+                if (row[q] == c) {
+#pragma unroll
+                    for (int jj = 0; jj < 8; ++jj) rowc[8 * cgp + jj] = p[q][jj];
+                }
+            __syncthreads();  // S1
+
+            float f = 0.0f, sg = 0.0f, rc = 0.0f;
+            if (wid == 0) {
+#pragma unroll
+                for (int u = 0; u < NW; ++u) f += red[u][lane];
+#pragma unroll
+                for (int u = 0; u < NW; ++u) sg += sig_part[u];
+                rc = rowc[lane];
+            }
+            if constexpr (CLUSTER) {
+                cg::cluster_group cl = cg::this_cluster();
+                if (wid == 0) {
+                    for (int qr = 0; qr < ncl; ++qr) {
+                        float *dst = cl.map_shared_rank(&xch[par][crank][0], qr);
+                        dst[lane] = f;
+                        if (lane == 0) dst[32] = sg;
+                        if (crank == 0) dst[33 + lane] = rc;
+                    }
+                }
+                cl.sync();
+                if (wid == 0) {
+                    f = 0.0f;
+                    sg = 0.0f;
+                    for (int qr = 0; qr < ncl; ++qr) {
+                        f += xch[par][qr][lane];
+                        sg += xch[par][qr][32];
+                    }
+                    rc = xch[par][0][33 + lane];
+                }
+            }
+            if (wid == 0) {
+                const float alpha = __shfl_sync(kFull, rc, c);
+                const bool fast = reflector_fast_ok(alpha, sg);
+                if (fast) {
+                    const Reflector r = reflector_from_float(alpha, sg);
+                    const float wl = rc + r.scale * f;
+                    tw_s[lane] = (lane > c) ? r.tau * wl : 0.0f;
+                    if (lane < c) Ysm[lane][c] = wl;
+                    if (lane == 0) {
+                        par_f[0] = r.beta;
+                        par_f[1] = r.tau;
+                        par_f[2] = r.scale;
+                        par_d[0] = r.scale_d;
+                        par_wide = 0;
+                        tau_s[c] = r.tau;
+                    }
+                }
+                if (lane == 0) par_f[3] = fast ? 0.0f : 1.0f;
+            }
+            __syncthreads();  // S2
+
+            if (par_f[3] != 0.0f) {
+                // Rare robust path: sigma again in double, over all rows.
+                double sd = 0.0;
+#pragma unroll
+                for (int q = 0; q < NR; ++q) {
+                    const double xm = row[q] > c ? (double)x[q] : 0.0;
+                    sd = fma(xm, xm, sd);
+                }
+                sd += __shfl_xor_sync(kFull, sd, 4);
+                sd += __shfl_xor_sync(kFull, sd, 8);
+                sd += __shfl_xor_sync(kFull, sd, 16);
+                if (lane == 0) sigd_part[wid] = sd;
+                __syncthreads();
+                double sdt = 0.0;
+                if (wid == 0)
+                    for (int u = 0; u < NW; ++u) sdt += sigd_part[u];
+                if constexpr (CLUSTER) {
+                    cg::cluster_group cl = cg::this_cluster();
+                    if (wid == 0 && lane == 0)
+                        for (int qr = 0; qr < ncl; ++qr) *cl.map_shared_rank(&xchd[crank], qr) = sdt;
+                    cl.sync();
+                    if (wid == 0) {
+                        sdt = 0.0;
+                        for (int qr = 0; qr < ncl; ++qr) sdt += xchd[qr];
+                    }
+                    cl.sync();
+                }
+                if (wid == 0) {
+                    const float alpha = __shfl_sync(kFull, rc, c);
+                    const Reflector r = reflector_from_double(alpha, sdt);
+                    const float sf = r.wide ? (float)(r.scale_d * (double)f) : r.scale * f;
+                    const float wl = rc + sf;
+                    tw_s[lane] = (lane > c) ? r.tau * wl : 0.0f;
+                    if (lane < c) Ysm[lane][c] = wl;
+                    if (lane == 0) {
+                        par_f[0] = r.beta;
+                        par_f[1] = r.tau;
+                        par_f[2] = r.scale;
+                        par_d[0] = r.scale_d;
+                        par_wide = r.wide ? 1 : 0;
+                        tau_s[c] = r.tau;
+                    }
+                }
+                __syncthreads();
+            }
+
+            // (3) rank-1 update of my tile; column c owners store v / beta
+            Reflector r;
+            r.beta = par_f[0];
+            r.tau = par_f[1];
+            r.scale = par_f[2];
+            r.scale_d = par_d[0];
+            r.wide = par_wide != 0;
+            const float4 t0 = *reinterpret_cast<const float4 *>(&tw_s[8 * cgp]);
+            const float4 t1 = *reinterpret_cast<const float4 *>(&tw_s[8 * cgp + 4]);
+            const float twv[8] = {t0.x, t0.y, t0.z, t0.w, t1.x, t1.y, t1.z, t1.w};
+#pragma unroll
+            for (int q = 0; q < NR; ++q) {
+                const float v = row[q] > c ? reflector_apply(r, x[q]) : (row[q] == c ? 1.0f : 0.0f);
+#pragma unroll
+                for (int jj = 0; jj < 8; ++jj) p[q][jj] = fmaf(-twv[jj], v, p[q][jj]);
+                if (cgp == cb) {
+                    if (row[q] > c) p[q][cc] = v;
+                    else if (row[q] == c) p[q][cc] = r.beta;
+                }
+            }
+        }
+    }
+    __syncthreads();
+
+    // T factor (warp 0 of the CTA holding the panel's top rows): lane i owns
+    // row i of T, built column by column; stored column-major.
+    if (crank == 0 && wid == 0) {
+        float trow[32];
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+            // trow[l] == 0 for l < lane, so the sum runs over l in [lane, c)
+            float acc = 0.0f;
+            if (c < w) {
+#pragma unroll
+                for (int l = 0; l < c; ++l) acc = fmaf(trow[l], Ysm[l][c], acc);
+            }
+            const float tc = c < w ? tau_s[c] : 0.0f;
+            trow[c] = lane < c ? -tc * acc : (lane == c ? tc : 0.0f);
+        }
+        float *Tm = Tws + mat * (kPanel * kPanel);
+#pragma unroll
+        for (int c = 0; c < 32; ++c) Tm[c * 32 + lane] = trow[c];
+        if (lane < w) tau[mat * n + k + lane] = tau_s[lane];
+    }
+
+#pragma unroll
+    for (int q = 0; q < NR; ++q) {
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) {
+            const int col = 8 * cgp + jj;
+            if (row[q] < m && col < w) Hm[(int64_t)(k + col) * n + k + row[q]] = p[q][jj];
+        }
+    }
+    if constexpr (CLUSTER) {
+        // keep every CTA's shared memory alive until all remote writes landed
+        cg::this_cluster().sync();
+    }
+}
+
+PanelShape panel_shape(int m)
+{
+    if (m <= 128) return {4, 1, 1};
+    if (m <= 256) return {8, 1, 1};
+    if (m <= 512) return {16, 1, 1};
+    if (m <= 1024) return {16, 2, 1};
+    return {16, 2, (m + 1023) / 1024};
+}
+
+template <int NW, int R>
+static cudaError_t launch_panel_t(float *H, float *tau, float *Tws, int64_t batch, int n, int k,
+                                  int cluster, cudaStream_t st)
+{
+    if (cluster <= 1) {
+        panel_kernel<NW, R, false><<<(unsigned)batch, NW * 32, 0, st>>>(H, tau, Tws, n, k);
+        return cudaGetLastError();
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(batch * cluster), 1, 1);
+    cfg.blockDim = dim3(NW * 32, 1, 1);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)cluster;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, panel_kernel<NW, R, true>, H, tau, Tws, n, k);
+}
+
+cudaError_t launch_panel(float *H, float *tau, float *Tws, int64_t batch, int n, int k,
+                         cudaStream_t st)
+{
+    const PanelShape s = panel_shape(n - k);
+    if (s.cluster > 8) return cudaErrorInvalidValue;
+    if (s.warps == 4) return launch_panel_t<4, 1>(H, tau, Tws, batch, n, k, 1, st);
+    if (s.warps == 8) return launch_panel_t<8, 1>(H, tau, Tws, batch, n, k, 1, st);
+    if (s.rows_per_thread_blocks == 1) return launch_panel_t<16, 1>(H, tau, Tws, batch, n, k, 1, st);
+    return launch_panel_t<16, 2>(H, tau, Tws, batch, n, k, s.cluster, st);
+}
+
+// ---------------------------------------------------------------------------
+// Trailing update (SIMT FP32): C := C - V (T^T (V^T C)) for one 32-column tile
+// of one matrix per CTA.  V is the unit-lower panel H[k:, k:k+32].
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+trailing_simt_kernel(float *__restrict__ H, const float *__restrict__ Tws, int n, int k)
+{
+    __shared__ float Vs[32][33];
+    __shared__ float Cs[32][33];
+    __shared__ float Ws[32][33];
+    __shared__ float Ts[32][33];
+    const int lane = threadIdx.x & 31, tg = threadIdx.x >> 5;
+    const int64_t mat = blockIdx.y;
+    const int c0 = k + kPanel + blockIdx.x * 32;
+    const int nct = (n - c0) < 32 ? (n - c0) : 32;
+    const int m = n - k;
+    float *Hm = H + mat * (int64_t)n * n;
+
+    auto load_chunk = [&](int r0) {
+        const int rr = r0 + lane;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int j = tg + 8 * i;
+            float v = 0.0f;
+            if (rr < m) v = rr > j ? Hm[(int64_t)(k + j) * n + k + rr] : (rr == j ? 1.0f : 0.0f);
+            Vs[lane][j] = v;
+            Cs[lane][j] = (rr < m && j < nct) ? Hm[(int64_t)(c0 + j) * n + k + rr] : 0.0f;
+        }
+    };
+
+    // W = V^T C : thread (c = lane, j = 4tg..4tg+3)
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int r0 = 0; r0 < m; r0 += 32) {
+        load_chunk(r0);
+        __syncthreads();
+#pragma unroll 8
+        for (int r = 0; r < 32; ++r) {
+            const float cv = Cs[r][lane];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) acc[q] = fmaf(Vs[r][4 * tg + q], cv, acc[q]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) Ws[4 * tg + q][lane] = acc[q];
+    const float *Tm = Tws + mat * (kPanel * kPanel);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int cc = tg + 8 * i;
+        Ts[lane][cc] = Tm[cc * 32 + lane];  // T(lane, cc), column-major source
+    }
+    __syncthreads();
+    // Y = T^T W : Y(j, c) = sum_{l <= j} T(l, j) W(l, c)
+    float y[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const int j = 4 * tg + q;
+        float s = 0.0f;
+        for (int l = 0; l <= j; ++l) s = fmaf(Ts[l][j], Ws[l][lane], s);
+        y[q] = s;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < 4; ++q) Ws[4 * tg + q][lane] = y[q];
+    __syncthreads();
+    float yreg[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) yreg[j] = Ws[j][lane];
+
+    // C -= V Y : staged per 32-row chunk, thread (c = lane, rows tg + 8i)
+    for (int r0 = 0; r0 < m; r0 += 32) {
+        load_chunk(r0);
+        __syncthreads();
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int r = tg + 8 * i;
+            float a = Cs[r][lane];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) a = fmaf(-Vs[r][j], yreg[j], a);
+            Cs[r][lane] = a;
+        }
+        __syncthreads();
+        const int rr = r0 + lane;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int j = tg + 8 * i;
+            if (rr < m && j < nct) Hm[(int64_t)(c0 + j) * n + k + rr] = Cs[lane][j];
+        }
+        __syncthreads();
+    }
+}
+
+cudaError_t launch_trailing(float *H, const float *Tws, int64_t batch, int n, int k,
+                            cudaStream_t st)
+{
+    const int nc = n - k - kPanel;
+    if (nc <= 0) return cudaSuccess;
+    const unsigned tiles = (unsigned)((nc + 31) / 32);
+    for (int64_t b0 = 0; b0 < batch; b0 += 65535) {
+        const int64_t nb = (batch - b0) < 65535 ? (batch - b0) : 65535;
+        dim3 grid(tiles, (unsigned)nb);
+        trailing_simt_kernel<<<grid, 256, 0, st>>>(H + b0 * (int64_t)n * n, Tws + b0 * kPanel * kPanel,
+                                                   n, k);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
+}  // namespace fqr

@@ -1,0 +1,128 @@
+"""PyTorch-facing entry points.
+
+``custom_kernel(data) -> (H, tau)`` mirrors the reference's submission entry
+(official/submission.py:5-6, submissions/candidate.py:8383-8415): a CUDA
+float32 tensor ``[batch, n, n]`` goes in; ``H`` (same shape, column-major per
+matrix, strides ``(n*n, 1, n)`` like torch.geqrf) and ``tau`` (``[batch, n]``)
+come out, with torch.geqrf's values.  ``geqrf`` is the same call with a
+torch.geqrf-like name and optional preallocated outputs.
+
+Everything runs on the caller's current CUDA stream through the C ABI
+(``fqr_geqrf_f32``).  There is no CPU or torch.geqrf fallback: a CPU tensor,
+a wrong dtype or a failing kernel raises.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from ._lib import FastQRError, load
+
+
+def _check_input(a: torch.Tensor) -> torch.Tensor:
+    if not isinstance(a, torch.Tensor):
+        raise TypeError("input must be a torch.Tensor")
+    if a.device.type != "cuda":
+        raise ValueError("fastqr runs on CUDA tensors only (no CPU fallback)")
+    if a.dtype != torch.float32:
+        raise ValueError(f"input dtype must be torch.float32, got {a.dtype}")
+    if a.ndim == 2:
+        a = a.unsqueeze(0)
+    if a.ndim != 3 or a.shape[-1] != a.shape[-2]:
+        raise ValueError(f"input must have shape (batch, n, n), got {tuple(a.shape)}")
+    return a
+
+
+def workspace_bytes(batch: int, n: int) -> int:
+    return int(load().fqr_workspace_bytes(batch, n))
+
+
+def plan(batch: int, n: int) -> str:
+    buf = ctypes.create_string_buffer(256)
+    rc = load().fqr_plan_describe(batch, n, buf, 256)
+    if rc:
+        raise FastQRError(rc, "fqr_plan_describe")
+    return buf.value.decode()
+
+
+def launch_count(batch: int, n: int) -> int:
+    return int(load().fqr_launch_count(batch, n))
+
+
+def empty_outputs(batch: int, n: int, device) -> tuple[torch.Tensor, torch.Tensor]:
+    """Column-major H (strides (n*n, 1, n)) and contiguous tau, as torch.geqrf
+    returns them (reference allocator: submissions/candidate.py:3752-3798)."""
+    h = torch.empty_strided((batch, n, n), (n * n, 1, n), device=device, dtype=torch.float32)
+    tau = torch.empty((batch, n), device=device, dtype=torch.float32)
+    return h, tau
+
+
+def geqrf(a: torch.Tensor, *, out: tuple[torch.Tensor, torch.Tensor] | None = None,
+          workspace: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Batched Householder QR of square float32 CUDA matrices.
+
+    Returns ``(H, tau)`` as torch.geqrf does.  ``out`` may supply
+    preallocated outputs (H must have strides (n*n, 1, n)); ``workspace`` a
+    uint8 CUDA tensor of at least ``workspace_bytes(batch, n)`` bytes.
+    """
+    squeeze = a.ndim == 2
+    a = _check_input(a)
+    batch, n, _ = a.shape
+    lib = load()
+    if out is None:
+        h, tau = empty_outputs(batch, n, a.device)
+    else:
+        h, tau = out
+        if h.shape != (batch, n, n) or h.stride() != (n * n, 1, n) or h.dtype != torch.float32:
+            raise ValueError("out H must be float32 (batch, n, n) with strides (n*n, 1, n)")
+        if tau.shape != (batch, n) or not tau.is_contiguous() or tau.dtype != torch.float32:
+            raise ValueError("out tau must be contiguous float32 (batch, n)")
+        if h.device != a.device or tau.device != a.device:
+            raise ValueError("outputs must be on the input's device")
+    need = int(lib.fqr_workspace_bytes(batch, n))
+    if need:
+        if workspace is None:
+            workspace = torch.empty(need, dtype=torch.uint8, device=a.device)
+        elif workspace.numel() * workspace.element_size() < need or workspace.device != a.device:
+            raise ValueError(f"workspace needs {need} bytes on {a.device}")
+        ws_ptr, ws_len = workspace.data_ptr(), workspace.numel() * workspace.element_size()
+    else:
+        ws_ptr, ws_len = None, 0
+    with torch.cuda.device(a.device):
+        stream = torch.cuda.current_stream(a.device).cuda_stream
+        bs, rs, cs = a.stride()
+        rc = lib.fqr_geqrf_f32(a.data_ptr(), batch, n, bs, rs, cs, h.data_ptr(), tau.data_ptr(),
+                               ws_ptr, ws_len, stream)
+    if rc:
+        raise FastQRError(rc)
+    if squeeze:
+        return h[0], tau[0]
+    return h, tau
+
+
+def geqrf_profile(a: torch.Tensor, out, workspace) -> dict:
+    """Run one geqrf with a CUDA event pair around every kernel (blocking).
+    Returns the summed device milliseconds per kernel class."""
+    from ._lib import STAGES
+
+    a = _check_input(a)
+    batch, n, _ = a.shape
+    h, tau = out
+    lib = load()
+    ms = (ctypes.c_float * len(STAGES))()
+    ws_ptr = workspace.data_ptr() if workspace is not None else None
+    ws_len = workspace.numel() * workspace.element_size() if workspace is not None else 0
+    with torch.cuda.device(a.device):
+        stream = torch.cuda.current_stream(a.device).cuda_stream
+        bs, rs, cs = a.stride()
+        rc = lib.fqr_geqrf_f32_profile(a.data_ptr(), batch, n, bs, rs, cs, h.data_ptr(),
+                                       tau.data_ptr(), ws_ptr, ws_len, stream, ms)
+    if rc:
+        raise FastQRError(rc, "fqr_geqrf_f32_profile")
+    return {name: float(ms[i]) for i, name in enumerate(STAGES)}
+
+
+def custom_kernel(data: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """The reference's submission contract: ``custom_kernel(data) -> (H, tau)``."""
+    return geqrf(data)

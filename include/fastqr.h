@@ -1,0 +1,119 @@
+/*
+ * fastqr -- batched square Householder QR (geqrf) for NVIDIA B200 (sm_100a).
+ *
+ * C ABI of libfastqr.so.  Plain pointers and sizes only; every pointer below
+ * is a CUDA device pointer unless stated otherwise, and `stream` is a
+ * cudaStream_t passed as void*.  All calls are asynchronous on `stream`: they
+ * validate arguments on the host, enqueue kernels and return.  The library
+ * allocates no device memory on this path; scratch space is caller-owned
+ * (see fqr_workspace_bytes).  Calls are reentrant: the only global state is a
+ * per-device cache of SM count and kernel attributes.
+ *
+ * Output layout (the contract of torch.geqrf, and of the reference's
+ * `custom_kernel(data) -> (H, tau)`):
+ *   H   : float32, column-major per matrix, element (i, j) of matrix b at
+ *         H[b*n*n + j*n + i]  (strides (n*n, 1, n) in elements).  R is on and
+ *         above the diagonal, the Householder vectors v_j (implicit unit
+ *         diagonal) below it.
+ *   tau : float32 [batch][n] contiguous.  tau[b][n-1] is always 0.
+ * Reflector convention (LAPACK xLARFG): H_j = I - tau_j v_j v_j^T with
+ * beta_j = -sign(alpha_j) * ||[alpha_j; x_j]||; tau_j = 0 when x_j == 0.
+ */
+#ifndef FASTQR_H
+#define FASTQR_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes.  The reference reports failures by raising from its pybind
+ * entry points (TORCH_CHECK / C10_CUDA_KERNEL_LAUNCH_CHECK,
+ * submissions/candidate.py:111-125, :1333-1353); this ABI returns codes. */
+enum {
+    FQR_OK = 0,
+    FQR_EINVAL = 1,        /* null pointer, negative size, bad stride */
+    FQR_EUNSUPPORTED = 2,  /* n outside the dispatch table */
+    FQR_ELAUNCH = 3,       /* a kernel launch failed */
+    FQR_ETIMEOUT = 4,      /* a bounded device-side wait gave up */
+    FQR_EWORKSPACE = 5,    /* workspace missing or too small */
+    FQR_ECUDA = 6          /* other CUDA runtime error (no device, ...) */
+};
+
+/* Largest supported n. */
+#define FQR_MAX_N 8192
+
+/*
+ * Batched QR of `batch` float32 n x n matrices.
+ *
+ * Replaces the reference's submission entry point
+ *   custom_kernel(data) -> (H, tau)       submissions/candidate.py:8383-8415
+ *                                         (contract: official/submission.py:5-6,
+ *                                          official/task.py:4-5)
+ * and the extension entries it dispatches to
+ *   geqrf32(data, h, tau)                 submissions/candidate.py:111-125
+ *   geqrf512_blocked(data, h, tau, ...)   submissions/candidate.py:1333-1353
+ * with caller-allocated H / tau as there.
+ *
+ * A: element (i, j) of matrix b at A[b*a_bstride + i*a_rstride + j*a_cstride]
+ *    (strides in elements; the reference passes row-major contiguous input,
+ *    a_bstride = n*n, a_rstride = n, a_cstride = 1).  A is read only.
+ * H, tau: outputs as described above; must not overlap A.
+ * workspace: device scratch of at least fqr_workspace_bytes(batch, n) bytes,
+ *    256-byte aligned (may be NULL when that size is 0).
+ * Returns FQR_OK once the work is enqueued.
+ */
+int fqr_geqrf_f32(const float *A, int64_t batch, int64_t n, int64_t a_bstride,
+                  int64_t a_rstride, int64_t a_cstride, float *H, float *tau,
+                  void *workspace, size_t workspace_bytes, void *stream);
+
+/* Scratch bytes fqr_geqrf_f32 needs for (batch, n); 0 for the small-n path.
+ * Replaces the reference's cached workspace sizing
+ * (submissions/candidate.py:3682-3851), which allocated inside the call. */
+size_t fqr_workspace_bytes(int64_t batch, int64_t n);
+
+/* Static string for a status code. */
+const char *fqr_status_string(int status);
+
+/* Writes a one-line description of the kernel plan chosen for (batch, n)
+ * into buf (NUL-terminated, truncated to len).  Returns FQR_OK or
+ * FQR_EUNSUPPORTED.  The plan depends only on (batch, n) and the device's SM
+ * count -- never on matrix values (the reference's data-dependent routing,
+ * submissions/candidate.py:7779-8381, is deliberately absent). */
+int fqr_plan_describe(int64_t batch, int64_t n, char *buf, size_t len);
+
+/* Number of kernel launches fqr_geqrf_f32 enqueues for (batch, n). */
+int fqr_launch_count(int64_t batch, int64_t n);
+
+/* Kernel classes timed by fqr_geqrf_f32_profile. */
+enum {
+    FQR_STAGE_SMALL = 0,     /* warp-per-matrix kernel (n <= 64) */
+    FQR_STAGE_COPY_IN = 1,   /* row-major A -> column-major H */
+    FQR_STAGE_PANEL = 2,     /* panel factorisation + T factor */
+    FQR_STAGE_TRAILING = 3,  /* trailing update C -= V T^T V^T C */
+    FQR_NUM_STAGES = 4
+};
+
+/*
+ * Diagnostic twin of fqr_geqrf_f32: identical launches, with a CUDA event
+ * pair recorded on `stream` around every kernel; synchronizes `stream` before
+ * returning and writes the summed device time per stage (milliseconds) into
+ * stage_ms[FQR_NUM_STAGES].  Not for production use (it blocks the host).
+ * No counterpart in the reference, which never times its kernels
+ * individually.
+ */
+int fqr_geqrf_f32_profile(const float *A, int64_t batch, int64_t n, int64_t a_bstride,
+                          int64_t a_rstride, int64_t a_cstride, float *H, float *tau,
+                          void *workspace, size_t workspace_bytes, void *stream,
+                          float *stage_ms);
+
+/* Library version, e.g. 100 for 0.1.0. */
+int fqr_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FASTQR_H */

@@ -1,0 +1,75 @@
+"""The C-ABI library loads and exports every declared symbol (CPU only:
+no call here reaches the GPU; argument validation returns before any CUDA
+call)."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+import fastqr
+from fastqr import _lib
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "fastqr.h"
+
+
+def declared_symbols():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"\b(fqr_\w+)\s*\(", text)))
+
+
+def test_header_declares_the_bound_symbols():
+    assert declared_symbols() == sorted(_lib.SIGNATURES)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(str(fastqr.LIB_PATH))
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+    fastqr.load()
+
+
+def test_status_strings_and_version():
+    lib = fastqr.load()
+    for code in range(7):
+        assert lib.fqr_status_string(code)
+    assert lib.fqr_status_string(99) == b"unknown status"
+    assert lib.fqr_version() >= 100
+
+
+def test_argument_validation_without_gpu():
+    lib = fastqr.load()
+    # null pointers
+    assert lib.fqr_geqrf_f32(None, 2, 8, 64, 8, 1, None, None, None, 0, None) == 1
+    # negative sizes
+    assert lib.fqr_geqrf_f32(None, -1, 8, 64, 8, 1, None, None, None, 0, None) == 1
+    # empty problems are a no-op
+    assert lib.fqr_geqrf_f32(None, 0, 8, 64, 8, 1, None, None, None, 0, None) == 0
+    assert lib.fqr_geqrf_f32(None, 4, 0, 0, 0, 1, None, None, None, 0, None) == 0
+    # n outside the dispatch table
+    assert lib.fqr_geqrf_f32(None, 1, 8193, 1, 1, 1, None, None, None, 0, None) == 2
+    # zero strides
+    dummy = ctypes.c_void_p(16)
+    assert lib.fqr_geqrf_f32(dummy, 1, 8, 64, 0, 1, dummy, dummy, None, 0, None) == 1
+    # blocked path without workspace
+    assert lib.fqr_geqrf_f32(dummy, 1, 100, 10000, 100, 1, dummy, dummy, None, 0, None) == 5
+
+
+def test_workspace_and_plan_depend_on_shape_only():
+    assert fastqr.workspace_bytes(1024, 32) == 0
+    assert fastqr.workspace_bytes(256, 256) == 256 * 32 * 32 * 4
+    assert fastqr.workspace_bytes(3, 100) % 256 == 0
+    assert fastqr.plan(1024, 32).startswith("small")
+    assert fastqr.plan(256, 256).startswith("blocked")
+    assert "cluster 4" in fastqr.plan(16, 4096)
+    with pytest.raises(fastqr.FastQRError):
+        fastqr.plan(1, 10000)
+    assert fastqr.launch_count(1024, 32) == 1
+    assert fastqr.launch_count(256, 256) == 1 + 8 + 7
+
+
+def test_python_api_rejects_cpu_tensors():
+    import torch
+    with pytest.raises(ValueError):
+        fastqr.geqrf(torch.zeros(2, 8, 8))
