@@ -26,9 +26,38 @@ struct Reflector {
     bool wide;
 };
 
-// Fast path valid when sigma and alpha are far from float over/underflow.
+// The fast kernels form the dot products d_j = x^T a_j with the UNSCALED tail
+// x in the same reduction as sigma = ||x||^2 (one reduction per column instead
+// of LAPACK's two) and rescale afterwards: w_j = a(k,j) + scale * d_j.  That is
+// exact arithmetic-wise but the products x_i a_ij can over/underflow when x is
+// far from unit scale.  The fast path is therefore taken only when
+//   sigma in [1e-20, 1e20]  (||x|| in [1e-10, 1e10]) and |alpha| <= 1e15,
+// and, checked after the reduction, every d_j is finite and not in the
+// denormal-product regime (0 < |d_j| < 1e-30).  Otherwise the column is redone
+// in LAPACK order: sigma in double, v = x / (alpha - beta), then w_j = v^T a_j.
+constexpr float kSigmaLo = 1e-20f;
+constexpr float kSigmaHi = 1e20f;
+constexpr float kAlphaHi = 1e15f;
+constexpr float kDotTiny = 1e-30f;
+
 __device__ __forceinline__ bool reflector_fast_ok(float alpha, float sigma) {
-    return sigma >= 1e-30f && sigma <= 1e30f && fabsf(alpha) <= 1e15f;
+    return sigma >= kSigmaLo && sigma <= kSigmaHi && fabsf(alpha) <= kAlphaHi;
+}
+
+// A fused dot product that the fast path may not use.
+__device__ __forceinline__ bool dot_unsafe(float d, float w) {
+    return !isfinite(w) || (d != 0.0f && fabsf(d) < kDotTiny);
+}
+
+// tau = 0 reflector (exactly zero tail): H = I, v = x = 0.
+__device__ __forceinline__ Reflector reflector_identity(float alpha) {
+    Reflector r;
+    r.beta = alpha;
+    r.tau = 0.0f;
+    r.scale = 1.0f;
+    r.scale_d = 1.0;
+    r.wide = false;
+    return r;
 }
 
 __device__ __forceinline__ Reflector reflector_from_float(float alpha, float sigma) {

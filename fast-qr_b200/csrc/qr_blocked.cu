@@ -111,13 +111,15 @@ cudaError_t launch_copy_in(const float *A, int64_t batch, int n, int64_t bs, int
 //   T(c, c) = tau_c,  T(0:c, c) = -tau_c T(0:c, 0:c) y(0:c, c).
 // ---------------------------------------------------------------------------
 template <int NW, int R, bool CLUSTER>
-__global__ void __launch_bounds__(NW * 32)
+__global__ void __launch_bounds__(NW * 32, 1)
 panel_kernel(float *__restrict__ H, float *__restrict__ tau, float *__restrict__ Tws, int n, int k)
 {
     constexpr int ROWS = NW * 32 * R;  // panel rows held by one CTA
     constexpr int NR = 4 * R;          // rows per thread
+    constexpr int XS = 68;             // exchange slots: 32 dots, sigma, nz flag, 32 row-c values
     __shared__ float red[NW][32];
     __shared__ float sig_part[NW];
+    __shared__ int nz_part[NW];
     __shared__ double sigd_part[NW];
     __shared__ float rowc[32];
     __shared__ __align__(16) float tw_s[32];
@@ -126,7 +128,9 @@ panel_kernel(float *__restrict__ H, float *__restrict__ tau, float *__restrict__
     __shared__ int par_wide;
     __shared__ float Ysm[32][33];
     __shared__ float tau_s[32];
-    __shared__ float xch[CLUSTER ? 2 : 1][CLUSTER ? 8 : 1][72];
+    __shared__ float alpha_s;
+    __shared__ float xch[CLUSTER ? 2 : 1][CLUSTER ? 8 : 1][XS];
+    __shared__ float xrb[CLUSTER ? 8 : 1][32];
     __shared__ double xchd[CLUSTER ? 8 : 1];
 
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
@@ -154,6 +158,52 @@ panel_kernel(float *__restrict__ H, float *__restrict__ tau, float *__restrict__
         }
     }
 
+    // Reduce-scatter of 8 per-lane values over the 8 row groups of a warp
+    // (lane bits 2..4): lane (cg, rg) ends with the warp sum for column 8cg+rg.
+    auto reduce_scatter8 = [&](float (&d)[8]) -> float {
+        const bool up4 = rg & 4;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float send = up4 ? d[i] : d[i + 4];
+            const float keep = up4 ? d[i + 4] : d[i];
+            d[i] = keep + __shfl_xor_sync(kFull, send, 16);
+        }
+        const bool up2 = rg & 2;
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const float send = up2 ? d[i] : d[i + 2];
+            const float keep = up2 ? d[i + 2] : d[i];
+            d[i] = keep + __shfl_xor_sync(kFull, send, 8);
+        }
+        const bool up1 = rg & 1;
+        const float send = up1 ? d[0] : d[1];
+        const float keep = up1 ? d[1] : d[0];
+        return keep + __shfl_xor_sync(kFull, send, 4);
+    };
+
+    // Warp 0 publishes the reflector and the update coefficients tau * w_l.
+    auto publish = [&](const Reflector &r, int c, float wl) {
+        tw_s[lane] = (lane > c) ? r.tau * wl : 0.0f;
+        if (lane < c) Ysm[lane][c] = wl;  // y_l = v_l^T v_c
+        if (lane == 0) {
+            par_f[0] = r.beta;
+            par_f[1] = r.tau;
+            par_f[2] = r.scale;
+            par_d[0] = r.scale_d;
+            par_wide = r.wide ? 1 : 0;
+            tau_s[c] = r.tau;
+        }
+    };
+    auto read_params = [&]() {
+        Reflector r;
+        r.beta = par_f[0];
+        r.tau = par_f[1];
+        r.scale = par_f[2];
+        r.scale_d = par_d[0];
+        r.wide = par_wide != 0;
+        return r;
+    };
+
 #pragma unroll 1
     for (int cb = 0; cb < 4; ++cb) {
 #pragma unroll
@@ -162,17 +212,18 @@ panel_kernel(float *__restrict__ H, float *__restrict__ tau, float *__restrict__
             if (c >= w) break;
             const int par = c & 1;
 
-            // (1) x for my rows, from lane (cb, rg)
+            // (1) x for my rows, from lane (cb, rg) (p[q][cc] holds column 8*cgp+cc)
             float x[NR];
             float s = 0.0f;
+            bool nz = false;
 #pragma unroll
             for (int q = 0; q < NR; ++q) {
-                // p[q][cc] holds column 8*cgp+cc; the source lane has cgp == cb
                 x[q] = __shfl_sync(kFull, p[q][cc], cb + 4 * rg);
                 const float xm = row[q] > c ? x[q] : 0.0f;
                 s = fmaf(xm, xm, s);
+                nz |= (xm != 0.0f);
             }
-            // (2) partial dots over rows > c for my 8 columns
+            // (2) unscaled partial dots over rows > c for my 8 columns
             float d[8];
 #pragma unroll
             for (int jj = 0; jj < 8; ++jj) {
@@ -181,33 +232,15 @@ panel_kernel(float *__restrict__ H, float *__restrict__ tau, float *__restrict__
                 for (int q = 0; q < NR; ++q) acc = fmaf(row[q] > c ? x[q] : 0.0f, p[q][jj], acc);
                 d[jj] = acc;
             }
-            // sigma over the 8 row groups (lane bits 2..4)
             s += __shfl_xor_sync(kFull, s, 4);
             s += __shfl_xor_sync(kFull, s, 8);
             s += __shfl_xor_sync(kFull, s, 16);
-            // reduce-scatter of d over row groups: lane (cg, rg) keeps column 8cg+rg
-            {
-                const bool up4 = rg & 4;
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const float send = up4 ? d[i] : d[i + 4];
-                    const float keep = up4 ? d[i + 4] : d[i];
-                    d[i] = keep + __shfl_xor_sync(kFull, send, 16);
-                }
-                const bool up2 = rg & 2;
-#pragma unroll
-                for (int i = 0; i < 2; ++i) {
-                    const float send = up2 ? d[i] : d[i + 2];
-                    const float keep = up2 ? d[i + 2] : d[i];
-                    d[i] = keep + __shfl_xor_sync(kFull, send, 8);
-                }
-                const bool up1 = rg & 1;
-                const float send = up1 ? d[0] : d[1];
-                const float keep = up1 ? d[1] : d[0];
-                d[0] = keep + __shfl_xor_sync(kFull, send, 4);
+            const bool wnz = __any_sync(kFull, nz);
+            red[wid][8 * cgp + rg] = reduce_scatter8(d);
+            if (lane == 0) {
+                sig_part[wid] = s;
+                nz_part[wid] = wnz ? 1 : 0;
             }
-            red[wid][8 * cgp + rg] = d[0];
-            if (lane == 0) sig_part[wid] = s;
 #pragma unroll
             for (int q = 0; q < NR; ++q)
                 if (row[q] == c) {
@@ -217,11 +250,14 @@ panel_kernel(float *__restrict__ H, float *__restrict__ tau, float *__restrict__
             __syncthreads();  // S1
 
             float f = 0.0f, sg = 0.0f, rc = 0.0f;
+            int anynz = 0;
             if (wid == 0) {
 #pragma unroll
-                for (int u = 0; u < NW; ++u) f += red[u][lane];
-#pragma unroll
-                for (int u = 0; u < NW; ++u) sg += sig_part[u];
+                for (int u = 0; u < NW; ++u) {
+                    f += red[u][lane];
+                    sg += sig_part[u];
+                    anynz |= nz_part[u];
+                }
                 rc = rowc[lane];
             }
             if constexpr (CLUSTER) {
@@ -230,44 +266,47 @@ panel_kernel(float *__restrict__ H, float *__restrict__ tau, float *__restrict__
                     for (int qr = 0; qr < ncl; ++qr) {
                         float *dst = cl.map_shared_rank(&xch[par][crank][0], qr);
                         dst[lane] = f;
-                        if (lane == 0) dst[32] = sg;
-                        if (crank == 0) dst[33 + lane] = rc;
+                        if (lane == 0) {
+                            dst[32] = sg;
+                            dst[33] = (float)anynz;
+                        }
+                        if (crank == 0) dst[34 + lane] = rc;
                     }
                 }
                 cl.sync();
                 if (wid == 0) {
                     f = 0.0f;
                     sg = 0.0f;
+                    anynz = 0;
                     for (int qr = 0; qr < ncl; ++qr) {
                         f += xch[par][qr][lane];
                         sg += xch[par][qr][32];
+                        anynz |= xch[par][qr][33] != 0.0f;
                     }
-                    rc = xch[par][0][33 + lane];
+                    rc = xch[par][0][34 + lane];
                 }
             }
+            // alpha = a(c, c); identical in every lane of warp 0 (and every CTA)
+            const float alpha = __shfl_sync(kFull, rc, c);
+            if (wid == 0 && lane == 0) alpha_s = alpha;
             if (wid == 0) {
-                const float alpha = __shfl_sync(kFull, rc, c);
-                const bool fast = reflector_fast_ok(alpha, sg);
-                if (fast) {
-                    const Reflector r = reflector_from_float(alpha, sg);
-                    const float wl = rc + r.scale * f;
-                    tw_s[lane] = (lane > c) ? r.tau * wl : 0.0f;
-                    if (lane < c) Ysm[lane][c] = wl;
-                    if (lane == 0) {
-                        par_f[0] = r.beta;
-                        par_f[1] = r.tau;
-                        par_f[2] = r.scale;
-                        par_d[0] = r.scale_d;
-                        par_wide = 0;
-                        tau_s[c] = r.tau;
-                    }
+                bool fast;
+                Reflector r = reflector_identity(alpha);
+                if (!anynz) {
+                    fast = true;
+                } else {
+                    fast = reflector_fast_ok(alpha, sg);
+                    if (fast) r = reflector_from_float(alpha, sg);
                 }
+                const float wl = rc + r.scale * f;
+                if (fast && anynz) fast = !__any_sync(kFull, dot_unsafe(f, wl));
+                if (fast) publish(r, c, wl);
                 if (lane == 0) par_f[3] = fast ? 0.0f : 1.0f;
             }
             __syncthreads();  // S2
 
             if (par_f[3] != 0.0f) {
-                // Rare robust path: sigma again in double, over all rows.
+                // Robust path, LAPACK order.  Round 1: sigma in double.
                 double sd = 0.0;
 #pragma unroll
                 for (int q = 0; q < NR; ++q) {
@@ -280,45 +319,50 @@ panel_kernel(float *__restrict__ H, float *__restrict__ tau, float *__restrict__
                 if (lane == 0) sigd_part[wid] = sd;
                 __syncthreads();
                 double sdt = 0.0;
-                if (wid == 0)
-                    for (int u = 0; u < NW; ++u) sdt += sigd_part[u];
+                for (int u = 0; u < NW; ++u) sdt += sigd_part[u];
                 if constexpr (CLUSTER) {
                     cg::cluster_group cl = cg::this_cluster();
                     if (wid == 0 && lane == 0)
                         for (int qr = 0; qr < ncl; ++qr) *cl.map_shared_rank(&xchd[crank], qr) = sdt;
                     cl.sync();
-                    if (wid == 0) {
-                        sdt = 0.0;
-                        for (int qr = 0; qr < ncl; ++qr) sdt += xchd[qr];
+                    sdt = 0.0;
+                    for (int qr = 0; qr < ncl; ++qr) sdt += xchd[qr];
+                }
+                // every thread forms the same reflector (same operands, same order)
+                const float alpha_all = alpha_s;
+                const Reflector r = reflector_from_double(alpha_all, sdt);
+                // Round 2: w_l = v^T a_l over rows >= c with the scaled v
+#pragma unroll
+                for (int jj = 0; jj < 8; ++jj) {
+                    float acc = 0.0f;
+#pragma unroll
+                    for (int q = 0; q < NR; ++q) {
+                        const float v = row[q] > c ? reflector_apply(r, x[q]) : (row[q] == c ? 1.0f : 0.0f);
+                        acc = fmaf(v, p[q][jj], acc);
                     }
+                    d[jj] = acc;
+                }
+                red[wid][8 * cgp + rg] = reduce_scatter8(d);
+                __syncthreads();
+                float wl = 0.0f;
+                if (wid == 0)
+                    for (int u = 0; u < NW; ++u) wl += red[u][lane];
+                if constexpr (CLUSTER) {
+                    cg::cluster_group cl = cg::this_cluster();
+                    if (wid == 0)
+                        for (int qr = 0; qr < ncl; ++qr) cl.map_shared_rank(&xrb[crank][0], qr)[lane] = wl;
                     cl.sync();
-                }
-                if (wid == 0) {
-                    const float alpha = __shfl_sync(kFull, rc, c);
-                    const Reflector r = reflector_from_double(alpha, sdt);
-                    const float sf = r.wide ? (float)(r.scale_d * (double)f) : r.scale * f;
-                    const float wl = rc + sf;
-                    tw_s[lane] = (lane > c) ? r.tau * wl : 0.0f;
-                    if (lane < c) Ysm[lane][c] = wl;
-                    if (lane == 0) {
-                        par_f[0] = r.beta;
-                        par_f[1] = r.tau;
-                        par_f[2] = r.scale;
-                        par_d[0] = r.scale_d;
-                        par_wide = r.wide ? 1 : 0;
-                        tau_s[c] = r.tau;
+                    if (wid == 0) {
+                        wl = 0.0f;
+                        for (int qr = 0; qr < ncl; ++qr) wl += xrb[qr][lane];
                     }
                 }
+                if (wid == 0) publish(r, c, wl);
                 __syncthreads();
             }
 
             // (3) rank-1 update of my tile; column c owners store v / beta
-            Reflector r;
-            r.beta = par_f[0];
-            r.tau = par_f[1];
-            r.scale = par_f[2];
-            r.scale_d = par_d[0];
-            r.wide = par_wide != 0;
+            const Reflector r = read_params();
             const float4 t0 = *reinterpret_cast<const float4 *>(&tw_s[8 * cgp]);
             const float4 t1 = *reinterpret_cast<const float4 *>(&tw_s[8 * cgp + 4]);
             const float twv[8] = {t0.x, t0.y, t0.z, t0.w, t1.x, t1.y, t1.z, t1.w};

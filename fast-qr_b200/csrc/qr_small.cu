@@ -55,11 +55,13 @@ geqrf_small_kernel(const float *__restrict__ A, int64_t batch, int n, int64_t bs
         // pass 1: sigma and unscaled partial dots, two accumulators each
         float s0 = 0.0f, s1 = 0.0f;
         float d0[NC], d1[NC];
+        bool anynz = false;
 #pragma unroll
         for (int c = 0; c < NC; ++c) d0[c] = d1[c] = 0.0f;
 #pragma unroll
         for (int i = k + 1; i < NP; ++i) {
             const float x = __shfl_sync(kFull, a[kc][i], kl);
+            anynz |= (x != 0.0f);
             if ((i - k) & 1) {
                 s0 = fmaf(x, x, s0);
 #pragma unroll
@@ -72,11 +74,27 @@ geqrf_small_kernel(const float *__restrict__ A, int64_t batch, int n, int64_t bs
         }
         const float alpha = __shfl_sync(kFull, a[kc][k], kl);
         const float sigma = s0 + s1;
-        Reflector r;
-        if (reflector_fast_ok(alpha, sigma)) {
-            r = reflector_from_float(alpha, sigma);
+        Reflector r = reflector_identity(alpha);
+        float wv[NC];
+        bool fast;
+        if (!anynz) {
+            fast = true;
         } else {
-            // rare: over/underflow-prone column, redo the norm in double
+            fast = reflector_fast_ok(alpha, sigma);
+            if (fast) r = reflector_from_float(alpha, sigma);
+        }
+        bool bad = false;
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+            const float dj = d0[c] + d1[c];
+            wv[c] = a[c][k] + r.scale * dj;
+            bad |= dot_unsafe(dj, wv[c]);
+        }
+        // all lanes hold identical sigma / alpha, so `fast` is warp-uniform;
+        // the dot check is per lane and is made uniform by the vote
+        if (fast && anynz) fast = !__any_sync(kFull, bad);
+        if (!fast) {
+            // LAPACK order: sigma in double, then v, then w_j = v^T a_j
             double sd = 0.0;
 #pragma unroll
             for (int i = k + 1; i < NP; ++i) {
@@ -84,16 +102,21 @@ geqrf_small_kernel(const float *__restrict__ A, int64_t batch, int n, int64_t bs
                 sd = fma(x, x, sd);
             }
             r = reflector_from_double(alpha, sd);
+#pragma unroll
+            for (int c = 0; c < NC; ++c) wv[c] = a[c][k];
+#pragma unroll
+            for (int i = k + 1; i < NP; ++i) {
+                const float v = reflector_apply(r, __shfl_sync(kFull, a[kc][i], kl));
+#pragma unroll
+                for (int c = 0; c < NC; ++c) wv[c] = fmaf(v, a[c][i], wv[c]);
+            }
         }
 
         float tw[NC];
 #pragma unroll
         for (int c = 0; c < NC; ++c) {
             const int j = lane + 32 * c;
-            const float dj = d0[c] + d1[c];
-            const float sdj = r.wide ? (float)(r.scale_d * (double)dj) : r.scale * dj;
-            const float wj = a[c][k] + sdj;
-            tw[c] = (j > k) ? r.tau * wj : 0.0f;
+            tw[c] = (j > k) ? r.tau * wv[c] : 0.0f;
             a[c][k] -= tw[c];  // row k: v_k = 1
         }
         if (lane == kl) a[kc][k] = r.beta;

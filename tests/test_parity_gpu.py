@@ -140,12 +140,14 @@ def test_extreme_scales_take_the_robust_path(n, scale, dev):
     h1, t1 = fastqr.geqrf(a * scale)
     torch.cuda.synchronize()
     assert torch.isfinite(h1).all() and torch.isfinite(t1).all()
+    # the scaled run takes the LAPACK-order path, the unscaled one the fused
+    # path: they agree to accumulated float rounding (~n eps), not bitwise
     r0, r1 = torch.triu(h0).double() * scale, torch.triu(h1).double()
     rel = (r1 - r0).norm() / r0.norm()
-    assert rel < 1e-5, rel
+    assert rel < 1e-4, rel
     v0, v1 = torch.tril(h0, -1), torch.tril(h1, -1)
-    assert (v1 - v0).norm() / v0.norm() < 1e-5
-    assert (t1 - t0).abs().max() < 1e-5
+    assert (v1 - v0).norm() / v0.norm() < 1e-4
+    assert (t1 - t0).abs().max() < 1e-4
 
 
 def test_custom_kernel_contract(dev):
