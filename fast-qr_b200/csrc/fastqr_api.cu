@@ -44,6 +44,9 @@ const char *fqr_status_string(int status)
     case FQR_ETIMEOUT: return "device-side bounded wait timed out";
     case FQR_EWORKSPACE: return "workspace missing or too small";
     case FQR_ECUDA: return "CUDA runtime error";
+    case FQR_ENOALLOC_LIMIT:
+        return "problem needs more scratch than fqr_geqrf_f32_noalloc's static area "
+               "(n > 64 with batch > FQR_NOALLOC_MAX_BATCH)";
     default: return "unknown status";
     }
 }
@@ -173,6 +176,14 @@ int run_geqrf(const float *A, int64_t batch, int64_t n, int64_t a_bstride, int64
 }
 
 }  // namespace
+
+int fqr::geqrf_enqueue(const float *A, int64_t batch, int64_t n, int64_t a_bstride,
+                       int64_t a_rstride, int64_t a_cstride, float *H, float *tau, void *workspace,
+                       size_t workspace_bytes, cudaStream_t st)
+{
+    return run_geqrf(A, batch, n, a_bstride, a_rstride, a_cstride, H, tau, workspace,
+                     workspace_bytes, st, nullptr);
+}
 
 extern "C" {
 

@@ -22,6 +22,12 @@ cudaError_t launch_panel(float *H, float *tau, float *Tws, int64_t batch, int n,
 cudaError_t launch_trailing(float *H, const float *Tws, int64_t batch, int n, int k,
                             cudaStream_t st);
 
+// Validates and enqueues one batched geqrf (the body of fqr_geqrf_f32);
+// returns an FQR_* status.
+int geqrf_enqueue(const float *A, int64_t batch, int64_t n, int64_t a_bstride, int64_t a_rstride,
+                  int64_t a_cstride, float *H, float *tau, void *workspace, size_t workspace_bytes,
+                  cudaStream_t st);
+
 // Panel plan for m remaining rows: threads per CTA and cluster size.
 struct PanelShape {
     int warps;

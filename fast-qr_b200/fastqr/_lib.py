@@ -18,6 +18,7 @@ SIGNATURES = {
     "fqr_geqrf_f32": (ctypes.c_int, [_p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, ctypes.c_size_t, _p]),
     "fqr_geqrf_f32_profile": (ctypes.c_int, [_p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p,
                                              ctypes.c_size_t, _p, _p]),
+    "fqr_geqrf_f32_noalloc": (ctypes.c_int, [_p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p]),
     "fqr_workspace_bytes": (ctypes.c_size_t, [_i64, _i64]),
     "fqr_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "fqr_plan_describe": (ctypes.c_int, [_i64, _i64, ctypes.c_char_p, ctypes.c_size_t]),
@@ -35,6 +36,7 @@ STATUS = {
     4: "FQR_ETIMEOUT",
     5: "FQR_EWORKSPACE",
     6: "FQR_ECUDA",
+    7: "FQR_ENOALLOC_LIMIT",
 }
 
 _lib = None

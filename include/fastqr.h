@@ -39,7 +39,8 @@ enum {
     FQR_ELAUNCH = 3,       /* a kernel launch failed */
     FQR_ETIMEOUT = 4,      /* a bounded device-side wait gave up */
     FQR_EWORKSPACE = 5,    /* workspace missing or too small */
-    FQR_ECUDA = 6          /* other CUDA runtime error (no device, ...) */
+    FQR_ECUDA = 6,         /* other CUDA runtime error (no device, ...) */
+    FQR_ENOALLOC_LIMIT = 7 /* batch too large for fqr_geqrf_f32_noalloc's scratch */
 };
 
 /* Largest supported n. */
@@ -86,6 +87,29 @@ int fqr_plan_describe(int64_t batch, int64_t n, char *buf, size_t len);
 
 /* Number of kernel launches fqr_geqrf_f32 enqueues for (batch, n). */
 int fqr_launch_count(int64_t batch, int64_t n);
+
+/* Largest batch fqr_geqrf_f32_noalloc accepts when n > 64 (its static
+ * scratch holds this many 32 x 32 float T factors: 4 MiB per device). */
+#define FQR_NOALLOC_MAX_BATCH 1024
+
+/*
+ * Same computation and output as fqr_geqrf_f32, for callers that cannot
+ * allocate device memory: no workspace argument, and the library allocates
+ * nothing.  Scratch comes from a fixed 4 MiB __device__ array inside the
+ * library, present on every GPU that loads it until the process exits.
+ * Its address is looked up on the first call made on each device (that device
+ * current); make that first call before any stream capture.
+ * n > 64 allows at most FQR_NOALLOC_MAX_BATCH matrices per call, else
+ * FQR_ENOALLOC_LIMIT is returned and nothing is enqueued; n <= 64 needs no
+ * scratch and has no batch limit.  Every call on a device shares the array:
+ * calls that may run concurrently on the GPU (unordered streams) race and give
+ * wrong results, so issue them on one stream or order them.
+ * No counterpart in the reference, whose entry points always allocate their
+ * outputs and workspace through PyTorch (submissions/candidate.py:3682-3851).
+ */
+int fqr_geqrf_f32_noalloc(const float *A, int64_t batch, int64_t n, int64_t a_bstride,
+                          int64_t a_rstride, int64_t a_cstride, float *H, float *tau,
+                          void *stream);
 
 /* Kernel classes timed by fqr_geqrf_f32_profile. */
 enum {

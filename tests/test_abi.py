@@ -32,7 +32,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_status_strings_and_version():
     lib = fastqr.load()
-    for code in range(7):
+    for code in range(8):
         assert lib.fqr_status_string(code)
     assert lib.fqr_status_string(99) == b"unknown status"
     assert lib.fqr_version() >= 100
