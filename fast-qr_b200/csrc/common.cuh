@@ -60,12 +60,20 @@ __device__ __forceinline__ Reflector reflector_identity(float alpha) {
     return r;
 }
 
+// Inside the fast envelope (sigma in [1e-20, 1e20], |alpha| <= 1e15) every
+// operand is a normal float far from the range limits, so branch-free
+// hardware approximations are used: rsqrt refined by one Newton step for the
+// norm, and the fast reciprocal-multiply division (accurate to ~2 ulp; the
+// IEEE-rounded versions add slow-path branches to every column step).
 __device__ __forceinline__ Reflector reflector_from_float(float alpha, float sigma) {
     Reflector r;
-    float rr = sqrtf(fmaf(alpha, alpha, sigma));
+    const float s = fmaf(alpha, alpha, sigma);
+    const float y = rsqrtf(s);
+    float rr = s * y;
+    rr = fmaf(0.5f * y, fmaf(-rr, rr, s), rr);  // Newton step on sqrt(s)
     r.beta = signbit(alpha) ? rr : -rr;
-    r.tau = (r.beta - alpha) / r.beta;
-    r.scale = 1.0f / (alpha - r.beta);
+    r.tau = __fdividef(r.beta - alpha, r.beta);
+    r.scale = __fdividef(1.0f, alpha - r.beta);
     r.scale_d = (double)r.scale;
     r.wide = false;
     return r;

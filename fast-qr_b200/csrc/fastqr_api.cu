@@ -15,9 +15,9 @@
 
 namespace {
 
-constexpr size_t kWsAlign = 256;
+using fqr::kWsAlign;
 
-size_t align_up(size_t v) { return (v + kWsAlign - 1) / kWsAlign * kWsAlign; }
+bool use_tc(int64_t n) { return fqr::trailing_tc_supported((int)n); }
 
 bool small_path(int64_t n) { return n <= 64; }
 
@@ -54,8 +54,8 @@ const char *fqr_status_string(int status)
 size_t fqr_workspace_bytes(int64_t batch, int64_t n)
 {
     if (batch <= 0 || n <= 0 || n > FQR_MAX_N || small_path(n)) return 0;
-    // one 32 x 32 T factor per matrix
-    return align_up((size_t)batch * fqr::kPanel * fqr::kPanel * sizeof(float));
+    // one 32 x 32 T factor per matrix, then a status word
+    return fqr::ws_total_bytes(batch);
 }
 
 int fqr_launch_count(int64_t batch, int64_t n)
@@ -83,9 +83,9 @@ int fqr_plan_describe(int64_t batch, int64_t n, char *buf, size_t len)
         const fqr::PanelShape s = fqr::panel_shape((int)n);
         snprintf(buf, len,
                  "blocked: panel %d cols (first panel %d warps x %d row blocks, cluster %d), "
-                 "trailing simt, %d launches",
+                 "trailing %s, %d launches",
                  fqr::kPanel, s.warps, s.rows_per_thread_blocks, s.cluster,
-                 fqr_launch_count(batch, n));
+                 use_tc(n) ? "tcgen05 3xTF32" : "simt fp32", fqr_launch_count(batch, n));
     }
     return FQR_OK;
 }
@@ -155,9 +155,11 @@ int run_geqrf(const float *A, int64_t batch, int64_t n, int64_t a_bstride, int64
     if (!workspace || workspace_bytes < need) return FQR_EWORKSPACE;
     if (((uintptr_t)workspace) % kWsAlign) return FQR_EINVAL;
     float *Tws = (float *)workspace;
+    int *status = (int *)((unsigned char *)workspace + fqr::ws_t_bytes(batch));
+    const bool tc = use_tc(n) && ((uintptr_t)H % 16) == 0;
 
     if (tm) tm->begin(FQR_STAGE_COPY_IN);
-    e = fqr::launch_copy_in(A, batch, ni, a_bstride, a_rstride, a_cstride, H, st);
+    e = fqr::launch_copy_in(A, batch, ni, a_bstride, a_rstride, a_cstride, H, status, st);
     if (tm) tm->end();
     if (e != cudaSuccess) return status_from(e);
     for (int k = 0; k < ni; k += fqr::kPanel) {
@@ -167,7 +169,8 @@ int run_geqrf(const float *A, int64_t batch, int64_t n, int64_t a_bstride, int64
         if (e != cudaSuccess) return status_from(e);
         if (k + fqr::kPanel < ni) {
             if (tm) tm->begin(FQR_STAGE_TRAILING);
-            e = fqr::launch_trailing(H, Tws, batch, ni, k, st);
+            e = tc ? fqr::launch_trailing_tc(H, Tws, status, batch, ni, k, st)
+                   : fqr::launch_trailing(H, Tws, batch, ni, k, st);
             if (tm) tm->end();
             if (e != cudaSuccess) return status_from(e);
         }
@@ -193,6 +196,20 @@ int fqr_geqrf_f32(const float *A, int64_t batch, int64_t n, int64_t a_bstride, i
 {
     return run_geqrf(A, batch, n, a_bstride, a_rstride, a_cstride, H, tau, workspace,
                      workspace_bytes, (cudaStream_t)stream, nullptr);
+}
+
+int fqr_check_status(const void *workspace, size_t workspace_bytes, int64_t batch, void *stream)
+{
+    if (batch <= 0) return FQR_OK;
+    const size_t t = fqr::ws_t_bytes(batch);
+    if (!workspace || workspace_bytes < t + sizeof(int)) return FQR_EINVAL;
+    int v = 0;
+    cudaStream_t st = (cudaStream_t)stream;
+    if (cudaMemcpyAsync(&v, (const unsigned char *)workspace + t, sizeof(int), cudaMemcpyDeviceToHost,
+                        st) != cudaSuccess)
+        return FQR_ECUDA;
+    if (cudaStreamSynchronize(st) != cudaSuccess) return FQR_ECUDA;
+    return v ? FQR_ETIMEOUT : FQR_OK;
 }
 
 int fqr_geqrf_f32_profile(const float *A, int64_t batch, int64_t n, int64_t a_bstride,

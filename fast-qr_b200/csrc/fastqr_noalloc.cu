@@ -10,13 +10,14 @@
 // synchronize the whole device.
 //
 // How: the only scratch the QR needs (one 32 x 32 T factor per matrix on the
-// blocked path, n > 64) lives in a file-scope __device__ array of fixed size,
-// kNoAllocScratchBytes (4 MiB).  Every GPU that loads this library keeps that
-// array until the process exits.  Its device address is looked up once per
-// device with cudaGetSymbolAddress, with that device current, on the first
-// call made while it is current; make that first call before any stream
-// capture begins.  Nothing in the array needs to start at zero: every T
-// factor is written completely before it is read.
+// blocked path, n > 64, plus a status word) lives in a file-scope __device__
+// array of fixed size, kNoAllocScratchBytes (4 MiB + 256 bytes).  Every GPU
+// that loads this library keeps that array until the process exits.  Its
+// device address is looked up once per device with cudaGetSymbolAddress, with
+// that device current, on the first call made while it is current; make that
+// first call before any stream capture begins.  Nothing in the array needs to
+// start at zero: every T factor is written completely before it is read, and
+// the status word is cleared by the first kernel of every call.
 //
 // Limits: on the blocked path (n > 64) at most FQR_NOALLOC_MAX_BATCH matrices
 // per call; larger batches are rejected with FQR_ENOALLOC_LIMIT before any
@@ -33,8 +34,7 @@
 
 namespace {
 
-constexpr size_t kNoAllocScratchBytes =
-    (size_t)FQR_NOALLOC_MAX_BATCH * fqr::kPanel * fqr::kPanel * sizeof(float);
+constexpr size_t kNoAllocScratchBytes = fqr::ws_total_bytes(FQR_NOALLOC_MAX_BATCH);
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 

@@ -16,11 +16,26 @@ cudaError_t launch_small(const float *A, int64_t batch, int n, int64_t bs, int64
 
 // Blocked path pieces (n > 64).
 cudaError_t launch_copy_in(const float *A, int64_t batch, int n, int64_t bs, int64_t rs, int64_t cs,
-                           float *H, cudaStream_t st);
+                           float *H, int *status, cudaStream_t st);
 cudaError_t launch_panel(float *H, float *tau, float *Tws, int64_t batch, int n, int k,
                          cudaStream_t st);
 cudaError_t launch_trailing(float *H, const float *Tws, int64_t batch, int n, int k,
                             cudaStream_t st);
+
+// Tensor-core (tcgen05, 3xTF32) trailing update; needs n % 4 == 0, n >= 128
+// and a 16-byte aligned H.  Sets *status to nonzero if a bounded wait gave up.
+bool trailing_tc_supported(int n);
+cudaError_t launch_trailing_tc(float *H, const float *Tws, int *status, int64_t batch, int n, int k,
+                               cudaStream_t st);
+
+// Workspace layout: one 32 x 32 float T factor per matrix, then a 256-byte
+// status block (int status word first).
+constexpr size_t kWsAlign = 256;
+constexpr size_t ws_t_bytes(int64_t batch)
+{
+    return ((size_t)batch * kPanel * kPanel * sizeof(float) + kWsAlign - 1) / kWsAlign * kWsAlign;
+}
+constexpr size_t ws_total_bytes(int64_t batch) { return ws_t_bytes(batch) + kWsAlign; }
 
 // Validates and enqueues one batched geqrf (the body of fqr_geqrf_f32);
 // returns an FQR_* status.

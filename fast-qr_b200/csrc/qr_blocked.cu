@@ -33,9 +33,10 @@ namespace fqr {
 // memory so both the reads (rows) and the writes (columns) are coalesced.
 __global__ void __launch_bounds__(256)
 copy_in_rowmajor_kernel(const float *__restrict__ A, int64_t batch, int n, int64_t bs, int64_t rs,
-                        float *__restrict__ H)
+                        float *__restrict__ H, int *__restrict__ status)
 {
     __shared__ float tile[32][33];
+    if (status && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && threadIdx.x == 0) *status = 0;
     const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
     const int j0 = blockIdx.x * 32, i0 = blockIdx.y * 32;
     for (int64_t b = blockIdx.z; b < batch; b += gridDim.z) {
@@ -60,8 +61,9 @@ copy_in_rowmajor_kernel(const float *__restrict__ A, int64_t batch, int n, int64
 // writes coalesced along columns of H.
 __global__ void __launch_bounds__(256)
 copy_in_strided_kernel(const float *__restrict__ A, int64_t batch, int n, int64_t bs, int64_t rs,
-                       int64_t cs, float *__restrict__ H)
+                       int64_t cs, float *__restrict__ H, int *__restrict__ status)
 {
+    if (status && blockIdx.x == 0 && threadIdx.x == 0) *status = 0;
     const int64_t nn = (int64_t)n * n;
     const int64_t total = batch * nn;
     for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
@@ -74,17 +76,17 @@ copy_in_strided_kernel(const float *__restrict__ A, int64_t batch, int n, int64_
 }
 
 cudaError_t launch_copy_in(const float *A, int64_t batch, int n, int64_t bs, int64_t rs, int64_t cs,
-                           float *H, cudaStream_t st)
+                           float *H, int *status, cudaStream_t st)
 {
     if (cs == 1) {
         const unsigned t = (unsigned)((n + 31) / 32);
         dim3 grid(t, t, (unsigned)(batch < 65535 ? batch : 65535));
-        copy_in_rowmajor_kernel<<<grid, 256, 0, st>>>(A, batch, n, bs, rs, H);
+        copy_in_rowmajor_kernel<<<grid, 256, 0, st>>>(A, batch, n, bs, rs, H, status);
     } else {
         const int64_t total = batch * (int64_t)n * n;
         int64_t blocks = (total + 255) / 256;
         if (blocks > 148 * 64) blocks = 148 * 64;
-        copy_in_strided_kernel<<<(unsigned)blocks, 256, 0, st>>>(A, batch, n, bs, rs, cs, H);
+        copy_in_strided_kernel<<<(unsigned)blocks, 256, 0, st>>>(A, batch, n, bs, rs, cs, H, status);
     }
     return cudaGetLastError();
 }
@@ -93,21 +95,26 @@ cudaError_t launch_copy_in(const float *A, int64_t batch, int n, int64_t bs, int
 // Panel kernel.
 //
 // Thread layout: a warp covers blocks of 32 panel rows x 32 columns; lane =
-// cg + 4*rg owns columns 8cg..8cg+7 of rows 4rg..4rg+3 of each block, in
-// registers.  Per column c:
-//   * the 4 x-values of the lane's rows are fetched from the lane of the same
-//     row group that owns column c (4 shuffles per block);
-//   * sigma and the 8 partial dots d_j = x^T a_j are reduced over the 8 row
-//     groups (3 + 7 shuffles: a reduce-scatter leaves column 8cg+rg in lane
-//     (cg, rg)), then over warps through shared memory, then -- for tall
-//     panels split over a thread-block cluster -- over CTAs through
-//     distributed shared memory;
-//   * warp 0 forms the reflector (identical arithmetic in every CTA of the
-//     cluster), w_j = a(c, j) + scale * d_j and tau * w_j, and the T-factor
-//     inputs y_i = v_i^T v_c = w_i for i < c;
-//   * every thread applies the rank-1 update to its 4R x 8 tile.
-// Two CTA barriers per column (plus one cluster barrier when split).
-// T is formed at the end from y and tau:
+// cg + 8*rg owns columns 4cg..4cg+3 of rows 8rg..8rg+7 of each block, in
+// registers (4 columns per lane keep the unrolled per-column body small
+// enough for the instruction cache).  Per column c:
+//   * the x-values of the lane's rows are fetched from the lane of the same
+//     row group that owns column c (one shuffle per row);
+//   * the 4 unscaled partial dots d_j = x^T a_j are reduced over the warp's 4
+//     row groups (3 shuffles; a reduce-scatter leaves column 4cg+rg in lane
+//     (cg, rg)); column c's own slot is sum x*x = sigma.  The per-warp
+//     results go to a shared buffer double-buffered by column parity;
+//   * ONE CTA barrier; then every warp sums the per-warp partials itself (in
+//     the same order, so all warps hold bitwise-identical values), forms the
+//     reflector and tau * w_j with w_j = a(c, j) + scale * d_j -- no serial
+//     single-warp section and no second barrier.  Panels taller than one CTA
+//     are split over a thread-block cluster: warp 0 of each CTA also sends its
+//     CTA's partials to every CTA of the cluster through distributed shared
+//     memory and one cluster barrier replaces the CTA barrier's role;
+//   * every thread applies the rank-1 update to its tile.
+// Only the warp holding panel rows 0..31 needs row masks (rows <= c are R
+// rows); it runs a masked copy of the per-column code, all others do not.
+// T is formed at the end from y_i = v_i^T v_c (= w_i for i < c) and tau:
 //   T(c, c) = tau_c,  T(0:c, c) = -tau_c T(0:c, 0:c) y(0:c, c).
 // ---------------------------------------------------------------------------
 template <int NW, int R, bool CLUSTER>
@@ -115,26 +122,21 @@ __global__ void __launch_bounds__(NW * 32, 1)
 panel_kernel(float *__restrict__ H, float *__restrict__ tau, float *__restrict__ Tws, int n, int k)
 {
     constexpr int ROWS = NW * 32 * R;  // panel rows held by one CTA
-    constexpr int NR = 4 * R;          // rows per thread
-    constexpr int XS = 68;             // exchange slots: 32 dots, sigma, nz flag, 32 row-c values
-    __shared__ float red[NW][32];
-    __shared__ float sig_part[NW];
-    __shared__ int nz_part[NW];
+    constexpr int NR = 8 * R;          // rows per thread
+    constexpr int PS = 33;             // partial slots: 32 dots (slot c = sigma)
+    constexpr int XS = 64;             // cluster slots: 32 dots + 32 row-c values
+    __shared__ float part[2][NW][PS];
+    __shared__ float rowc_s[2][32];
+    __shared__ float red2[NW][32];
     __shared__ double sigd_part[NW];
-    __shared__ float rowc[32];
-    __shared__ __align__(16) float tw_s[32];
-    __shared__ float par_f[4];   // beta, tau, scale, robust flag
-    __shared__ double par_d[1];  // scale in double
-    __shared__ int par_wide;
     __shared__ float Ysm[32][33];
     __shared__ float tau_s[32];
-    __shared__ float alpha_s;
     __shared__ float xch[CLUSTER ? 2 : 1][CLUSTER ? 8 : 1][XS];
     __shared__ float xrb[CLUSTER ? 8 : 1][32];
     __shared__ double xchd[CLUSTER ? 8 : 1];
 
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    const int cgp = lane & 3, rg = lane >> 2;
+    const int cgp = lane & 7, rg = lane >> 3;
     int crank = 0, ncl = 1;
     if constexpr (CLUSTER) {
         cg::cluster_group cl = cg::this_cluster();
@@ -145,175 +147,112 @@ panel_kernel(float *__restrict__ H, float *__restrict__ tau, float *__restrict__
     const int m = n - k;
     const int w = m < kPanel ? m : kPanel;
     float *Hm = H + mat * (int64_t)n * n;
+    const bool top = crank == 0 && wid == 0;  // holds panel rows 0..31
 
     int row[NR];
-    float p[NR][8];
+    float p[NR][4];
 #pragma unroll
     for (int q = 0; q < NR; ++q) {
-        row[q] = crank * ROWS + (q >> 2) * (NW * 32) + wid * 32 + 4 * rg + (q & 3);
+        row[q] = crank * ROWS + (q >> 3) * (NW * 32) + wid * 32 + 8 * rg + (q & 7);
 #pragma unroll
-        for (int jj = 0; jj < 8; ++jj) {
-            const int col = 8 * cgp + jj;
+        for (int jj = 0; jj < 4; ++jj) {
+            const int col = 4 * cgp + jj;
             p[q][jj] = (row[q] < m && col < w) ? Hm[(int64_t)(k + col) * n + k + row[q]] : 0.0f;
         }
     }
 
-    // Reduce-scatter of 8 per-lane values over the 8 row groups of a warp
-    // (lane bits 2..4): lane (cg, rg) ends with the warp sum for column 8cg+rg.
-    auto reduce_scatter8 = [&](float (&d)[8]) -> float {
-        const bool up4 = rg & 4;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const float send = up4 ? d[i] : d[i + 4];
-            const float keep = up4 ? d[i + 4] : d[i];
-            d[i] = keep + __shfl_xor_sync(kFull, send, 16);
-        }
+    // Reduce-scatter of 4 per-lane values over the 4 row groups of a warp
+    // (lane bits 3..4): lane (cg, rg) ends with the warp sum for column 4cg+rg.
+    auto reduce_scatter4 = [&](float (&d)[4]) -> float {
         const bool up2 = rg & 2;
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
             const float send = up2 ? d[i] : d[i + 2];
             const float keep = up2 ? d[i + 2] : d[i];
-            d[i] = keep + __shfl_xor_sync(kFull, send, 8);
+            d[i] = keep + __shfl_xor_sync(kFull, send, 16);
         }
         const bool up1 = rg & 1;
         const float send = up1 ? d[0] : d[1];
         const float keep = up1 ? d[1] : d[0];
-        return keep + __shfl_xor_sync(kFull, send, 4);
-    };
-
-    // Warp 0 publishes the reflector and the update coefficients tau * w_l.
-    auto publish = [&](const Reflector &r, int c, float wl) {
-        tw_s[lane] = (lane > c) ? r.tau * wl : 0.0f;
-        if (lane < c) Ysm[lane][c] = wl;  // y_l = v_l^T v_c
-        if (lane == 0) {
-            par_f[0] = r.beta;
-            par_f[1] = r.tau;
-            par_f[2] = r.scale;
-            par_d[0] = r.scale_d;
-            par_wide = r.wide ? 1 : 0;
-            tau_s[c] = r.tau;
-        }
-    };
-    auto read_params = [&]() {
-        Reflector r;
-        r.beta = par_f[0];
-        r.tau = par_f[1];
-        r.scale = par_f[2];
-        r.scale_d = par_d[0];
-        r.wide = par_wide != 0;
-        return r;
+        return keep + __shfl_xor_sync(kFull, send, 8);
     };
 
 #pragma unroll 1
-    for (int cb = 0; cb < 4; ++cb) {
+    for (int cb = 0; cb < 8; ++cb) {
 #pragma unroll
-        for (int cc = 0; cc < 8; ++cc) {
-            const int c = cb * 8 + cc;
+        for (int cc = 0; cc < 4; ++cc) {
+            const int c = cb * 4 + cc;
             if (c >= w) break;
             const int par = c & 1;
 
-            // (1) x for my rows, from lane (cb, rg) (p[q][cc] holds column 8*cgp+cc)
-            float x[NR];
-            float s = 0.0f;
-            bool nz = false;
+            // (1) x for my rows (p[q][cc] holds column 4*cgp+cc; the source
+            // lane has cgp == cb), sigma and unscaled dots over rows > c
+            float x[NR], xm[NR];
 #pragma unroll
-            for (int q = 0; q < NR; ++q) {
-                x[q] = __shfl_sync(kFull, p[q][cc], cb + 4 * rg);
-                const float xm = row[q] > c ? x[q] : 0.0f;
-                s = fmaf(xm, xm, s);
-                nz |= (xm != 0.0f);
+            for (int q = 0; q < NR; ++q) x[q] = __shfl_sync(kFull, p[q][cc], cb + 8 * rg);
+            if (top) {
+#pragma unroll
+                for (int q = 0; q < NR; ++q) xm[q] = (q < 8 && row[q] <= c) ? 0.0f : x[q];
+            } else {
+#pragma unroll
+                for (int q = 0; q < NR; ++q) xm[q] = x[q];
             }
-            // (2) unscaled partial dots over rows > c for my 8 columns
-            float d[8];
+            // (column c's own slot gives sum xm * x = sigma for free)
+            float d[4];
 #pragma unroll
-            for (int jj = 0; jj < 8; ++jj) {
-                float acc = 0.0f;
+            for (int jj = 0; jj < 4; ++jj) {
+                float a2[2] = {0.0f, 0.0f};
 #pragma unroll
-                for (int q = 0; q < NR; ++q) acc = fmaf(row[q] > c ? x[q] : 0.0f, p[q][jj], acc);
-                d[jj] = acc;
+                for (int q = 0; q < NR; ++q) a2[q & 1] = fmaf(xm[q], p[q][jj], a2[q & 1]);
+                d[jj] = a2[0] + a2[1];
             }
-            s += __shfl_xor_sync(kFull, s, 4);
-            s += __shfl_xor_sync(kFull, s, 8);
-            s += __shfl_xor_sync(kFull, s, 16);
-            const bool wnz = __any_sync(kFull, nz);
-            red[wid][8 * cgp + rg] = reduce_scatter8(d);
-            if (lane == 0) {
-                sig_part[wid] = s;
-                nz_part[wid] = wnz ? 1 : 0;
+            part[par][wid][4 * cgp + rg] = reduce_scatter4(d);
+            if (top) {
+#pragma unroll
+                for (int q = 0; q < 8; ++q)
+                    if (row[q] == c) {
+#pragma unroll
+                        for (int jj = 0; jj < 4; ++jj) rowc_s[par][4 * cgp + jj] = p[q][jj];
+                    }
             }
-#pragma unroll
-            for (int q = 0; q < NR; ++q)
-                if (row[q] == c) {
-#pragma unroll
-                    for (int jj = 0; jj < 8; ++jj) rowc[8 * cgp + jj] = p[q][jj];
-                }
-            __syncthreads();  // S1
+            __syncthreads();
 
-            float f = 0.0f, sg = 0.0f, rc = 0.0f;
-            int anynz = 0;
-            if (wid == 0) {
+            // (2) every warp: CTA (and cluster) totals, reflector, tau * w_j
+            float f = 0.0f, rc;
 #pragma unroll
-                for (int u = 0; u < NW; ++u) {
-                    f += red[u][lane];
-                    sg += sig_part[u];
-                    anynz |= nz_part[u];
-                }
-                rc = rowc[lane];
-            }
+            for (int u = 0; u < NW; ++u) f += part[par][u][lane];
+            rc = rowc_s[par][lane];
             if constexpr (CLUSTER) {
                 cg::cluster_group cl = cg::this_cluster();
                 if (wid == 0) {
                     for (int qr = 0; qr < ncl; ++qr) {
                         float *dst = cl.map_shared_rank(&xch[par][crank][0], qr);
                         dst[lane] = f;
-                        if (lane == 0) {
-                            dst[32] = sg;
-                            dst[33] = (float)anynz;
-                        }
-                        if (crank == 0) dst[34 + lane] = rc;
+                        if (crank == 0) dst[32 + lane] = rc;
                     }
                 }
                 cl.sync();
-                if (wid == 0) {
-                    f = 0.0f;
-                    sg = 0.0f;
-                    anynz = 0;
-                    for (int qr = 0; qr < ncl; ++qr) {
-                        f += xch[par][qr][lane];
-                        sg += xch[par][qr][32];
-                        anynz |= xch[par][qr][33] != 0.0f;
-                    }
-                    rc = xch[par][0][34 + lane];
-                }
+                f = 0.0f;
+                for (int qr = 0; qr < ncl; ++qr) f += xch[par][qr][lane];
+                rc = xch[par][0][32 + lane];
             }
-            // alpha = a(c, c); identical in every lane of warp 0 (and every CTA)
             const float alpha = __shfl_sync(kFull, rc, c);
-            if (wid == 0 && lane == 0) alpha_s = alpha;
-            if (wid == 0) {
-                bool fast;
-                Reflector r = reflector_identity(alpha);
-                if (!anynz) {
-                    fast = true;
-                } else {
-                    fast = reflector_fast_ok(alpha, sg);
-                    if (fast) r = reflector_from_float(alpha, sg);
-                }
-                const float wl = rc + r.scale * f;
-                if (fast && anynz) fast = !__any_sync(kFull, dot_unsafe(f, wl));
-                if (fast) publish(r, c, wl);
-                if (lane == 0) par_f[3] = fast ? 0.0f : 1.0f;
-            }
-            __syncthreads();  // S2
+            const float sg = __shfl_sync(kFull, f, c);
+            // sigma == 0 (an exactly zero tail, or one whose squares
+            // underflow) also goes to the robust path, which sorts the two out
+            bool fast = reflector_fast_ok(alpha, sg);
+            Reflector r = fast ? reflector_from_float(alpha, sg) : reflector_identity(alpha);
+            float wl = rc + r.scale * f;
+            if (fast) fast = !__any_sync(kFull, dot_unsafe(f, wl));
 
-            if (par_f[3] != 0.0f) {
-                // Robust path, LAPACK order.  Round 1: sigma in double.
+            if (!fast) {
+                // Robust path, LAPACK order (uniform across the CTA and the
+                // cluster: every warp saw the same sums).  Round 1: sigma in
+                // double over rows > c.
                 double sd = 0.0;
 #pragma unroll
-                for (int q = 0; q < NR; ++q) {
-                    const double xm = row[q] > c ? (double)x[q] : 0.0;
-                    sd = fma(xm, xm, sd);
-                }
-                sd += __shfl_xor_sync(kFull, sd, 4);
+                for (int q = 0; q < NR; ++q) sd = fma((double)xm[q], (double)xm[q], sd);
+                // over the 4 row groups (lane bits 3..4) only
                 sd += __shfl_xor_sync(kFull, sd, 8);
                 sd += __shfl_xor_sync(kFull, sd, 16);
                 if (lane == 0) sigd_part[wid] = sd;
@@ -328,52 +267,73 @@ panel_kernel(float *__restrict__ H, float *__restrict__ tau, float *__restrict__
                     sdt = 0.0;
                     for (int qr = 0; qr < ncl; ++qr) sdt += xchd[qr];
                 }
-                // every thread forms the same reflector (same operands, same order)
-                const float alpha_all = alpha_s;
-                const Reflector r = reflector_from_double(alpha_all, sdt);
+                r = reflector_from_double(alpha, sdt);
+                if (sdt == 0.0) {
+                    // exactly zero tail: H = I, v = e_c, w_l = a(c, l)
+                    wl = rc;
+                } else {
                 // Round 2: w_l = v^T a_l over rows >= c with the scaled v
 #pragma unroll
-                for (int jj = 0; jj < 8; ++jj) {
+                for (int jj = 0; jj < 4; ++jj) {
                     float acc = 0.0f;
 #pragma unroll
                     for (int q = 0; q < NR; ++q) {
-                        const float v = row[q] > c ? reflector_apply(r, x[q]) : (row[q] == c ? 1.0f : 0.0f);
+                        const bool below = !top || q >= 8 || row[q] > c;
+                        const bool diag = top && q < 8 && row[q] == c;
+                        const float v = below ? reflector_apply(r, x[q]) : (diag ? 1.0f : 0.0f);
                         acc = fmaf(v, p[q][jj], acc);
                     }
                     d[jj] = acc;
                 }
-                red[wid][8 * cgp + rg] = reduce_scatter8(d);
+                red2[wid][4 * cgp + rg] = reduce_scatter4(d);
                 __syncthreads();
-                float wl = 0.0f;
-                if (wid == 0)
-                    for (int u = 0; u < NW; ++u) wl += red[u][lane];
+                wl = 0.0f;
+                for (int u = 0; u < NW; ++u) wl += red2[u][lane];
                 if constexpr (CLUSTER) {
                     cg::cluster_group cl = cg::this_cluster();
                     if (wid == 0)
                         for (int qr = 0; qr < ncl; ++qr) cl.map_shared_rank(&xrb[crank][0], qr)[lane] = wl;
                     cl.sync();
-                    if (wid == 0) {
-                        wl = 0.0f;
-                        for (int qr = 0; qr < ncl; ++qr) wl += xrb[qr][lane];
-                    }
+                    wl = 0.0f;
+                    for (int qr = 0; qr < ncl; ++qr) wl += xrb[qr][lane];
                 }
-                if (wid == 0) publish(r, c, wl);
-                __syncthreads();
+                }
+            }
+            const float tw = (lane > c) ? r.tau * wl : 0.0f;
+            if (top) {
+                if (lane < c) Ysm[lane][c] = wl;  // y_l = v_l^T v_c
+                if (lane == 0) tau_s[c] = r.tau;
             }
 
-            // (3) rank-1 update of my tile; column c owners store v / beta
-            const Reflector r = read_params();
-            const float4 t0 = *reinterpret_cast<const float4 *>(&tw_s[8 * cgp]);
-            const float4 t1 = *reinterpret_cast<const float4 *>(&tw_s[8 * cgp + 4]);
-            const float twv[8] = {t0.x, t0.y, t0.z, t0.w, t1.x, t1.y, t1.z, t1.w};
+            // (3) rank-1 update of my tile; the column-c owners store v / beta
+            float twv[4];
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) twv[jj] = __shfl_sync(kFull, tw, 4 * cgp + jj);
+            const bool owner = cgp == cb;
+            // v = scale * x; `wide` is CTA-uniform, so branch once and keep the
+            // common path free of double conversions
+            float vv[NR];
+            if (!r.wide) {
+#pragma unroll
+                for (int q = 0; q < NR; ++q) vv[q] = x[q] * r.scale;
+            } else {
+#pragma unroll
+                for (int q = 0; q < NR; ++q) vv[q] = (float)((double)x[q] * r.scale_d);
+            }
 #pragma unroll
             for (int q = 0; q < NR; ++q) {
-                const float v = row[q] > c ? reflector_apply(r, x[q]) : (row[q] == c ? 1.0f : 0.0f);
+                float v;
+                if (top && q < 8) v = row[q] > c ? vv[q] : (row[q] == c ? 1.0f : 0.0f);
+                else v = vv[q];
 #pragma unroll
-                for (int jj = 0; jj < 8; ++jj) p[q][jj] = fmaf(-twv[jj], v, p[q][jj]);
-                if (cgp == cb) {
-                    if (row[q] > c) p[q][cc] = v;
-                    else if (row[q] == c) p[q][cc] = r.beta;
+                for (int jj = 0; jj < 4; ++jj) p[q][jj] = fmaf(-twv[jj], v, p[q][jj]);
+                if (owner) {
+                    if (top && q < 8) {
+                        if (row[q] > c) p[q][cc] = v;
+                        else if (row[q] == c) p[q][cc] = r.beta;
+                    } else {
+                        p[q][cc] = v;
+                    }
                 }
             }
         }
@@ -382,15 +342,18 @@ panel_kernel(float *__restrict__ H, float *__restrict__ tau, float *__restrict__
 
     // T factor (warp 0 of the CTA holding the panel's top rows): lane i owns
     // row i of T, built column by column; stored column-major.
-    if (crank == 0 && wid == 0) {
+    if (top) {
         float trow[32];
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
-            // trow[l] == 0 for l < lane, so the sum runs over l in [lane, c)
+            // trow[l] == 0 for l < lane, so the sum runs over l in [lane, c);
+            // four accumulators keep the dependency chain short
             float acc = 0.0f;
             if (c < w) {
+                float a4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-                for (int l = 0; l < c; ++l) acc = fmaf(trow[l], Ysm[l][c], acc);
+                for (int l = 0; l < c; ++l) a4[l & 3] = fmaf(trow[l], Ysm[l][c], a4[l & 3]);
+                acc = (a4[0] + a4[1]) + (a4[2] + a4[3]);
             }
             const float tc = c < w ? tau_s[c] : 0.0f;
             trow[c] = lane < c ? -tc * acc : (lane == c ? tc : 0.0f);
@@ -404,8 +367,8 @@ panel_kernel(float *__restrict__ H, float *__restrict__ tau, float *__restrict__
 #pragma unroll
     for (int q = 0; q < NR; ++q) {
 #pragma unroll
-        for (int jj = 0; jj < 8; ++jj) {
-            const int col = 8 * cgp + jj;
+        for (int jj = 0; jj < 4; ++jj) {
+            const int col = 4 * cgp + jj;
             if (row[q] < m && col < w) Hm[(int64_t)(k + col) * n + k + row[q]] = p[q][jj];
         }
     }
@@ -417,9 +380,11 @@ panel_kernel(float *__restrict__ H, float *__restrict__ tau, float *__restrict__
 
 PanelShape panel_shape(int m)
 {
+    // Fewer, fuller warps: per column every warp pays a fixed cost (shuffles,
+    // partial reads, reflector), so 16 rows per thread beat 8.
     if (m <= 128) return {4, 1, 1};
-    if (m <= 256) return {8, 1, 1};
-    if (m <= 512) return {16, 1, 1};
+    if (m <= 256) return {4, 2, 1};
+    if (m <= 512) return {8, 2, 1};
     if (m <= 1024) return {16, 2, 1};
     return {16, 2, (m + 1023) / 1024};
 }
@@ -452,9 +417,10 @@ cudaError_t launch_panel(float *H, float *tau, float *Tws, int64_t batch, int n,
 {
     const PanelShape s = panel_shape(n - k);
     if (s.cluster > 8) return cudaErrorInvalidValue;
-    if (s.warps == 4) return launch_panel_t<4, 1>(H, tau, Tws, batch, n, k, 1, st);
-    if (s.warps == 8) return launch_panel_t<8, 1>(H, tau, Tws, batch, n, k, 1, st);
-    if (s.rows_per_thread_blocks == 1) return launch_panel_t<16, 1>(H, tau, Tws, batch, n, k, 1, st);
+    if (s.warps == 4 && s.rows_per_thread_blocks == 1)
+        return launch_panel_t<4, 1>(H, tau, Tws, batch, n, k, 1, st);
+    if (s.warps == 4) return launch_panel_t<4, 2>(H, tau, Tws, batch, n, k, 1, st);
+    if (s.warps == 8) return launch_panel_t<8, 2>(H, tau, Tws, batch, n, k, 1, st);
     return launch_panel_t<16, 2>(H, tau, Tws, batch, n, k, s.cluster, st);
 }
 

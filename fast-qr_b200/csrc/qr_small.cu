@@ -2,16 +2,26 @@
 //
 // Replaces the reference's n=32 kernel (submissions/candidate.py:146-226,
 // launcher :228-248), which stages each matrix in shared memory and does one
-// block-level dot reduction per (k, j) pair.  Here lane L owns columns L and
-// L+32 (n <= 64) in registers; the reflector column is broadcast with warp
-// shuffles so every lane forms its own dot product locally -- no reductions
-// at all.  Each step makes two broadcast passes over the tail x = a(k+1:n, k):
-//   pass 1: sigma = ||x||^2 and d_j = x^T a(k+1:n, j) for the lane's columns
-//   (reflector: beta, tau, scale = 1/(alpha - beta))
-//   pass 2: v = scale * x; a(k+1:n, j) -= tau * w_j * v, with
-//           w_j = a(k, j) + scale * d_j  (= v^T a(k:n, j), v_k = 1)
-// A is read in its own (row-major) layout with coalesced 128-byte row loads;
-// H is written column-major through a per-warp shared-memory transpose.
+// block-level dot reduction per (k, j) pair.  Here lane L owns column L (and
+// column L+32 when n > 32) in registers and the reflector column is broadcast
+// with warp shuffles, so every lane forms its own dot product locally -- no
+// reductions at all.
+//
+// Sliding register window: after step k the lane's column is shifted up one
+// row (the finished row k goes to a shared-memory stage), so at every step
+// the pivot row is a[0] and the tail x is a[1..]; rows below the matrix shift
+// in as zeros.  All register indices are compile-time constants, the step
+// loop is a runtime loop over one small body (the instruction cache holds
+// it; a fully unrolled step loop stalls on instruction fetch), and no row
+// masks or branches sit in the inner loops, so the shuffles pipeline.
+// Per step k:
+//   x_i = a_owner[i] (shuffle from the lane owning column k), i = 1..
+//   sigma = ||x||^2,  d = x^T a[1..]  (unscaled, one pass)
+//   beta, tau, scale = 1 / (alpha - beta)   (LAPACK xLARFG convention)
+//   w = a[0] + scale * d,  a[0] -= tau w,  a[i] -= tau * w * scale * x_i
+//   the owner lane stores beta and v = scale * x instead.
+// The shared-memory stage then holds the factor transposed for coalesced
+// column-major stores of H.
 #include "common.cuh"
 #include "internal.h"
 
@@ -19,17 +29,135 @@ namespace fqr {
 
 constexpr int kSmallWarps = 4;
 
+// One step of the sliding-window factorisation for register slot S (the
+// slot holding column k; lanes with a column j <= k are left unchanged).
+// The owner lane keeps its column unscaled (x, not v = scale * x) so the
+// update needs no per-element select; its scale is recorded and applied when
+// the factor is written out.
+template <int NP, int NC, int S>
+__device__ __forceinline__ void small_step(float (&a)[NC][NP], int k, int lane, float *stage_row,
+                                           float *tau_stage, float *scale_stage,
+                                           double *scaled_stage)
+{
+    const int kl = k & 31;
+    const bool owner = lane == kl;
+    float x[NP];
+    float s0 = 0.0f, s1 = 0.0f;
+    float d0[NC], d1[NC];
+    bool anynz = false;
+#pragma unroll
+    for (int c = 0; c < NC; ++c) d0[c] = d1[c] = 0.0f;
+    const float alpha = __shfl_sync(kFull, a[S][0], kl);
+#pragma unroll
+    for (int i = 1; i < NP; ++i) {
+        x[i] = __shfl_sync(kFull, a[S][i], kl);
+        anynz |= (x[i] != 0.0f);
+        if (i & 1) {
+            s0 = fmaf(x[i], x[i], s0);
+#pragma unroll
+            for (int c = 0; c < NC; ++c) d0[c] = fmaf(x[i], a[c][i], d0[c]);
+        } else {
+            s1 = fmaf(x[i], x[i], s1);
+#pragma unroll
+            for (int c = 0; c < NC; ++c) d1[c] = fmaf(x[i], a[c][i], d1[c]);
+        }
+    }
+    const float sigma = s0 + s1;
+    Reflector r = reflector_identity(alpha);
+    bool fast = true;
+    if (anynz) {
+        fast = reflector_fast_ok(alpha, sigma);
+        if (fast) r = reflector_from_float(alpha, sigma);
+    }
+    // fast path: a(i, j) -= (tau * w_j * scale) * x_i, one FMA per element
+    float tw[NC], tws[NC];
+    bool bad = false;
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+        const int j = lane + 32 * c;
+        const float dj = d0[c] + d1[c];
+        const float wj = a[c][0] + r.scale * dj;
+        tw[c] = (j > k) ? r.tau * wj : 0.0f;
+        tws[c] = tw[c] * r.scale;
+        bad |= dot_unsafe(dj, wj) || !isfinite(tws[c]);
+    }
+    // sigma / alpha are identical in all lanes, so `fast` is warp-uniform;
+    // the per-lane checks are made uniform by the vote
+    if (fast && anynz) fast = !__any_sync(kFull, bad);
+    float rowk[NC];  // finished row k (v_k = 1), taken before the window shifts
+    if (fast) {
+#pragma unroll
+        for (int c = 0; c < NC; ++c) rowk[c] = (owner && c == S) ? r.beta : a[c][0] - tw[c];
+#pragma unroll
+        for (int i = 1; i < NP; ++i) {
+#pragma unroll
+            for (int c = 0; c < NC; ++c) a[c][i - 1] = fmaf(-tws[c], x[i], a[c][i]);
+        }
+    } else {
+        // LAPACK order: sigma in double, then v, then w_j = v^T a_j
+        double sd = 0.0;
+#pragma unroll
+        for (int i = 1; i < NP; ++i) sd = fma((double)x[i], (double)x[i], sd);
+        r = reflector_from_double(alpha, sd);
+        float wv[NC];
+#pragma unroll
+        for (int c = 0; c < NC; ++c) wv[c] = a[c][0];
+#pragma unroll
+        for (int i = 1; i < NP; ++i) {
+            const float v = reflector_apply(r, x[i]);
+#pragma unroll
+            for (int c = 0; c < NC; ++c) wv[c] = fmaf(v, a[c][i], wv[c]);
+        }
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+            const int j = lane + 32 * c;
+            tw[c] = (j > k) ? r.tau * wv[c] : 0.0f;
+            rowk[c] = (owner && c == S) ? r.beta : a[c][0] - tw[c];
+        }
+#pragma unroll
+        for (int i = 1; i < NP; ++i) {
+            const float v = reflector_apply(r, x[i]);
+#pragma unroll
+            for (int c = 0; c < NC; ++c) a[c][i - 1] = fmaf(-tw[c], v, a[c][i]);
+        }
+    }
+    // finished row k (shifted out above), and the owner's column scale
+#pragma unroll
+    for (int c = 0; c < NC; ++c) stage_row[32 * c] = rowk[c];
+    if (lane == 0) {
+        tau_stage[k] = r.tau;
+        scale_stage[k] = r.wide ? 0.0f : r.scale;
+        scaled_stage[k] = r.scale_d;
+    }
+#pragma unroll
+    for (int c = 0; c < NC; ++c) a[c][NP - 1] = 0.0f;
+}
+
+// The final row (k = n-1) has an empty tail: tau = 0, the row is unchanged.
+template <int NP, int NC>
+__device__ __forceinline__ void small_last_row(float (&a)[NC][NP], float *stage_row)
+{
+#pragma unroll
+    for (int c = 0; c < NC; ++c) stage_row[32 * c] = a[c][0];
+}
+
 template <int NP>
 __global__ void __launch_bounds__(kSmallWarps * 32)
 geqrf_small_kernel(const float *__restrict__ A, int64_t batch, int n, int64_t bs, int64_t rs,
                    int64_t cs, float *__restrict__ H, float *__restrict__ tau)
 {
     constexpr int NC = NP / 32;
-    __shared__ float stage[kSmallWarps][32][33];
+    constexpr int LD = NP + 1;  // stage row stride (columns), padded
+    constexpr int WS = NP * LD + 2 * NP + 2 * NP;  // floats per warp: stage, tau, scale, scale_d
+    extern __shared__ float smem_small[];
     const int lane = threadIdx.x & 31;
     const int wid = threadIdx.x >> 5;
     const int64_t mat = (int64_t)blockIdx.x * kSmallWarps + wid;
     if (mat >= batch) return;  // warp-uniform; the kernel has no block barrier
+    float *stage = smem_small + wid * WS;  // [row][col]
+    float *tau_stage = stage + NP * LD;
+    float *scale_stage = tau_stage + NP;
+    double *scaled_stage = reinterpret_cast<double *>(scale_stage + NP);  // 8-byte aligned
 
     float a[NC][NP];
     const float *Am = A + mat * bs;
@@ -42,117 +170,49 @@ geqrf_small_kernel(const float *__restrict__ A, int64_t batch, int n, int64_t bs
             a[c][i] = (jin && i < n) ? __ldg(Am + (int64_t)i * rs + (int64_t)j * cs) : 0.0f;
     }
 
-    float my_tau[NC];
-#pragma unroll
-    for (int c = 0; c < NC; ++c) my_tau[c] = 0.0f;
-
-#pragma unroll
-    for (int k = 0; k < NP - 1; ++k) {
-        if (k >= n - 1) break;
-        const int kc = k >> 5;   // register slot holding column k
-        const int kl = k & 31;   // lane owning column k
-
-        // pass 1: sigma and unscaled partial dots, two accumulators each
-        float s0 = 0.0f, s1 = 0.0f;
-        float d0[NC], d1[NC];
-        bool anynz = false;
-#pragma unroll
-        for (int c = 0; c < NC; ++c) d0[c] = d1[c] = 0.0f;
-#pragma unroll
-        for (int i = k + 1; i < NP; ++i) {
-            const float x = __shfl_sync(kFull, a[kc][i], kl);
-            anynz |= (x != 0.0f);
-            if ((i - k) & 1) {
-                s0 = fmaf(x, x, s0);
-#pragma unroll
-                for (int c = 0; c < NC; ++c) d0[c] = fmaf(x, a[c][i], d0[c]);
-            } else {
-                s1 = fmaf(x, x, s1);
-#pragma unroll
-                for (int c = 0; c < NC; ++c) d1[c] = fmaf(x, a[c][i], d1[c]);
-            }
-        }
-        const float alpha = __shfl_sync(kFull, a[kc][k], kl);
-        const float sigma = s0 + s1;
-        Reflector r = reflector_identity(alpha);
-        float wv[NC];
-        bool fast;
-        if (!anynz) {
-            fast = true;
-        } else {
-            fast = reflector_fast_ok(alpha, sigma);
-            if (fast) r = reflector_from_float(alpha, sigma);
-        }
-        bool bad = false;
-#pragma unroll
-        for (int c = 0; c < NC; ++c) {
-            const float dj = d0[c] + d1[c];
-            wv[c] = a[c][k] + r.scale * dj;
-            bad |= dot_unsafe(dj, wv[c]);
-        }
-        // all lanes hold identical sigma / alpha, so `fast` is warp-uniform;
-        // the dot check is per lane and is made uniform by the vote
-        if (fast && anynz) fast = !__any_sync(kFull, bad);
-        if (!fast) {
-            // LAPACK order: sigma in double, then v, then w_j = v^T a_j
-            double sd = 0.0;
-#pragma unroll
-            for (int i = k + 1; i < NP; ++i) {
-                const double x = (double)__shfl_sync(kFull, a[kc][i], kl);
-                sd = fma(x, x, sd);
-            }
-            r = reflector_from_double(alpha, sd);
-#pragma unroll
-            for (int c = 0; c < NC; ++c) wv[c] = a[c][k];
-#pragma unroll
-            for (int i = k + 1; i < NP; ++i) {
-                const float v = reflector_apply(r, __shfl_sync(kFull, a[kc][i], kl));
-#pragma unroll
-                for (int c = 0; c < NC; ++c) wv[c] = fmaf(v, a[c][i], wv[c]);
-            }
-        }
-
-        float tw[NC];
-#pragma unroll
-        for (int c = 0; c < NC; ++c) {
-            const int j = lane + 32 * c;
-            tw[c] = (j > k) ? r.tau * wv[c] : 0.0f;
-            a[c][k] -= tw[c];  // row k: v_k = 1
-        }
-        if (lane == kl) a[kc][k] = r.beta;
-
-        // pass 2: apply the reflector below row k; the owner lane stores v
-#pragma unroll
-        for (int i = k + 1; i < NP; ++i) {
-            const float x = __shfl_sync(kFull, a[kc][i], kl);
-            const float v = reflector_apply(r, x);
-#pragma unroll
-            for (int c = 0; c < NC; ++c) a[c][i] = fmaf(-tw[c], v, a[c][i]);
-            if (lane == kl) a[kc][i] = v;
-        }
-        if (lane == kl) my_tau[kc] = r.tau;
+    const int k1 = (n - 1) < 32 ? (n - 1) : 32;  // steps whose column sits in slot 0
+#pragma unroll 1
+    for (int k = 0; k < k1; ++k)
+        small_step<NP, NC, 0>(a, k, lane, stage + k * LD + lane, tau_stage, scale_stage, scaled_stage);
+    if constexpr (NC == 2) {
+#pragma unroll 1
+        for (int k = 32; k < n - 1; ++k)
+            small_step<NP, NC, 1>(a, k, lane, stage + k * LD + lane, tau_stage, scale_stage,
+                                  scaled_stage);
     }
+    small_last_row<NP, NC>(a, stage + (n - 1) * LD + lane);
+    if (lane == 0) tau_stage[n - 1] = 0.0f;
+    __syncwarp();
 
-    // column-major store through a 32x33 shared-memory transpose per warp
+    // column-major store: lanes write consecutive rows of one column; rows
+    // below the diagonal hold x and become v = scale_j * x here
     float *Hm = H + mat * (int64_t)n * n;
-#pragma unroll
-    for (int c = 0; c < NC; ++c) {
+#pragma unroll 1
+    for (int j = 0; j < n; ++j) {
+        const float sj = j < n - 1 ? scale_stage[j] : 1.0f;
+        const bool widej = j < n - 1 && sj == 0.0f;
+        const double sdj = widej ? scaled_stage[j] : 1.0;
 #pragma unroll
         for (int rb = 0; rb < NC; ++rb) {
-#pragma unroll
-            for (int ii = 0; ii < 32; ++ii) stage[wid][lane][ii] = a[c][rb * 32 + ii];
-            __syncwarp();
             const int i = rb * 32 + lane;
-#pragma unroll 8
-            for (int jj = 0; jj < 32; ++jj) {
-                const int j = c * 32 + jj;
-                if (j < n && i < n) Hm[(int64_t)j * n + i] = stage[wid][jj][lane];
+            if (i < n) {
+                float h = stage[i * LD + j];
+                if (i > j) h = widej ? (float)((double)h * sdj) : h * sj;
+                Hm[(int64_t)j * n + i] = h;
             }
-            __syncwarp();
         }
-        const int j = c * 32 + lane;
-        if (j < n) tau[mat * n + j] = my_tau[c];
     }
+#pragma unroll
+    for (int rb = 0; rb < NC; ++rb) {
+        const int i = rb * 32 + lane;
+        if (i < n) tau[mat * n + i] = tau_stage[i];
+    }
+}
+
+template <int NP>
+static size_t small_smem_bytes()
+{
+    return (size_t)kSmallWarps * (NP * (NP + 1) + 4 * NP) * sizeof(float);
 }
 
 cudaError_t launch_small(const float *A, int64_t batch, int n, int64_t bs, int64_t rs, int64_t cs,
@@ -161,10 +221,15 @@ cudaError_t launch_small(const float *A, int64_t batch, int n, int64_t bs, int64
     const int64_t blocks = (batch + kSmallWarps - 1) / kSmallWarps;
     if (blocks > 0x7fffffffLL) return cudaErrorInvalidValue;
     dim3 grid((unsigned)blocks), block(kSmallWarps * 32);
-    if (n <= 32)
-        geqrf_small_kernel<32><<<grid, block, 0, st>>>(A, batch, n, bs, rs, cs, H, tau);
-    else
-        geqrf_small_kernel<64><<<grid, block, 0, st>>>(A, batch, n, bs, rs, cs, H, tau);
+    if (n <= 32) {
+        geqrf_small_kernel<32><<<grid, block, small_smem_bytes<32>(), st>>>(A, batch, n, bs, rs, cs, H, tau);
+    } else {
+        const size_t smem = small_smem_bytes<64>();
+        cudaError_t e = cudaFuncSetAttribute(geqrf_small_kernel<64>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        geqrf_small_kernel<64><<<grid, block, smem, st>>>(A, batch, n, bs, rs, cs, H, tau);
+    }
     return cudaGetLastError();
 }
 

@@ -1,0 +1,298 @@
+// Trailing update of the blocked QR on the 5th-generation tensor cores:
+//   C := C - V (T^T (V^T C))      (C = H[k:n, k+32:n], V = unit-lower panel)
+// in 3xTF32 split precision (x = hi + lo; products hi*hi + hi*lo + lo*hi
+// accumulate in FP32), which keeps the update at FP32 accuracy -- a plain TF32
+// update fails the factor gate (the reference's own evidence,
+// tests/test_qr_smoke.py:217-229; restated in tests/test_oracle.py).
+//
+// One CTA (4 warps) owns a tile of kTN = 128 trailing columns of one matrix:
+//   phase A  W^T[c][j] = sum_r C(r, c) V(r, j)    tcgen05.mma M=128 (c) N=32 (j),
+//            K = rows, accumulated over 128-row chunks into TMEM
+//   phase B  Y = T^T W                            per thread (one column c)
+//   phase C  P[r][c] = sum_j V(r, j) Y(j, c)      tcgen05.mma M=128 (r) N=128 (c)
+//            K = 32 per 128-row chunk; epilogue C(r, c) -= P from TMEM
+// Operands are staged by the threads (global -> registers -> hi/lo split ->
+// shared memory) in the no-swizzle K-major "core matrix" layout: a core holds
+// 8 rows of the M/N dimension x 4 consecutive K elements (16 bytes per row).
+// The reference's trailing_update_kernel (submissions/candidate.py:2507-2716)
+// is SIMT FP32 with T recomputed in every CTA; nothing here follows it.
+#include "common.cuh"
+#include "internal.h"
+#include "tc.cuh"
+
+namespace fqr {
+
+namespace {
+
+constexpr int kTN = 128;          // trailing columns per CTA
+constexpr int kRC = 128;          // rows per chunk
+constexpr int kThreads = 128;
+constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kDA = 0;       // TMEM column of W^T (32 columns)
+constexpr uint32_t kDC = 128;     // TMEM column of P (128 columns)
+constexpr uint64_t kWaitLimit = 1000000000ull;  // 1 s of wall time per wait
+
+// shared memory map (bytes)
+constexpr int kOffChi = 0;        // C^T chunk hi: 128 c x 128 r (64 KB)
+constexpr int kOffClo = 65536;    // C^T chunk lo (64 KB)
+constexpr int kOffVhi = 131072;   // V chunk hi: 32 j x 128 r (16 KB)
+constexpr int kOffVlo = 147456;   // V chunk lo (16 KB)
+constexpr int kOffT = 163840;     // T, column-major 32 x 32 (4 KB)
+constexpr int kOffBar = 167936;   // mbarrier (8 B) + TMEM base address (4 B)
+constexpr int kSmem = kOffBar + 64;
+constexpr int kOffYhi = kOffChi;  // Y: 128 c x 32 j (16 KB), reuses the C area in phase C
+constexpr int kOffYlo = kOffChi + 16384;
+
+constexpr uint32_t kIdescA = tc::idesc_tf32(128, 32, 0, 0);   // K-major A (C^T), K-major B (V)
+constexpr uint32_t kIdescC = tc::idesc_tf32(128, 128, 0, 0);  // K-major A (V), K-major B (Y)
+
+// Stage NO columns x kRC rows of a column-major matrix (column o at
+// base + o * ld, rows r0 ..) into hi/lo core layouts: core (o/8, r/4) at
+// ((o/8) * 32 + r/4) * 128 bytes, column o%8 at +16 * (o%8).  Each warp
+// iteration moves 8 columns x 16 rows: 64 contiguous bytes per column from
+// global memory, 512 contiguous bytes of shared memory.
+// UNIT selects V's unit-lower mask (panel rows < j are 0, row j is 1).
+template <int NO, bool UNIT>
+__device__ __forceinline__ void stage_cols(const float *base, int64_t ld, int r0, int rows, int cols,
+                                           unsigned char *hi, unsigned char *lo, int warp, int lane)
+{
+    constexpr int ITER = (NO / 8) * 8;  // (column groups) x (row-quad groups of 4)
+    const int oc = lane & 7, qi = lane >> 3;
+#pragma unroll 4
+    for (int it = warp; it < ITER; it += 4) {
+        const int og = it >> 3, qg = it & 7;
+        const int o = og * 8 + oc;
+        const int rq = qg * 4 + qi;      // row quad within the chunk, 0..31
+        const int r = r0 + rq * 4;       // first panel row of the quad
+        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (o < cols && r < rows) v = __ldg(reinterpret_cast<const float4 *>(base + (int64_t)o * ld + r));
+        if (UNIT) {
+            float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) e[i] = (r + i < o) ? 0.0f : ((r + i == o) ? 1.0f : e[i]);
+            v = make_float4(e[0], e[1], e[2], e[3]);
+        }
+        float4 h, l;
+        tc::split_tf32(v.x, h.x, l.x);
+        tc::split_tf32(v.y, h.y, l.y);
+        tc::split_tf32(v.z, h.z, l.z);
+        tc::split_tf32(v.w, h.w, l.w);
+        const uint32_t off = (uint32_t)((og * 32 + rq) * 128 + oc * 16);
+        *reinterpret_cast<float4 *>(hi + off) = h;
+        *reinterpret_cast<float4 *>(lo + off) = l;
+    }
+}
+
+// V chunk as the K-major A operand of phase C (M = rows, K = the 32 panel
+// columns): core (r/8, j/4) at ((r/8) * 8 + j/4) * 128 bytes, row r%8 at
+// +16 * (r%8).  Thread = row: 4 column loads (coalesced across the warp) per
+// 16-byte store; a warp's stores cover 4 contiguous 128-byte cores.
+__device__ __forceinline__ void stage_v_kmajor(const float *Vbase, int64_t ld, int r0, int rows,
+                                               unsigned char *hi, unsigned char *lo, int tid)
+{
+    const int r = r0 + tid;  // panel row
+#pragma unroll 2
+    for (int jq = 0; jq < kPanel / 4; ++jq) {
+        float e[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int j = 4 * jq + i;
+            float v = 0.0f;
+            if (r < rows) v = r > j ? __ldg(Vbase + (int64_t)j * ld + r) : (r == j ? 1.0f : 0.0f);
+            e[i] = v;
+        }
+        float4 h, l;
+        tc::split_tf32(e[0], h.x, l.x);
+        tc::split_tf32(e[1], h.y, l.y);
+        tc::split_tf32(e[2], h.z, l.z);
+        tc::split_tf32(e[3], h.w, l.w);
+        const uint32_t off = (uint32_t)(((tid >> 3) * 8 + jq) * 128 + (tid & 7) * 16);
+        *reinterpret_cast<float4 *>(hi + off) = h;
+        *reinterpret_cast<float4 *>(lo + off) = l;
+    }
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(kThreads, 1)
+trailing_tc_kernel(float *__restrict__ H, const float *__restrict__ Tws, int *__restrict__ status,
+                   int n, int k)
+{
+    extern __shared__ __align__(1024) unsigned char smem[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int64_t mat = blockIdx.y;
+    const int c0 = k + kPanel + blockIdx.x * kTN;  // first trailing column of the tile
+    const int nct = min(kTN, n - c0);
+    const int m = n - k;
+    float *Hm = H + mat * (int64_t)n * n;
+    const float *Cbase = Hm + (int64_t)c0 * n + k;  // C(r, c) at Cbase[c * n + r]
+    const float *Vbase = Hm + (int64_t)k * n + k;   // V(r, j) at Vbase[j * n + r]
+
+    uint64_t *bar = reinterpret_cast<uint64_t *>(smem + kOffBar);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kOffBar + 8);
+    float *Ts = reinterpret_cast<float *>(smem + kOffT);
+
+    if (warp == 0) {
+        tc::tmem_alloc(tmem_slot, kTmemCols);
+        tc::tmem_relinquish();
+    }
+    if (tid == 0) {
+        tc::mbar_init(bar, 1);
+        tc::fence_mbar_init();
+    }
+    const float *Tm = Tws + mat * (kPanel * kPanel);
+    for (int i = tid; i < kPanel * kPanel; i += kThreads) Ts[i] = Tm[i];
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+    uint32_t phase = 0;
+    bool ok = true;
+
+    const uint32_t sChi = tc::smem_addr(smem + kOffChi), sClo = tc::smem_addr(smem + kOffClo);
+    const uint32_t sVhi = tc::smem_addr(smem + kOffVhi), sVlo = tc::smem_addr(smem + kOffVlo);
+    const uint32_t sYhi = tc::smem_addr(smem + kOffYhi), sYlo = tc::smem_addr(smem + kOffYlo);
+
+    // ---- phase A: W^T = C^T V over all rows --------------------------------
+    for (int r0 = 0; r0 < m && ok; r0 += kRC) {
+        stage_cols<kTN, false>(Cbase, n, r0, m, nct, smem + kOffChi, smem + kOffClo, warp, lane);
+        stage_cols<kPanel, true>(Vbase, n, r0, m, kPanel, smem + kOffVhi, smem + kOffVlo, warp, lane);
+        tc::fence_proxy_async_smem();
+        __syncthreads();
+        if (tid == 0) {
+            tc::fence_after_sync();
+#pragma unroll 1
+            for (int s = 0; s < kRC / 8; ++s) {
+                const uint32_t ko = (uint32_t)s * 256;  // 8 rows = 2 cores along K
+                const uint64_t ah = tc::smem_desc(sChi + ko, 128, 4096);
+                const uint64_t al = tc::smem_desc(sClo + ko, 128, 4096);
+                const uint64_t bh = tc::smem_desc(sVhi + ko, 128, 4096);
+                const uint64_t bl = tc::smem_desc(sVlo + ko, 128, 4096);
+                const uint32_t acc = (r0 > 0 || s > 0) ? 1u : 0u;
+                tc::mma_tf32(tmem + kDA, al, bh, kIdescA, acc);
+                tc::mma_tf32(tmem + kDA, ah, bl, kIdescA, 1u);
+                tc::mma_tf32(tmem + kDA, ah, bh, kIdescA, 1u);
+            }
+            tc::mma_commit(bar);
+        }
+        const bool done = tc::mbar_wait(bar, phase, kWaitLimit);
+        phase ^= 1u;
+        ok = !__syncthreads_or(!done);
+    }
+
+    // ---- phase B: Y = T^T W, thread = tile column c ------------------------
+    if (ok) {
+        tc::fence_after_sync();
+        float w[32];
+        tc::tmem_ld_32x32(tmem + ((uint32_t)(32 * warp) << 16) + kDA, w);
+        tc::tmem_ld_wait();
+        const int c = 32 * warp + lane;
+        float y[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            float a4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+            for (int l = 0; l <= j; ++l) a4[l & 3] = fmaf(Ts[j * 32 + l], w[l], a4[l & 3]);
+            y[j] = (a4[0] + a4[1]) + (a4[2] + a4[3]);
+        }
+        // Y as the K-major B operand of phase C: core (c/8, j/4) at
+        // ((c/8) * 8 + j/4) * 128 bytes, column c%8 at +16 * (c%8)
+#pragma unroll
+        for (int jq = 0; jq < 8; ++jq) {
+            float4 h, l;
+            tc::split_tf32(y[4 * jq + 0], h.x, l.x);
+            tc::split_tf32(y[4 * jq + 1], h.y, l.y);
+            tc::split_tf32(y[4 * jq + 2], h.z, l.z);
+            tc::split_tf32(y[4 * jq + 3], h.w, l.w);
+            const uint32_t off = (uint32_t)(((c >> 3) * 8 + jq) * 128 + (c & 7) * 16);
+            *reinterpret_cast<float4 *>(smem + kOffYhi + off) = h;
+            *reinterpret_cast<float4 *>(smem + kOffYlo + off) = l;
+        }
+        tc::fence_before_sync();
+    }
+
+    // ---- phase C: C -= V Y, 128 rows per chunk -----------------------------
+    for (int r0 = 0; r0 < m && ok; r0 += kRC) {
+        stage_v_kmajor(Vbase, n, r0, m, smem + kOffVhi, smem + kOffVlo, tid);
+        tc::fence_proxy_async_smem();
+        __syncthreads();
+        if (tid == 0) {
+            tc::fence_after_sync();
+#pragma unroll
+            for (int s = 0; s < kPanel / 8; ++s) {
+                // A = V (K-major, M = rows), B = Y (K-major, N = columns):
+                // 8 K-columns = 2 cores = 256 bytes per step
+                const uint64_t ah = tc::smem_desc(sVhi + (uint32_t)s * 256, 128, 1024);
+                const uint64_t al = tc::smem_desc(sVlo + (uint32_t)s * 256, 128, 1024);
+                const uint64_t bh = tc::smem_desc(sYhi + (uint32_t)s * 256, 128, 1024);
+                const uint64_t bl = tc::smem_desc(sYlo + (uint32_t)s * 256, 128, 1024);
+                tc::mma_tf32(tmem + kDC, al, bh, kIdescC, s > 0 ? 1u : 0u);
+                tc::mma_tf32(tmem + kDC, ah, bl, kIdescC, 1u);
+                tc::mma_tf32(tmem + kDC, ah, bh, kIdescC, 1u);
+            }
+            tc::mma_commit(bar);
+        }
+        const bool done = tc::mbar_wait(bar, phase, kWaitLimit);
+        phase ^= 1u;
+        ok = !__syncthreads_or(!done);
+        if (!ok) break;
+        tc::fence_after_sync();
+        // epilogue: thread = row r0 + 32 warp + lane, 128 columns from TMEM
+        const int r = r0 + 32 * warp + lane;
+        float *Crow = Hm + (int64_t)c0 * n + k + r;
+#pragma unroll 1
+        for (int cc = 0; cc < kTN / 32; ++cc) {
+            float p[32];
+            tc::tmem_ld_32x32(tmem + ((uint32_t)(32 * warp) << 16) + kDC + 32 * cc, p);
+            tc::tmem_ld_wait();
+            if (r < m) {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const int c = 32 * cc + i;
+                    if (c < nct) Crow[(int64_t)c * n] -= p[i];
+                }
+            }
+        }
+        tc::fence_before_sync();
+        __syncthreads();
+    }
+
+    if (!ok && tid == 0) {
+        atomicOr(status, 1);
+        // let the MMA group that did not signal in time drain (bounded)
+        // before its tensor memory is released
+        tc::mbar_wait(bar, phase ^ 1u, kWaitLimit);
+    }
+    __syncthreads();
+    if (warp == 0) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+bool trailing_tc_supported(int n)
+{
+    return n % 4 == 0 && n >= 128;
+}
+
+cudaError_t launch_trailing_tc(float *H, const float *Tws, int *status, int64_t batch, int n, int k,
+                               cudaStream_t st)
+{
+    const int nc = n - k - kPanel;
+    if (nc <= 0) return cudaSuccess;
+    cudaError_t e = cudaFuncSetAttribute(trailing_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kSmem);
+    if (e != cudaSuccess) return e;
+    const unsigned tiles = (unsigned)((nc + kTN - 1) / kTN);
+    for (int64_t b0 = 0; b0 < batch; b0 += 65535) {
+        const int64_t nb = (batch - b0) < 65535 ? (batch - b0) : 65535;
+        dim3 grid(tiles, (unsigned)nb);
+        trailing_tc_kernel<<<grid, kThreads, kSmem, st>>>(H + b0 * (int64_t)n * n,
+                                                          Tws + b0 * kPanel * kPanel, status, n, k);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
+}  // namespace fqr

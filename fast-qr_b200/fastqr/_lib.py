@@ -20,6 +20,7 @@ SIGNATURES = {
                                              ctypes.c_size_t, _p, _p]),
     "fqr_geqrf_f32_noalloc": (ctypes.c_int, [_p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p]),
     "fqr_workspace_bytes": (ctypes.c_size_t, [_i64, _i64]),
+    "fqr_check_status": (ctypes.c_int, [_p, ctypes.c_size_t, _i64, _p]),
     "fqr_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "fqr_plan_describe": (ctypes.c_int, [_i64, _i64, ctypes.c_char_p, ctypes.c_size_t]),
     "fqr_launch_count": (ctypes.c_int, [_i64, _i64]),

@@ -101,6 +101,16 @@ def geqrf(a: torch.Tensor, *, out: tuple[torch.Tensor, torch.Tensor] | None = No
     return h, tau
 
 
+def check_status(workspace: torch.Tensor, batch: int) -> None:
+    """Blocks on the current stream and raises if the last geqrf that used
+    ``workspace`` recorded a device-side wait that gave up."""
+    stream = torch.cuda.current_stream(workspace.device).cuda_stream
+    rc = load().fqr_check_status(workspace.data_ptr(), workspace.numel() * workspace.element_size(),
+                                 batch, stream)
+    if rc:
+        raise FastQRError(rc, "fqr_check_status")
+
+
 def geqrf_profile(a: torch.Tensor, out, workspace) -> dict:
     """Run one geqrf with a CUDA event pair around every kernel (blocking).
     Returns the summed device milliseconds per kernel class."""

@@ -111,6 +111,15 @@ int fqr_geqrf_f32_noalloc(const float *A, int64_t batch, int64_t n, int64_t a_bs
                           int64_t a_rstride, int64_t a_cstride, float *H, float *tau,
                           void *stream);
 
+/*
+ * Synchronizes `stream`, then reports whether the last fqr_geqrf_f32 that
+ * used `workspace` (for `batch` matrices) hit a bounded device-side wait that
+ * gave up: FQR_OK or FQR_ETIMEOUT.  The tensor-core kernels never spin
+ * without a limit; on giving up they record it here and return.  No
+ * counterpart in the reference, whose kernels have no device-side waits.
+ */
+int fqr_check_status(const void *workspace, size_t workspace_bytes, int64_t batch, void *stream);
+
 /* Kernel classes timed by fqr_geqrf_f32_profile. */
 enum {
     FQR_STAGE_SMALL = 0,     /* warp-per-matrix kernel (n <= 64) */

@@ -58,7 +58,7 @@ def test_argument_validation_without_gpu():
 
 def test_workspace_and_plan_depend_on_shape_only():
     assert fastqr.workspace_bytes(1024, 32) == 0
-    assert fastqr.workspace_bytes(256, 256) == 256 * 32 * 32 * 4
+    assert fastqr.workspace_bytes(256, 256) == 256 * 32 * 32 * 4 + 256  # T factors + status
     assert fastqr.workspace_bytes(3, 100) % 256 == 0
     assert fastqr.plan(1024, 32).startswith("small")
     assert fastqr.plan(256, 256).startswith("blocked")

@@ -229,3 +229,24 @@ def test_large_n_properties(n, batch, dev):
     h, t = fastqr.geqrf(a)
     g = gates(a, h, t, chunk=1)
     assert g["ok"], g
+
+
+@pytest.mark.parametrize("n", [128, 256, 512, 1024])
+def test_tensor_core_path_reports_no_timeout(n, dev):
+    """The tcgen05 trailing update records any bounded wait that gave up in
+    the workspace status word; a normal run must leave it clear."""
+    assert "tcgen05" in fastqr.plan(4, n)
+    a = inputs.generate_input(4, n, 1, 4242 + n, device=dev)
+    ws = torch.empty(fastqr.workspace_bytes(4, n), dtype=torch.uint8, device=dev)
+    h, t = fastqr.geqrf(a, workspace=ws)
+    fastqr.check_status(ws, 4)
+    assert gates(a, h, t)["ok"]
+
+
+def test_simt_fallback_for_unaligned_sizes(dev):
+    """n % 4 != 0 takes the SIMT trailing update; results equal in quality."""
+    assert "simt" in fastqr.plan(2, 258)
+    a = inputs.generate_input(2, 258, 1, 77, device=dev)
+    h, t = fastqr.geqrf(a)
+    g = gates(a, h, t)
+    assert g["ok"], g
