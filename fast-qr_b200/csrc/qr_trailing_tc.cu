@@ -5,15 +5,19 @@
 // update fails the factor gate (the reference's own evidence,
 // tests/test_qr_smoke.py:217-229; restated in tests/test_oracle.py).
 //
-// One CTA (4 warps) owns a tile of kTN = 128 trailing columns of one matrix:
+// One CTA (4 warps, two CTAs per SM) owns a tile of kTN = 128 trailing
+// columns of one matrix:
 //   phase A  W^T[c][j] = sum_r C(r, c) V(r, j)    tcgen05.mma M=128 (c) N=32 (j),
-//            K = rows, accumulated over 128-row chunks into TMEM
+//            K = rows, accumulated over 64-row chunks into TMEM; the chunks
+//            arrive by cp.async (all 40 KB in flight at once)
 //   phase B  Y = T^T W                            per thread (one column c)
 //   phase C  P[r][c] = sum_j V(r, j) Y(j, c)      tcgen05.mma M=128 (r) N=128 (c)
 //            K = 32 per 128-row chunk; epilogue C(r, c) -= P from TMEM
-// Operands are staged by the threads (global -> registers -> hi/lo split ->
-// shared memory) in the no-swizzle K-major "core matrix" layout: a core holds
-// 8 rows of the M/N dimension x 4 consecutive K elements (16 bytes per row).
+// Operands sit in shared memory in the no-swizzle K-major "core matrix"
+// layout (a core holds 8 rows of the M/N dimension x 4 consecutive K
+// elements, 16 bytes per row).  The raw fp32 data is the hi operand (the
+// tensor core truncates it to TF32); threads write lo = x - trunc_tf32(x) into
+// a second buffer.
 // The reference's trailing_update_kernel (submissions/candidate.py:2507-2716)
 // is SIMT FP32 with T recomputed in every CTA; nothing here follows it.
 #include "common.cuh"
@@ -25,61 +29,65 @@ namespace fqr {
 namespace {
 
 constexpr int kTN = 128;          // trailing columns per CTA
-constexpr int kRC = 128;          // rows per chunk
+constexpr int kRC = 64;           // rows per phase-A chunk (MMA K)
+constexpr int kRCC = 128;         // rows per phase-C chunk (MMA M)
 constexpr int kThreads = 128;
 constexpr uint32_t kTmemCols = 256;
 constexpr uint32_t kDA = 0;       // TMEM column of W^T (32 columns)
 constexpr uint32_t kDC = 128;     // TMEM column of P (128 columns)
 constexpr uint64_t kWaitLimit = 1000000000ull;  // 1 s of wall time per wait
 
-// shared memory map (bytes)
-constexpr int kOffChi = 0;        // C^T chunk hi: 128 c x 128 r (64 KB)
-constexpr int kOffClo = 65536;    // C^T chunk lo (64 KB)
-constexpr int kOffVhi = 131072;   // V chunk hi: 32 j x 128 r (16 KB)
-constexpr int kOffVlo = 147456;   // V chunk lo (16 KB)
-constexpr int kOffT = 163840;     // T, column-major 32 x 32 (4 KB)
-constexpr int kOffBar = 167936;   // mbarrier (8 B) + TMEM base address (4 B)
-constexpr int kSmem = kOffBar + 64;
-constexpr int kOffYhi = kOffChi;  // Y: 128 c x 32 j (16 KB), reuses the C area in phase C
-constexpr int kOffYlo = kOffChi + 16384;
+// shared memory map (bytes).  Phase A: C^T and V chunks as raw fp32 (the hi
+// operand) plus lo = x - trunc_tf32(x); K-major cores of 8 rows x 4 K.
+constexpr int kCQ = kRC / 4;                // cores along K in a phase-A row
+constexpr int kOffCraw = 0;                 // 128 c x 64 r (32 KB)
+constexpr int kOffClo = 32768;              // (32 KB)
+constexpr int kOffVraw = 65536;             // 32 j x 64 r (8 KB)
+constexpr int kOffVlo = 73728;              // (8 KB)
+constexpr int kOffT = 81920;                // T, column-major 32 x 32 (4 KB)
+constexpr int kOffBar = 86016;              // mbarrier (8 B) + TMEM base address (4 B)
+constexpr int kSmem = kOffBar + 64;         // 2 CTAs per SM
+// Phase C (reuses the phase-A area): V chunk as the K-major A operand
+// (128 r x 32 j) and Y as the K-major B operand (128 c x 32 j), raw + lo.
+constexpr int kOffVCraw = 0;
+constexpr int kOffVClo = 16384;
+constexpr int kOffYraw = 32768;
+constexpr int kOffYlo = 49152;
 
-constexpr uint32_t kIdescA = tc::idesc_tf32(128, 32, 0, 0);   // K-major A (C^T), K-major B (V)
-constexpr uint32_t kIdescC = tc::idesc_tf32(128, 128, 0, 0);  // K-major A (V), K-major B (Y)
+constexpr uint32_t kIdescA = tc::idesc_tf32(128, 32, 0, 0);   // A = C^T (M = c), B = V (N = j)
+constexpr uint32_t kIdescC = tc::idesc_tf32(128, 128, 0, 0);  // A = V (M = r), B = Y (N = c)
 
-// Stage NO columns x kRC rows of a column-major matrix (column o at
-// base + o * ld, rows r0 ..) into hi/lo core layouts: core (o/8, r/4) at
-// ((o/8) * 32 + r/4) * 128 bytes, column o%8 at +16 * (o%8).  Each warp
-// iteration moves 8 columns x 16 rows: 64 contiguous bytes per column from
-// global memory, 512 contiguous bytes of shared memory.
-// UNIT selects V's unit-lower mask (panel rows < j are 0, row j is 1).
-template <int NO, bool UNIT>
-__device__ __forceinline__ void stage_cols(const float *base, int64_t ld, int r0, int rows, int cols,
-                                           unsigned char *hi, unsigned char *lo, int warp, int lane)
+// cp.async a [NO columns] x [kRC rows] block of a column-major matrix
+// (column o at base + o * ld, panel rows r0 ..) into the K-major core layout:
+// core (o/8, r/4) at ((o/8) * kCQ + r/4) * 128 bytes, column o%8 at
+// +16 * (o%8).  A warp step copies 8 columns x 4 row quads (64 contiguous
+// bytes per column; 512 contiguous bytes of shared memory).  Rows >= rows
+// and columns >= cols are zero-filled.
+template <int NO>
+__device__ __forceinline__ void copy_block(const float *base, int64_t ld, int r0, int rows, int cols,
+                                           unsigned char *dst, int warp, int lane)
 {
-    constexpr int ITER = (NO / 8) * 8;  // (column groups) x (row-quad groups of 4)
+    constexpr int ITER = (NO / 8) * (kCQ / 4);
     const int oc = lane & 7, qi = lane >> 3;
-#pragma unroll 4
-    for (int it = warp; it < ITER; it += 4) {
-        const int og = it >> 3, qg = it & 7;
-        const int o = og * 8 + oc;
-        const int rq = qg * 4 + qi;      // row quad within the chunk, 0..31
-        const int r = r0 + rq * 4;       // first panel row of the quad
-        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        if (o < cols && r < rows) v = __ldg(reinterpret_cast<const float4 *>(base + (int64_t)o * ld + r));
-        if (UNIT) {
-            float e[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-            for (int i = 0; i < 4; ++i) e[i] = (r + i < o) ? 0.0f : ((r + i == o) ? 1.0f : e[i]);
-            v = make_float4(e[0], e[1], e[2], e[3]);
-        }
-        float4 h, l;
-        tc::split_tf32(v.x, h.x, l.x);
-        tc::split_tf32(v.y, h.y, l.y);
-        tc::split_tf32(v.z, h.z, l.z);
-        tc::split_tf32(v.w, h.w, l.w);
-        const uint32_t off = (uint32_t)((og * 32 + rq) * 128 + oc * 16);
-        *reinterpret_cast<float4 *>(hi + off) = h;
-        *reinterpret_cast<float4 *>(lo + off) = l;
+    for (int it = warp; it < ITER; it += 4) {
+        const int og = it / (kCQ / 4), qg = it % (kCQ / 4);
+        const int o = og * 8 + oc;
+        const int rq = qg * 4 + qi;  // row quad in the chunk
+        const int r = r0 + 4 * rq;
+        const bool valid = o < cols && r < rows;
+        const float *src = valid ? base + (int64_t)o * ld + r : base;
+        tc::cp_async16(dst + (og * kCQ + rq) * 128 + oc * 16, src, valid ? 16u : 0u);
+    }
+}
+
+// lo = x - trunc_tf32(x) over `bytes` of shared memory, elementwise
+__device__ __forceinline__ void make_lo(const unsigned char *raw, unsigned char *lo, int bytes, int tid)
+{
+    for (int off = tid * 16; off < bytes; off += kThreads * 16) {
+        const float4 v = *reinterpret_cast<const float4 *>(raw + off);
+        *reinterpret_cast<float4 *>(lo + off) =
+            make_float4(tc::tf32_lo(v.x), tc::tf32_lo(v.y), tc::tf32_lo(v.z), tc::tf32_lo(v.w));
     }
 }
 
@@ -88,33 +96,26 @@ __device__ __forceinline__ void stage_cols(const float *base, int64_t ld, int r0
 // +16 * (r%8).  Thread = row: 4 column loads (coalesced across the warp) per
 // 16-byte store; a warp's stores cover 4 contiguous 128-byte cores.
 __device__ __forceinline__ void stage_v_kmajor(const float *Vbase, int64_t ld, int r0, int rows,
-                                               unsigned char *hi, unsigned char *lo, int tid)
+                                               unsigned char *raw, unsigned char *lo, int tid)
 {
     const int r = r0 + tid;  // panel row
-#pragma unroll 2
-    for (int jq = 0; jq < kPanel / 4; ++jq) {
-        float e[4];
+    float e[kPanel];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int j = 4 * jq + i;
-            float v = 0.0f;
-            if (r < rows) v = r > j ? __ldg(Vbase + (int64_t)j * ld + r) : (r == j ? 1.0f : 0.0f);
-            e[i] = v;
-        }
-        float4 h, l;
-        tc::split_tf32(e[0], h.x, l.x);
-        tc::split_tf32(e[1], h.y, l.y);
-        tc::split_tf32(e[2], h.z, l.z);
-        tc::split_tf32(e[3], h.w, l.w);
+    for (int j = 0; j < kPanel; ++j)
+        e[j] = (r < rows && r > j) ? __ldg(Vbase + (int64_t)j * ld + r) : (r == j ? 1.0f : 0.0f);
+#pragma unroll
+    for (int jq = 0; jq < kPanel / 4; ++jq) {
         const uint32_t off = (uint32_t)(((tid >> 3) * 8 + jq) * 128 + (tid & 7) * 16);
-        *reinterpret_cast<float4 *>(hi + off) = h;
-        *reinterpret_cast<float4 *>(lo + off) = l;
+        const float4 v = make_float4(e[4 * jq], e[4 * jq + 1], e[4 * jq + 2], e[4 * jq + 3]);
+        *reinterpret_cast<float4 *>(raw + off) = v;
+        *reinterpret_cast<float4 *>(lo + off) =
+            make_float4(tc::tf32_lo(v.x), tc::tf32_lo(v.y), tc::tf32_lo(v.z), tc::tf32_lo(v.w));
     }
 }
 
 }  // namespace
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
 trailing_tc_kernel(float *__restrict__ H, const float *__restrict__ Tws, int *__restrict__ status,
                    int n, int k)
 {
@@ -148,26 +149,39 @@ trailing_tc_kernel(float *__restrict__ H, const float *__restrict__ Tws, int *__
     const uint32_t tmem = *tmem_slot;
     uint32_t phase = 0;
     bool ok = true;
-
-    const uint32_t sChi = tc::smem_addr(smem + kOffChi), sClo = tc::smem_addr(smem + kOffClo);
-    const uint32_t sVhi = tc::smem_addr(smem + kOffVhi), sVlo = tc::smem_addr(smem + kOffVlo);
-    const uint32_t sYhi = tc::smem_addr(smem + kOffYhi), sYlo = tc::smem_addr(smem + kOffYlo);
+    const uint32_t sbase = tc::smem_addr(smem);
 
     // ---- phase A: W^T = C^T V over all rows --------------------------------
     for (int r0 = 0; r0 < m && ok; r0 += kRC) {
-        stage_cols<kTN, false>(Cbase, n, r0, m, nct, smem + kOffChi, smem + kOffClo, warp, lane);
-        stage_cols<kPanel, true>(Vbase, n, r0, m, kPanel, smem + kOffVhi, smem + kOffVlo, warp, lane);
+        copy_block<kTN>(Cbase, n, r0, m, nct, smem + kOffCraw, warp, lane);
+        copy_block<kPanel>(Vbase, n, r0, m, kPanel, smem + kOffVraw, warp, lane);
+        tc::cp_async_commit();
+        tc::cp_async_wait_all();
+        __syncthreads();
+        if (r0 == 0) {
+            // V is unit lower triangular: panel rows r < j are 0, row j is 1
+            for (int e = tid; e < kPanel * kPanel; e += kThreads) {
+                const int j = e >> 5, r = e & 31;
+                if (r <= j) {
+                    const int off = ((j >> 3) * kCQ + (r >> 2)) * 128 + (j & 7) * 16 + (r & 3) * 4;
+                    *reinterpret_cast<float *>(smem + kOffVraw + off) = r == j ? 1.0f : 0.0f;
+                }
+            }
+            __syncthreads();
+        }
+        make_lo(smem + kOffCraw, smem + kOffClo, kTN * kRC * 4, tid);
+        make_lo(smem + kOffVraw, smem + kOffVlo, kPanel * kRC * 4, tid);
         tc::fence_proxy_async_smem();
         __syncthreads();
         if (tid == 0) {
             tc::fence_after_sync();
-#pragma unroll 1
+#pragma unroll
             for (int s = 0; s < kRC / 8; ++s) {
                 const uint32_t ko = (uint32_t)s * 256;  // 8 rows = 2 cores along K
-                const uint64_t ah = tc::smem_desc(sChi + ko, 128, 4096);
-                const uint64_t al = tc::smem_desc(sClo + ko, 128, 4096);
-                const uint64_t bh = tc::smem_desc(sVhi + ko, 128, 4096);
-                const uint64_t bl = tc::smem_desc(sVlo + ko, 128, 4096);
+                const uint64_t ah = tc::smem_desc(sbase + kOffCraw + ko, 128, kCQ * 128);
+                const uint64_t al = tc::smem_desc(sbase + kOffClo + ko, 128, kCQ * 128);
+                const uint64_t bh = tc::smem_desc(sbase + kOffVraw + ko, 128, kCQ * 128);
+                const uint64_t bl = tc::smem_desc(sbase + kOffVlo + ko, 128, kCQ * 128);
                 const uint32_t acc = (r0 > 0 || s > 0) ? 1u : 0u;
                 tc::mma_tf32(tmem + kDA, al, bh, kIdescA, acc);
                 tc::mma_tf32(tmem + kDA, ah, bl, kIdescA, 1u);
@@ -199,21 +213,18 @@ trailing_tc_kernel(float *__restrict__ H, const float *__restrict__ Tws, int *__
         // ((c/8) * 8 + j/4) * 128 bytes, column c%8 at +16 * (c%8)
 #pragma unroll
         for (int jq = 0; jq < 8; ++jq) {
-            float4 h, l;
-            tc::split_tf32(y[4 * jq + 0], h.x, l.x);
-            tc::split_tf32(y[4 * jq + 1], h.y, l.y);
-            tc::split_tf32(y[4 * jq + 2], h.z, l.z);
-            tc::split_tf32(y[4 * jq + 3], h.w, l.w);
+            const float4 v = make_float4(y[4 * jq], y[4 * jq + 1], y[4 * jq + 2], y[4 * jq + 3]);
             const uint32_t off = (uint32_t)(((c >> 3) * 8 + jq) * 128 + (c & 7) * 16);
-            *reinterpret_cast<float4 *>(smem + kOffYhi + off) = h;
-            *reinterpret_cast<float4 *>(smem + kOffYlo + off) = l;
+            *reinterpret_cast<float4 *>(smem + kOffYraw + off) = v;
+            *reinterpret_cast<float4 *>(smem + kOffYlo + off) =
+                make_float4(tc::tf32_lo(v.x), tc::tf32_lo(v.y), tc::tf32_lo(v.z), tc::tf32_lo(v.w));
         }
         tc::fence_before_sync();
     }
 
     // ---- phase C: C -= V Y, 128 rows per chunk -----------------------------
-    for (int r0 = 0; r0 < m && ok; r0 += kRC) {
-        stage_v_kmajor(Vbase, n, r0, m, smem + kOffVhi, smem + kOffVlo, tid);
+    for (int r0 = 0; r0 < m && ok; r0 += kRCC) {
+        stage_v_kmajor(Vbase, n, r0, m, smem + kOffVCraw, smem + kOffVClo, tid);
         tc::fence_proxy_async_smem();
         __syncthreads();
         if (tid == 0) {
@@ -222,10 +233,10 @@ trailing_tc_kernel(float *__restrict__ H, const float *__restrict__ Tws, int *__
             for (int s = 0; s < kPanel / 8; ++s) {
                 // A = V (K-major, M = rows), B = Y (K-major, N = columns):
                 // 8 K-columns = 2 cores = 256 bytes per step
-                const uint64_t ah = tc::smem_desc(sVhi + (uint32_t)s * 256, 128, 1024);
-                const uint64_t al = tc::smem_desc(sVlo + (uint32_t)s * 256, 128, 1024);
-                const uint64_t bh = tc::smem_desc(sYhi + (uint32_t)s * 256, 128, 1024);
-                const uint64_t bl = tc::smem_desc(sYlo + (uint32_t)s * 256, 128, 1024);
+                const uint64_t ah = tc::smem_desc(sbase + kOffVCraw + (uint32_t)s * 256, 128, 1024);
+                const uint64_t al = tc::smem_desc(sbase + kOffVClo + (uint32_t)s * 256, 128, 1024);
+                const uint64_t bh = tc::smem_desc(sbase + kOffYraw + (uint32_t)s * 256, 128, 1024);
+                const uint64_t bl = tc::smem_desc(sbase + kOffYlo + (uint32_t)s * 256, 128, 1024);
                 tc::mma_tf32(tmem + kDC, al, bh, kIdescC, s > 0 ? 1u : 0u);
                 tc::mma_tf32(tmem + kDC, ah, bl, kIdescC, 1u);
                 tc::mma_tf32(tmem + kDC, ah, bh, kIdescC, 1u);
@@ -237,7 +248,8 @@ trailing_tc_kernel(float *__restrict__ H, const float *__restrict__ Tws, int *__
         ok = !__syncthreads_or(!done);
         if (!ok) break;
         tc::fence_after_sync();
-        // epilogue: thread = row r0 + 32 warp + lane, 128 columns from TMEM
+        // epilogue: thread = row r0 + 32 warp + lane, 128 columns from TMEM;
+        // all loads of a 32-column group are issued before any store
         const int r = r0 + 32 * warp + lane;
         float *Crow = Hm + (int64_t)c0 * n + k + r;
 #pragma unroll 1
@@ -245,11 +257,17 @@ trailing_tc_kernel(float *__restrict__ H, const float *__restrict__ Tws, int *__
             float p[32];
             tc::tmem_ld_32x32(tmem + ((uint32_t)(32 * warp) << 16) + kDC + 32 * cc, p);
             tc::tmem_ld_wait();
-            if (r < m) {
+            if (r < m && 32 * cc < nct) {
+                float cv[32];
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
                     const int c = 32 * cc + i;
-                    if (c < nct) Crow[(int64_t)c * n] -= p[i];
+                    cv[i] = c < nct ? Crow[(int64_t)c * n] : 0.0f;
+                }
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const int c = 32 * cc + i;
+                    if (c < nct) Crow[(int64_t)c * n] = cv[i] - p[i];
                 }
             }
         }

@@ -154,7 +154,31 @@ __device__ __forceinline__ void tmem_ld_wait()
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// --- asynchronous 16-byte global -> shared copies (cp.async, L2 only) -----
+// src_bytes = 0 zero-fills the destination without reading the source.
+__device__ __forceinline__ void cp_async16(void *dst_smem, const void *src, uint32_t src_bytes)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;"
+                 :: "r"(smem_addr(dst_smem)), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit()
+{
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all()
+{
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+}
+
 // --- 3xTF32 split: x = hi + lo with hi exactly representable in TF32 -------
+// kind::tf32 reads a 32-bit operand by dropping its 13 low mantissa bits
+// (measured: raw fp32 operands give bitwise the same products as their
+// truncated copies), so the raw fp32 data serves as the hi operand and only
+// lo = x - trunc_tf32(x) needs a second buffer.
+__device__ __forceinline__ float tf32_lo(float x)
+{
+    return x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+}
 __device__ __forceinline__ void split_tf32(float x, float &hi, float &lo)
 {
     hi = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
