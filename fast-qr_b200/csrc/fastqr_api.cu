@@ -169,8 +169,8 @@ int run_geqrf(const float *A, int64_t batch, int64_t n, int64_t a_bstride, int64
         if (e != cudaSuccess) return status_from(e);
         if (k + fqr::kPanel < ni) {
             if (tm) tm->begin(FQR_STAGE_TRAILING);
-            e = tc ? fqr::launch_trailing_tc(H, Tws, status, batch, ni, k, st)
-                   : fqr::launch_trailing(H, Tws, batch, ni, k, st);
+            e = tc ? fqr::launch_trailing_tc(H, Tws, tau, status, batch, ni, k, st)
+                   : fqr::launch_trailing(H, Tws, tau, batch, ni, k, st);
             if (tm) tm->end();
             if (e != cudaSuccess) return status_from(e);
         }

@@ -19,17 +19,18 @@ cudaError_t launch_copy_in(const float *A, int64_t batch, int n, int64_t bs, int
                            float *H, int *status, cudaStream_t st);
 cudaError_t launch_panel(float *H, float *tau, float *Tws, int64_t batch, int n, int k,
                          cudaStream_t st);
-cudaError_t launch_trailing(float *H, const float *Tws, int64_t batch, int n, int k,
+cudaError_t launch_trailing(float *H, const float *Sws, const float *tau, int64_t batch, int n, int k,
                             cudaStream_t st);
 
 // Tensor-core (tcgen05, 3xTF32) trailing update; needs n % 4 == 0, n >= 128
 // and a 16-byte aligned H.  Sets *status to nonzero if a bounded wait gave up.
 bool trailing_tc_supported(int n);
-cudaError_t launch_trailing_tc(float *H, const float *Tws, int *status, int64_t batch, int n, int k,
-                               cudaStream_t st);
+cudaError_t launch_trailing_tc(float *H, const float *Sws, const float *tau, int *status, int64_t batch,
+                               int n, int k, cudaStream_t st);
 
-// Workspace layout: one 32 x 32 float T factor per matrix, then a 256-byte
-// status block (int status word first).
+// Workspace layout: one 32 x 32 float block per matrix holding the panel's
+// S = V^T V (strictly upper; the compact-WY T factor is T = D (I + S D)^-1,
+// D = diag(tau)), then a 256-byte status block (int status word first).
 constexpr size_t kWsAlign = 256;
 constexpr size_t ws_t_bytes(int64_t batch)
 {

@@ -10,7 +10,9 @@
 //   phase A  W^T[c][j] = sum_r C(r, c) V(r, j)    tcgen05.mma M=128 (c) N=32 (j),
 //            K = rows, accumulated over 64-row chunks into TMEM; the chunks
 //            arrive by cp.async (all 40 KB in flight at once)
-//   phase B  Y = T^T W                            per thread (one column c)
+//   phase B  Y = T^T W                            per thread (one column c), by
+//            forward substitution with S = V^T V (strict upper) and tau:
+//            T = D (I + S D)^-1, so (I + D S^T) Y = D W
 //   phase C  P[r][c] = sum_j V(r, j) Y(j, c)      tcgen05.mma M=128 (r) N=128 (c)
 //            K = 32 per 128-row chunk; epilogue C(r, c) -= P from TMEM
 // Operands sit in shared memory in the no-swizzle K-major "core matrix"
@@ -44,8 +46,9 @@ constexpr int kOffCraw = 0;                 // 128 c x 64 r (32 KB)
 constexpr int kOffClo = 32768;              // (32 KB)
 constexpr int kOffVraw = 65536;             // 32 j x 64 r (8 KB)
 constexpr int kOffVlo = 73728;              // (8 KB)
-constexpr int kOffT = 81920;                // T, column-major 32 x 32 (4 KB)
-constexpr int kOffBar = 86016;              // mbarrier (8 B) + TMEM base address (4 B)
+constexpr int kOffT = 81920;                // S, column-major 32 x 32 (4 KB)
+constexpr int kOffTau = 86016;              // tau of the panel (128 B)
+constexpr int kOffBar = 86144;              // mbarrier (8 B) + TMEM base address (4 B)
 constexpr int kSmem = kOffBar + 64;         // 2 CTAs per SM
 // Phase C (reuses the phase-A area): V chunk as the K-major A operand
 // (128 r x 32 j) and Y as the K-major B operand (128 c x 32 j), raw + lo.
@@ -116,8 +119,8 @@ __device__ __forceinline__ void stage_v_kmajor(const float *Vbase, int64_t ld, i
 }  // namespace
 
 __global__ void __launch_bounds__(kThreads, 2)
-trailing_tc_kernel(float *__restrict__ H, const float *__restrict__ Tws, int *__restrict__ status,
-                   int n, int k)
+trailing_tc_kernel(float *__restrict__ H, const float *__restrict__ Sws, const float *__restrict__ tau,
+                   int *__restrict__ status, int n, int k)
 {
     extern __shared__ __align__(1024) unsigned char smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -131,7 +134,8 @@ trailing_tc_kernel(float *__restrict__ H, const float *__restrict__ Tws, int *__
 
     uint64_t *bar = reinterpret_cast<uint64_t *>(smem + kOffBar);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kOffBar + 8);
-    float *Ts = reinterpret_cast<float *>(smem + kOffT);
+    float *Ts = reinterpret_cast<float *>(smem + kOffT);    // S(l, c) at c * 32 + l
+    float *taus = reinterpret_cast<float *>(smem + kOffTau);
 
     if (warp == 0) {
         tc::tmem_alloc(tmem_slot, kTmemCols);
@@ -141,8 +145,9 @@ trailing_tc_kernel(float *__restrict__ H, const float *__restrict__ Tws, int *__
         tc::mbar_init(bar, 1);
         tc::fence_mbar_init();
     }
-    const float *Tm = Tws + mat * (kPanel * kPanel);
-    for (int i = tid; i < kPanel * kPanel; i += kThreads) Ts[i] = Tm[i];
+    const float *Sm = Sws + mat * (kPanel * kPanel);
+    for (int i = tid; i < kPanel * kPanel; i += kThreads) Ts[i] = Sm[i];
+    if (tid < kPanel) taus[tid] = tau[mat * n + k + tid];
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
@@ -201,13 +206,15 @@ trailing_tc_kernel(float *__restrict__ H, const float *__restrict__ Tws, int *__
         tc::tmem_ld_32x32(tmem + ((uint32_t)(32 * warp) << 16) + kDA, w);
         tc::tmem_ld_wait();
         const int c = 32 * warp + lane;
+        // Y = T^T W with T = D (I + S D)^-1: forward substitution
+        //   y_c = tau_c (w_c - sum_{l < c} S(l, c) y_l)
         float y[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-            float a4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        for (int c = 0; c < 32; ++c) {
+            float a = w[c];
 #pragma unroll
-            for (int l = 0; l <= j; ++l) a4[l & 3] = fmaf(Ts[j * 32 + l], w[l], a4[l & 3]);
-            y[j] = (a4[0] + a4[1]) + (a4[2] + a4[3]);
+            for (int l = 0; l < c; ++l) a = fmaf(-Ts[c * 32 + l], y[l], a);
+            y[c] = taus[c] * a;
         }
         // Y as the K-major B operand of phase C: core (c/8, j/4) at
         // ((c/8) * 8 + j/4) * 128 bytes, column c%8 at +16 * (c%8)
@@ -293,8 +300,8 @@ bool trailing_tc_supported(int n)
     return n % 4 == 0 && n >= 128;
 }
 
-cudaError_t launch_trailing_tc(float *H, const float *Tws, int *status, int64_t batch, int n, int k,
-                               cudaStream_t st)
+cudaError_t launch_trailing_tc(float *H, const float *Sws, const float *tau, int *status, int64_t batch,
+                               int n, int k, cudaStream_t st)
 {
     const int nc = n - k - kPanel;
     if (nc <= 0) return cudaSuccess;
@@ -306,7 +313,8 @@ cudaError_t launch_trailing_tc(float *H, const float *Tws, int *status, int64_t 
         const int64_t nb = (batch - b0) < 65535 ? (batch - b0) : 65535;
         dim3 grid(tiles, (unsigned)nb);
         trailing_tc_kernel<<<grid, kThreads, kSmem, st>>>(H + b0 * (int64_t)n * n,
-                                                          Tws + b0 * kPanel * kPanel, status, n, k);
+                                                          Sws + b0 * kPanel * kPanel, tau + b0 * n,
+                                                          status, n, k);
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
