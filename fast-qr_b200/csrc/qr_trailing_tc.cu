@@ -8,8 +8,9 @@
 // One CTA (4 warps, two CTAs per SM) owns a tile of kTN = 128 trailing
 // columns of one matrix:
 //   phase A  W^T[c][j] = sum_r C(r, c) V(r, j)    tcgen05.mma M=128 (c) N=32 (j),
-//            K = rows, accumulated over 64-row chunks into TMEM; the chunks
-//            arrive by cp.async (all 40 KB in flight at once)
+//            K = rows, accumulated over 32-row chunks into TMEM; the chunks
+//            stream in by cp.async through a 3-stage ring (two in flight
+//            while one is split and multiplied)
 //   phase B  Y = T^T W                            per thread (one column c), by
 //            forward substitution with S = V^T V (strict upper) and tau:
 //            T = D (I + S D)^-1, so (I + D S^T) Y = D W
@@ -31,7 +32,8 @@ namespace fqr {
 namespace {
 
 constexpr int kTN = 128;          // trailing columns per CTA
-constexpr int kRC = 64;           // rows per phase-A chunk (MMA K)
+constexpr int kRC = 32;           // rows per phase-A chunk (MMA K)
+constexpr int kStages = 3;        // phase-A chunks in flight
 constexpr int kRCC = 128;         // rows per phase-C chunk (MMA M)
 constexpr int kThreads = 128;
 constexpr uint32_t kTmemCols = 256;
@@ -39,23 +41,24 @@ constexpr uint32_t kDA = 0;       // TMEM column of W^T (32 columns)
 constexpr uint32_t kDC = 128;     // TMEM column of P (128 columns)
 constexpr uint64_t kWaitLimit = 1000000000ull;  // 1 s of wall time per wait
 
-// shared memory map (bytes).  Phase A: C^T and V chunks as raw fp32 (the hi
-// operand) plus lo = x - trunc_tf32(x); K-major cores of 8 rows x 4 K.
-constexpr int kCQ = kRC / 4;                // cores along K in a phase-A row
-constexpr int kOffCraw = 0;                 // 128 c x 64 r (32 KB)
-constexpr int kOffClo = 32768;              // (32 KB)
-constexpr int kOffVraw = 65536;             // 32 j x 64 r (8 KB)
-constexpr int kOffVlo = 73728;              // (8 KB)
-constexpr int kOffT = 81920;                // S, column-major 32 x 32 (4 KB)
-constexpr int kOffTau = 86016;              // tau of the panel (128 B)
-constexpr int kOffBar = 86144;              // mbarrier (8 B) + TMEM base address (4 B)
-constexpr int kSmem = kOffBar + 64;         // 2 CTAs per SM
+// shared memory map (bytes).  Phase A: a ring of kStages chunks, each C^T
+// (128 c x 32 r) and V (32 j x 32 r) as raw fp32 -- the hi operand -- plus
+// one lo = x - trunc_tf32(x) buffer; K-major cores of 8 rows x 4 K.
+constexpr int kCQ = kRC / 4;                    // cores along K in a row of cores
+constexpr int kStageBytes = (kTN + kPanel) * kRC * 4;  // 20 KB
+constexpr int kOffLoC = kStages * kStageBytes;  // 60 KB
+constexpr int kOffLoV = kOffLoC + kTN * kRC * 4;
+constexpr int kOffT = kOffLoV + kPanel * kRC * 4;   // S, column-major 32 x 32 (4 KB)
+constexpr int kOffTau = kOffT + 4096;               // tau of the panel (128 B)
+constexpr int kOffBar = kOffTau + 128;              // mbarrier (8 B) + TMEM base address (4 B)
+constexpr int kSmem = kOffBar + 64;                 // ~86 KB: 2 CTAs per SM
 // Phase C (reuses the phase-A area): V chunk as the K-major A operand
 // (128 r x 32 j) and Y as the K-major B operand (128 c x 32 j), raw + lo.
 constexpr int kOffVCraw = 0;
 constexpr int kOffVClo = 16384;
 constexpr int kOffYraw = 32768;
 constexpr int kOffYlo = 49152;
+static_assert(kOffYlo + 16384 <= kOffT, "phase-C buffers overlap S");
 
 constexpr uint32_t kIdescA = tc::idesc_tf32(128, 32, 0, 0);   // A = C^T (M = c), B = V (N = j)
 constexpr uint32_t kIdescC = tc::idesc_tf32(128, 128, 0, 0);  // A = V (M = r), B = Y (N = c)
@@ -87,6 +90,7 @@ __device__ __forceinline__ void copy_block(const float *base, int64_t ld, int r0
 // lo = x - trunc_tf32(x) over `bytes` of shared memory, elementwise
 __device__ __forceinline__ void make_lo(const unsigned char *raw, unsigned char *lo, int bytes, int tid)
 {
+#pragma unroll 4
     for (int off = tid * 16; off < bytes; off += kThreads * 16) {
         const float4 v = *reinterpret_cast<const float4 *>(raw + off);
         *reinterpret_cast<float4 *>(lo + off) =
@@ -137,6 +141,18 @@ trailing_tc_kernel(float *__restrict__ H, const float *__restrict__ Sws, const f
     float *Ts = reinterpret_cast<float *>(smem + kOffT);    // S(l, c) at c * 32 + l
     float *taus = reinterpret_cast<float *>(smem + kOffTau);
 
+    // phase-A prologue: the first kStages chunks start streaming at once
+    const int nchunks = (m + kRC - 1) / kRC;
+#pragma unroll
+    for (int s = 0; s < kStages; ++s) {
+        if (s < nchunks) {
+            unsigned char *st = smem + s * kStageBytes;
+            copy_block<kTN>(Cbase, n, s * kRC, m, nct, st, warp, lane);
+            copy_block<kPanel>(Vbase, n, s * kRC, m, kPanel, st + kTN * kRC * 4, warp, lane);
+        }
+        tc::cp_async_commit();
+    }
+
     if (warp == 0) {
         tc::tmem_alloc(tmem_slot, kTmemCols);
         tc::tmem_relinquish();
@@ -156,38 +172,38 @@ trailing_tc_kernel(float *__restrict__ H, const float *__restrict__ Sws, const f
     bool ok = true;
     const uint32_t sbase = tc::smem_addr(smem);
 
-    // ---- phase A: W^T = C^T V over all rows --------------------------------
-    for (int r0 = 0; r0 < m && ok; r0 += kRC) {
-        copy_block<kTN>(Cbase, n, r0, m, nct, smem + kOffCraw, warp, lane);
-        copy_block<kPanel>(Vbase, n, r0, m, kPanel, smem + kOffVraw, warp, lane);
-        tc::cp_async_commit();
-        tc::cp_async_wait_all();
+    // ---- phase A: W^T = C^T V over all rows, kStages chunks in flight -----
+    for (int i = 0; i < nchunks && ok; ++i) {
+        const int sidx = i % kStages;
+        unsigned char *st = smem + sidx * kStageBytes;
+        tc::cp_async_wait_pending<kStages - 1>();  // chunk i has landed
         __syncthreads();
-        if (r0 == 0) {
+        if (i == 0) {
             // V is unit lower triangular: panel rows r < j are 0, row j is 1
             for (int e = tid; e < kPanel * kPanel; e += kThreads) {
                 const int j = e >> 5, r = e & 31;
                 if (r <= j) {
                     const int off = ((j >> 3) * kCQ + (r >> 2)) * 128 + (j & 7) * 16 + (r & 3) * 4;
-                    *reinterpret_cast<float *>(smem + kOffVraw + off) = r == j ? 1.0f : 0.0f;
+                    *reinterpret_cast<float *>(st + kTN * kRC * 4 + off) = r == j ? 1.0f : 0.0f;
                 }
             }
             __syncthreads();
         }
-        make_lo(smem + kOffCraw, smem + kOffClo, kTN * kRC * 4, tid);
-        make_lo(smem + kOffVraw, smem + kOffVlo, kPanel * kRC * 4, tid);
+        make_lo(st, smem + kOffLoC, kTN * kRC * 4, tid);
+        make_lo(st + kTN * kRC * 4, smem + kOffLoV, kPanel * kRC * 4, tid);
         tc::fence_proxy_async_smem();
         __syncthreads();
         if (tid == 0) {
             tc::fence_after_sync();
+            const uint32_t sC = sbase + sidx * kStageBytes, sV = sC + kTN * kRC * 4;
 #pragma unroll
             for (int s = 0; s < kRC / 8; ++s) {
                 const uint32_t ko = (uint32_t)s * 256;  // 8 rows = 2 cores along K
-                const uint64_t ah = tc::smem_desc(sbase + kOffCraw + ko, 128, kCQ * 128);
-                const uint64_t al = tc::smem_desc(sbase + kOffClo + ko, 128, kCQ * 128);
-                const uint64_t bh = tc::smem_desc(sbase + kOffVraw + ko, 128, kCQ * 128);
-                const uint64_t bl = tc::smem_desc(sbase + kOffVlo + ko, 128, kCQ * 128);
-                const uint32_t acc = (r0 > 0 || s > 0) ? 1u : 0u;
+                const uint64_t ah = tc::smem_desc(sC + ko, 128, kCQ * 128);
+                const uint64_t al = tc::smem_desc(sbase + kOffLoC + ko, 128, kCQ * 128);
+                const uint64_t bh = tc::smem_desc(sV + ko, 128, kCQ * 128);
+                const uint64_t bl = tc::smem_desc(sbase + kOffLoV + ko, 128, kCQ * 128);
+                const uint32_t acc = (i > 0 || s > 0) ? 1u : 0u;
                 tc::mma_tf32(tmem + kDA, al, bh, kIdescA, acc);
                 tc::mma_tf32(tmem + kDA, ah, bl, kIdescA, 1u);
                 tc::mma_tf32(tmem + kDA, ah, bh, kIdescA, 1u);
@@ -197,7 +213,15 @@ trailing_tc_kernel(float *__restrict__ H, const float *__restrict__ Sws, const f
         const bool done = tc::mbar_wait(bar, phase, kWaitLimit);
         phase ^= 1u;
         ok = !__syncthreads_or(!done);
+        // this chunk's stage and the lo buffers are free again: refill
+        const int nx = i + kStages;
+        if (nx < nchunks) {
+            copy_block<kTN>(Cbase, n, nx * kRC, m, nct, st, warp, lane);
+            copy_block<kPanel>(Vbase, n, nx * kRC, m, kPanel, st + kTN * kRC * 4, warp, lane);
+        }
+        tc::cp_async_commit();
     }
+    tc::cp_async_wait_all();
 
     // ---- phase B: Y = T^T W, thread = tile column c ------------------------
     if (ok) {
@@ -210,12 +234,13 @@ trailing_tc_kernel(float *__restrict__ H, const float *__restrict__ Sws, const f
         //   y_c = tau_c (w_c - sum_{l < c} S(l, c) y_l)
         float y[32];
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-            float a = w[c];
+        for (int cc = 0; cc < 32; ++cc) {
+            float a = w[cc];
 #pragma unroll
-            for (int l = 0; l < c; ++l) a = fmaf(-Ts[c * 32 + l], y[l], a);
-            y[c] = taus[c] * a;
+            for (int l = 0; l < cc; ++l) a = fmaf(-Ts[cc * 32 + l], y[l], a);
+            y[cc] = taus[cc] * a;
         }
+        __syncthreads();  // every thread is done with the phase-A buffers
         // Y as the K-major B operand of phase C: core (c/8, j/4) at
         // ((c/8) * 8 + j/4) * 128 bytes, column c%8 at +16 * (c%8)
 #pragma unroll
@@ -250,33 +275,39 @@ trailing_tc_kernel(float *__restrict__ H, const float *__restrict__ Sws, const f
             }
             tc::mma_commit(bar);
         }
+        // epilogue: thread = row r0 + 32 warp + lane.  The first 16 columns of
+        // C are loaded while the MMA runs; each later group is loaded before
+        // the previous one is stored.
+        const int r = r0 + 32 * warp + lane;
+        float *Crow = Hm + (int64_t)c0 * n + k + r;
+        const bool rv = r < m;
+        float cv[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) cv[i] = (rv && i < nct) ? Crow[(int64_t)i * n] : 0.0f;
         const bool done = tc::mbar_wait(bar, phase, kWaitLimit);
         phase ^= 1u;
         ok = !__syncthreads_or(!done);
         if (!ok) break;
         tc::fence_after_sync();
-        // epilogue: thread = row r0 + 32 warp + lane, 128 columns from TMEM;
-        // all loads of a 32-column group are issued before any store
-        const int r = r0 + 32 * warp + lane;
-        float *Crow = Hm + (int64_t)c0 * n + k + r;
 #pragma unroll 1
-        for (int cc = 0; cc < kTN / 32; ++cc) {
-            float p[32];
-            tc::tmem_ld_32x32(tmem + ((uint32_t)(32 * warp) << 16) + kDC + 32 * cc, p);
+        for (int cg16 = 0; cg16 < kTN / 16; ++cg16) {
+            float pv[16];
+            tc::tmem_ld_32x16(tmem + ((uint32_t)(32 * warp) << 16) + kDC + 16 * cg16, pv);
             tc::tmem_ld_wait();
-            if (r < m && 32 * cc < nct) {
-                float cv[32];
+            float nxt[16];
+            const int nb = 16 * (cg16 + 1);
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const int c = 32 * cc + i;
-                    cv[i] = c < nct ? Crow[(int64_t)c * n] : 0.0f;
-                }
+            for (int i = 0; i < 16; ++i)
+                nxt[i] = (rv && cg16 + 1 < kTN / 16 && nb + i < nct) ? Crow[(int64_t)(nb + i) * n] : 0.0f;
+            if (rv) {
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const int c = 32 * cc + i;
-                    if (c < nct) Crow[(int64_t)c * n] = cv[i] - p[i];
+                for (int i = 0; i < 16; ++i) {
+                    const int c = 16 * cg16 + i;
+                    if (c < nct) Crow[(int64_t)c * n] = cv[i] - pv[i];
                 }
             }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) cv[i] = nxt[i];
         }
         tc::fence_before_sync();
         __syncthreads();
