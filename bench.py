@@ -367,22 +367,20 @@ def _traffic_from_profiles(cfg_name):
 
 
 def end_to_end(a, n, batch, dev, steps) -> dict:
-    """Same call through the public API with pinned host buffers: H2D of A,
-    geqrf, D2H of H and tau, all inside the events."""
+    """The host-buffer entry point of the public API (fastqr.geqrf_host ->
+    fqr_geqrf_f32_host) on page-locked host buffers: every step uploads A,
+    factors it and downloads H and tau (chunked, the copies overlapping the
+    kernels), all inside the events."""
     import fastqr
 
     stream = torch.cuda.current_stream(dev)
     a_host = a.cpu().pin_memory()
-    # host outputs share the device layout, so each D2H is one flat copy
     h_host = torch.empty_strided((batch, n, n), (n * n, 1, n), dtype=torch.float32, pin_memory=True)
     t_host = torch.empty((batch, n), dtype=torch.float32, pin_memory=True)
-    a_dev = torch.empty_like(a)
+    ws = torch.empty(max(fastqr.host_workspace_bytes(batch, n), 1), dtype=torch.uint8, device=dev)
 
     def one():
-        a_dev.copy_(a_host, non_blocking=True)
-        hh, tt = fastqr.geqrf(a_dev)
-        h_host.copy_(hh, non_blocking=True)
-        t_host.copy_(tt, non_blocking=True)
+        fastqr.geqrf_host(a_host, out=(h_host, t_host), workspace=ws, device=dev, synchronize=False)
 
     for _ in range(2):
         one()

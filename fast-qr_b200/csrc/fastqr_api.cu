@@ -132,9 +132,11 @@ struct StageTimer {
     }
 };
 
+// status_word: where the tensor-core kernels record a bounded wait that gave
+// up (NULL: the word after the T factors in the workspace).
 int run_geqrf(const float *A, int64_t batch, int64_t n, int64_t a_bstride, int64_t a_rstride,
               int64_t a_cstride, float *H, float *tau, void *workspace, size_t workspace_bytes,
-              cudaStream_t st, StageTimer *tm)
+              cudaStream_t st, StageTimer *tm, int *status_word = nullptr)
 {
     if (batch < 0 || n < 0) return FQR_EINVAL;
     if (batch == 0 || n == 0) return FQR_OK;
@@ -155,7 +157,8 @@ int run_geqrf(const float *A, int64_t batch, int64_t n, int64_t a_bstride, int64
     if (!workspace || workspace_bytes < need) return FQR_EWORKSPACE;
     if (((uintptr_t)workspace) % kWsAlign) return FQR_EINVAL;
     float *Tws = (float *)workspace;
-    int *status = (int *)((unsigned char *)workspace + fqr::ws_t_bytes(batch));
+    int *status = status_word ? status_word
+                              : (int *)((unsigned char *)workspace + fqr::ws_t_bytes(batch));
     const bool tc = use_tc(n) && ((uintptr_t)H % 16) == 0;
 
     if (tm) tm->begin(FQR_STAGE_COPY_IN);
@@ -186,6 +189,15 @@ int fqr::geqrf_enqueue(const float *A, int64_t batch, int64_t n, int64_t a_bstri
 {
     return run_geqrf(A, batch, n, a_bstride, a_rstride, a_cstride, H, tau, workspace,
                      workspace_bytes, st, nullptr);
+}
+
+int fqr::geqrf_enqueue_status(const float *A, int64_t batch, int64_t n, int64_t a_bstride,
+                              int64_t a_rstride, int64_t a_cstride, float *H, float *tau,
+                              void *workspace, size_t workspace_bytes, int *status_word,
+                              cudaStream_t st)
+{
+    return run_geqrf(A, batch, n, a_bstride, a_rstride, a_cstride, H, tau, workspace,
+                     workspace_bytes, st, nullptr, status_word);
 }
 
 extern "C" {

@@ -43,6 +43,12 @@ constexpr size_t ws_total_bytes(int64_t batch) { return ws_t_bytes(batch) + kWsA
 int geqrf_enqueue(const float *A, int64_t batch, int64_t n, int64_t a_bstride, int64_t a_rstride,
                   int64_t a_cstride, float *H, float *tau, void *workspace, size_t workspace_bytes,
                   cudaStream_t st);
+// The same with the bounded-wait status word at `status_word` instead of
+// inside the workspace (the first kernel of the call clears it).
+int geqrf_enqueue_status(const float *A, int64_t batch, int64_t n, int64_t a_bstride,
+                         int64_t a_rstride, int64_t a_cstride, float *H, float *tau,
+                         void *workspace, size_t workspace_bytes, int *status_word,
+                         cudaStream_t st);
 
 // Panel plan for m remaining rows: threads per CTA and cluster size.
 struct PanelShape {

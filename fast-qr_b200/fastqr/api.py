@@ -101,6 +101,83 @@ def geqrf(a: torch.Tensor, *, out: tuple[torch.Tensor, torch.Tensor] | None = No
     return h, tau
 
 
+def host_workspace_bytes(batch: int, n: int) -> int:
+    return int(load().fqr_host_workspace_bytes(batch, n))
+
+
+def geqrf_host(a: torch.Tensor, *, out: tuple[torch.Tensor, torch.Tensor] | None = None,
+               workspace: torch.Tensor | None = None, device=None,
+               synchronize: bool = True) -> tuple[torch.Tensor, torch.Tensor]:
+    """Batched QR of a HOST float32 batch ``[batch, n, n]`` on a CUDA device.
+
+    The result ``(H, tau)`` lands in host tensors with torch.geqrf's layout
+    (page-locked when allocated here).  Chunks of the batch are uploaded,
+    factored and downloaded on overlapping streams (``fqr_geqrf_f32_host``).
+    ``a`` must hold each matrix as one dense row- or column-major block; pin it
+    (``a.pin_memory()``) for the copies to overlap.  ``workspace`` is a uint8
+    tensor on ``device`` of at least ``host_workspace_bytes(batch, n)`` bytes.
+    With ``synchronize=False`` the call returns once the work is enqueued on
+    the device's current stream; the outputs are valid after that stream has
+    passed it.
+    """
+    if not isinstance(a, torch.Tensor):
+        raise TypeError("input must be a torch.Tensor")
+    if a.device.type != "cpu":
+        raise ValueError("geqrf_host takes a host (CPU) tensor; use geqrf for CUDA tensors")
+    if a.dtype != torch.float32:
+        raise ValueError(f"input dtype must be torch.float32, got {a.dtype}")
+    squeeze = a.ndim == 2
+    if squeeze:
+        a = a.unsqueeze(0)
+    if a.ndim != 3 or a.shape[-1] != a.shape[-2]:
+        raise ValueError(f"input must have shape (batch, n, n), got {tuple(a.shape)}")
+    batch, n, _ = a.shape
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    lib = load()
+    if out is None:
+        h = torch.empty_strided((batch, n, n), (n * n, 1, n), dtype=torch.float32, pin_memory=True)
+        tau = torch.empty((batch, n), dtype=torch.float32, pin_memory=True)
+    else:
+        h, tau = out
+        if h.device.type != "cpu" or tau.device.type != "cpu":
+            raise ValueError("geqrf_host outputs must be host tensors")
+        if h.shape != (batch, n, n) or h.stride() != (n * n, 1, n) or h.dtype != torch.float32:
+            raise ValueError("out H must be float32 (batch, n, n) with strides (n*n, 1, n)")
+        if tau.shape != (batch, n) or not tau.is_contiguous() or tau.dtype != torch.float32:
+            raise ValueError("out tau must be contiguous float32 (batch, n)")
+    need = int(lib.fqr_host_workspace_bytes(batch, n))
+    if need:
+        if workspace is None:
+            workspace = torch.empty(need, dtype=torch.uint8, device=dev)
+        elif workspace.numel() * workspace.element_size() < need or workspace.device != dev:
+            raise ValueError(f"workspace needs {need} bytes on {dev}")
+        ws_ptr, ws_len = workspace.data_ptr(), workspace.numel() * workspace.element_size()
+    else:
+        ws_ptr, ws_len = None, 0
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev)
+        bs, rs, cs = a.stride()
+        rc = lib.fqr_geqrf_f32_host(a.data_ptr(), batch, n, bs, rs, cs, h.data_ptr(),
+                                    tau.data_ptr(), ws_ptr, ws_len, stream.cuda_stream)
+        if rc:
+            raise FastQRError(rc, "fqr_geqrf_f32_host")
+        if synchronize:
+            stream.synchronize()
+    if squeeze:
+        return h[0], tau[0]
+    return h, tau
+
+
+def host_check_status(workspace: torch.Tensor, batch: int, n: int) -> None:
+    """Blocks on the current stream and raises if a chunk of the last
+    geqrf_host that used ``workspace`` recorded a device-side wait that gave up."""
+    stream = torch.cuda.current_stream(workspace.device).cuda_stream
+    rc = load().fqr_host_check_status(workspace.data_ptr(),
+                                      workspace.numel() * workspace.element_size(), batch, n, stream)
+    if rc:
+        raise FastQRError(rc, "fqr_host_check_status")
+
+
 def check_status(workspace: torch.Tensor, batch: int) -> None:
     """Blocks on the current stream and raises if the last geqrf that used
     ``workspace`` recorded a device-side wait that gave up."""

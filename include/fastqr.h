@@ -112,6 +112,35 @@ int fqr_geqrf_f32_noalloc(const float *A, int64_t batch, int64_t n, int64_t a_bs
                           void *stream);
 
 /*
+ * Batched QR of matrices in HOST memory: the same result as fqr_geqrf_f32,
+ * with A, H and tau host pointers (page-locked memory, from cudaHostAlloc or
+ * cudaHostRegister, lets the copies overlap; pageable memory works, slower).
+ * The batch is cut into chunks that are uploaded, factored and downloaded on
+ * internal streams with separate device staging, so that copies in both
+ * directions overlap the kernels.  Asynchronous on `stream` like
+ * fqr_geqrf_f32: H and tau are complete, and A may be reused, once `stream`
+ * has passed the call.
+ * A: each matrix one dense n x n block, row-major (a_rstride = n,
+ *    a_cstride = 1) or column-major (1, n); a_bstride >= n*n elements.
+ * H, tau: host, layouts as for fqr_geqrf_f32.
+ * workspace: DEVICE scratch of fqr_host_workspace_bytes(batch, n) bytes,
+ *    256-byte aligned (staging for the chunks in flight).
+ * Creates a few streams and events per device on its first call there.
+ * The reference's entry point takes device tensors only
+ * (submissions/candidate.py:8383-8415, official/eval.py:125-132); this is the
+ * form a host-resident caller (a CPU library's ctypes/JNI binding) uses
+ * instead of copying the batch itself around the device call.
+ */
+size_t fqr_host_workspace_bytes(int64_t batch, int64_t n);
+int fqr_geqrf_f32_host(const float *A, int64_t batch, int64_t n, int64_t a_bstride,
+                       int64_t a_rstride, int64_t a_cstride, float *H, float *tau,
+                       void *workspace, size_t workspace_bytes, void *stream);
+/* fqr_check_status for fqr_geqrf_f32_host: synchronizes `stream`, then
+ * returns FQR_ETIMEOUT if any chunk's bounded device-side wait gave up. */
+int fqr_host_check_status(const void *workspace, size_t workspace_bytes, int64_t batch, int64_t n,
+                          void *stream);
+
+/*
  * Synchronizes `stream`, then reports whether the last fqr_geqrf_f32 that
  * used `workspace` (for `batch` matrices) hit a bounded device-side wait that
  * gave up: FQR_OK or FQR_ETIMEOUT.  The tensor-core kernels never spin

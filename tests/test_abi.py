@@ -73,3 +73,42 @@ def test_python_api_rejects_cpu_tensors():
     import torch
     with pytest.raises(ValueError):
         fastqr.geqrf(torch.zeros(2, 8, 8))
+
+
+def test_host_entry_validation_without_gpu():
+    lib = fastqr.load()
+    dummy = ctypes.c_void_p(16)
+    # empty problems are a no-op; negative sizes and null pointers are rejected
+    assert lib.fqr_geqrf_f32_host(None, 0, 8, 64, 8, 1, None, None, None, 0, None) == 0
+    assert lib.fqr_geqrf_f32_host(None, -1, 8, 64, 8, 1, None, None, None, 0, None) == 1
+    assert lib.fqr_geqrf_f32_host(None, 2, 8, 64, 8, 1, None, None, None, 0, None) == 1
+    assert lib.fqr_geqrf_f32_host(dummy, 1, 8193, 1, 1, 1, dummy, dummy, None, 0, None) == 2
+    # each host matrix must be a dense row- or column-major block
+    assert lib.fqr_geqrf_f32_host(dummy, 2, 8, 64, 16, 1, dummy, dummy, None, 0, None) == 1
+    assert lib.fqr_geqrf_f32_host(dummy, 2, 8, 32, 8, 1, dummy, dummy, None, 0, None) == 1
+    # no (or too little) device workspace
+    assert lib.fqr_geqrf_f32_host(dummy, 2, 8, 64, 8, 1, dummy, dummy, None, 0, None) == 5
+    need = lib.fqr_host_workspace_bytes(2, 8)
+    assert lib.fqr_geqrf_f32_host(dummy, 2, 8, 64, 8, 1, dummy, dummy, dummy, need - 1, None) == 5
+
+
+def test_host_workspace_plan():
+    # staging for at most 4 chunks in flight, each chunk >= 1 MiB of input or
+    # 1/8 of the batch; sizes depend on (batch, n) only
+    for batch, n in [(1024, 32), (256, 256), (512, 512), (64, 1024), (16, 4096), (1, 8), (3, 100)]:
+        mat = n * n * 4
+        need = fastqr.host_workspace_bytes(batch, n)
+        assert need % 256 == 0
+        assert need >= 2 * mat  # at least one A and one H staging block
+        # never more staging than four slots of the whole batch
+        assert need <= 4 * (batch * (2 * mat + n * 4) + fastqr.workspace_bytes(batch, n) + 1024)
+    # C2: 8 chunks of 32 matrices, 4 slots of (A + H + tau + T factors)
+    slot = 2 * 32 * 256 * 256 * 4 + 32 * 256 * 4 + fastqr.workspace_bytes(32, 256)
+    assert fastqr.host_workspace_bytes(256, 256) == 256 + 4 * slot
+    assert fastqr.host_workspace_bytes(0, 8) == 0
+
+
+def test_host_api_rejects_cuda_tensors_and_bad_dtypes():
+    import torch
+    with pytest.raises(ValueError):
+        fastqr.geqrf_host(torch.zeros(2, 8, 8, dtype=torch.float64))
