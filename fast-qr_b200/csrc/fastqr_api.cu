@@ -160,6 +160,8 @@ int run_geqrf(const float *A, int64_t batch, int64_t n, int64_t a_bstride, int64
     int *status = status_word ? status_word
                               : (int *)((unsigned char *)workspace + fqr::ws_t_bytes(batch));
     const bool tc = use_tc(n) && ((uintptr_t)H % 16) == 0;
+    fqr::TrailingMaps maps;
+    if (tc && fqr::prepare_trailing_tc(H, batch, ni, &maps) != cudaSuccess) return FQR_ECUDA;
 
     if (tm) tm->begin(FQR_STAGE_COPY_IN);
     e = fqr::launch_copy_in(A, batch, ni, a_bstride, a_rstride, a_cstride, H, status, st);
@@ -172,7 +174,7 @@ int run_geqrf(const float *A, int64_t batch, int64_t n, int64_t a_bstride, int64
         if (e != cudaSuccess) return status_from(e);
         if (k + fqr::kPanel < ni) {
             if (tm) tm->begin(FQR_STAGE_TRAILING);
-            e = tc ? fqr::launch_trailing_tc(H, Tws, tau, status, batch, ni, k, st)
+            e = tc ? fqr::launch_trailing_tc(maps, H, Tws, tau, status, batch, ni, k, st)
                    : fqr::launch_trailing(H, Tws, tau, batch, ni, k, st);
             if (tm) tm->end();
             if (e != cudaSuccess) return status_from(e);

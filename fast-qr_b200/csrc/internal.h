@@ -1,6 +1,7 @@
 // Host-side launchers shared between the fastqr translation units.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -24,9 +25,16 @@ cudaError_t launch_trailing(float *H, const float *Sws, const float *tau, int64_
 
 // Tensor-core (tcgen05, 3xTF32) trailing update; needs n % 4 == 0, n >= 128
 // and a 16-byte aligned H.  Sets *status to nonzero if a bounded wait gave up.
+// Its phase-A operands arrive by TMA through two tensor maps of H, encoded
+// once per call by prepare_trailing_tc (they depend on H, n and batch only).
 bool trailing_tc_supported(int n);
-cudaError_t launch_trailing_tc(float *H, const float *Sws, const float *tau, int *status, int64_t batch,
-                               int n, int k, cudaStream_t st);
+struct TrailingMaps {
+    CUtensorMap c;  // 32 rows x 128 trailing columns, 128-byte swizzle
+    CUtensorMap v;  // 32 rows x 32 panel columns, 128-byte swizzle
+};
+cudaError_t prepare_trailing_tc(float *H, int64_t batch, int n, TrailingMaps *maps);
+cudaError_t launch_trailing_tc(const TrailingMaps &maps, float *H, const float *Sws, const float *tau,
+                               int *status, int64_t batch, int n, int k, cudaStream_t st);
 
 // Workspace layout: one 32 x 32 float block per matrix holding the panel's
 // S = V^T V (strictly upper; the compact-WY T factor is T = D (I + S D)^-1,

@@ -8,21 +8,27 @@
 // One CTA (4 warps, two CTAs per SM) owns a tile of kTN = 128 trailing
 // columns of one matrix:
 //   phase A  W^T[c][j] = sum_r C(r, c) V(r, j)    tcgen05.mma M=128 (c) N=32 (j),
-//            K = rows, accumulated over 32-row chunks into TMEM; the chunks
-//            stream in by cp.async through a 3-stage ring (two in flight
-//            while one is split and multiplied)
+//            K = rows, accumulated over 32-row chunks into TMEM.  Thread 0
+//            streams the chunks by TMA (tensor maps over H, 128-byte
+//            swizzle: each column's 32 rows are one 128-byte operand row)
+//            through a 3-stage ring; all threads split chunk i into its lo
+//            buffer (two, alternating) while the MMAs of chunk i-1 run.
 //   phase B  Y = T^T W                            per thread (one column c), by
 //            forward substitution with S = V^T V (strict upper) and tau:
 //            T = D (I + S D)^-1, so (I + D S^T) Y = D W
 //   phase C  P[r][c] = sum_j V(r, j) Y(j, c)      tcgen05.mma M=128 (r) N=128 (c)
 //            K = 32 per 128-row chunk; epilogue C(r, c) -= P from TMEM
-// Operands sit in shared memory in the no-swizzle K-major "core matrix"
-// layout (a core holds 8 rows of the M/N dimension x 4 consecutive K
-// elements, 16 bytes per row).  The raw fp32 data is the hi operand (the
-// tensor core truncates it to TF32); threads write lo = x - trunc_tf32(x) into
-// a second buffer.
+// The raw fp32 data is the hi operand (the tensor core truncates it to TF32);
+// threads write lo = x - trunc_tf32(x) into a second buffer of the same
+// layout.  Phase C's V and Y operands are staged by threads in the
+// no-swizzle K-major "core matrix" layout (8 rows of the M/N dimension x 4
+// consecutive K elements, 16 bytes per row).
 // The reference's trailing_update_kernel (submissions/candidate.py:2507-2716)
 // is SIMT FP32 with T recomputed in every CTA; nothing here follows it.
+#include <mutex>
+
+#include <cudaTypedefs.h>
+
 #include "common.cuh"
 #include "internal.h"
 #include "tc.cuh"
@@ -32,8 +38,8 @@ namespace fqr {
 namespace {
 
 constexpr int kTN = 128;          // trailing columns per CTA
-constexpr int kRC = 32;           // rows per phase-A chunk (MMA K)
-constexpr int kStages = 3;        // phase-A chunks in flight
+constexpr int kRC = 32;           // rows per phase-A chunk (MMA K; one 128-byte swizzle row)
+constexpr int kStages = 3;        // phase-A ring of raw chunks
 constexpr int kRCC = 128;         // rows per phase-C chunk (MMA M)
 constexpr int kThreads = 128;
 constexpr uint32_t kTmemCols = 256;
@@ -41,17 +47,18 @@ constexpr uint32_t kDA = 0;       // TMEM column of W^T (32 columns)
 constexpr uint32_t kDC = 128;     // TMEM column of P (128 columns)
 constexpr uint64_t kWaitLimit = 1000000000ull;  // 1 s of wall time per wait
 
-// shared memory map (bytes).  Phase A: a ring of kStages chunks, each C^T
-// (128 c x 32 r) and V (32 j x 32 r) as raw fp32 -- the hi operand -- plus
-// one lo = x - trunc_tf32(x) buffer; K-major cores of 8 rows x 4 K.
-constexpr int kCQ = kRC / 4;                    // cores along K in a row of cores
-constexpr int kStageBytes = (kTN + kPanel) * kRC * 4;  // 20 KB
-constexpr int kOffLoC = kStages * kStageBytes;  // 60 KB
-constexpr int kOffLoV = kOffLoC + kTN * kRC * 4;
-constexpr int kOffT = kOffLoV + kPanel * kRC * 4;   // S, column-major 32 x 32 (4 KB)
-constexpr int kOffTau = kOffT + 4096;               // tau of the panel (128 B)
-constexpr int kOffBar = kOffTau + 128;              // mbarrier (8 B) + TMEM base address (4 B)
-constexpr int kSmem = kOffBar + 64;                 // ~86 KB: 2 CTAs per SM
+// shared memory map (bytes, from a 1024-byte aligned base).  Phase A: a ring
+// of kStages chunks, each C^T (128 c x 32 r, 16 KB) then V (32 j x 32 r,
+// 4 KB) as raw fp32 in the 128-byte swizzle layout, and two lo buffers of the
+// same shape.
+constexpr int kCBytes = kTN * kRC * 4;                   // 16 KB
+constexpr int kStageBytes = kCBytes + kPanel * kRC * 4;  // 20 KB
+constexpr int kOffLo = kStages * kStageBytes;            // 60 KB
+constexpr int kOffT = kOffLo + 2 * kStageBytes;          // 100 KB: S, column-major 32 x 32 (4 KB)
+constexpr int kOffTau = kOffT + 4096;                    // tau of the panel (128 B)
+constexpr int kOffBar = kOffTau + 128;  // mbarriers: full[3], mma[2], phase C; TMEM address
+constexpr int kSmemUsed = kOffBar + 64;
+constexpr int kSmem = kSmemUsed + 1024;                  // + alignment slack: ~105 KB, 2 CTAs per SM
 // Phase C (reuses the phase-A area): V chunk as the K-major A operand
 // (128 r x 32 j) and Y as the K-major B operand (128 c x 32 j), raw + lo.
 constexpr int kOffVCraw = 0;
@@ -59,40 +66,32 @@ constexpr int kOffVClo = 16384;
 constexpr int kOffYraw = 32768;
 constexpr int kOffYlo = 49152;
 static_assert(kOffYlo + 16384 <= kOffT, "phase-C buffers overlap S");
+static_assert(kStageBytes % 1024 == 0 && kCBytes % 1024 == 0, "swizzle atoms need 1024-byte alignment");
 
 constexpr uint32_t kIdescA = tc::idesc_tf32(128, 32, 0, 0);   // A = C^T (M = c), B = V (N = j)
 constexpr uint32_t kIdescC = tc::idesc_tf32(128, 128, 0, 0);  // A = V (M = r), B = Y (N = c)
 
-// cp.async a [NO columns] x [kRC rows] block of a column-major matrix
-// (column o at base + o * ld, panel rows r0 ..) into the K-major core layout:
-// core (o/8, r/4) at ((o/8) * kCQ + r/4) * 128 bytes, column o%8 at
-// +16 * (o%8).  A warp step copies 8 columns x 4 row quads (64 contiguous
-// bytes per column; 512 contiguous bytes of shared memory).  Rows >= rows
-// and columns >= cols are zero-filled.
-template <int NO>
-__device__ __forceinline__ void copy_block(const float *base, int64_t ld, int r0, int rows, int cols,
-                                           unsigned char *dst, int warp, int lane)
+// lo = x - trunc_tf32(x) over one stage (C then V, elementwise: the layout
+// does not matter).  For the first chunk the V part is also made unit lower
+// triangular in place (panel rows r < j hold R, row j holds beta).
+__device__ __forceinline__ void split_stage(unsigned char *raw, unsigned char *lo, bool first, int tid)
 {
-    constexpr int ITER = (NO / 8) * (kCQ / 4);
-    const int oc = lane & 7, qi = lane >> 3;
+#pragma unroll 2
+    for (int off = tid * 16; off < kStageBytes; off += kThreads * 16) {
+        float4 v = *reinterpret_cast<const float4 *>(raw + off);
+        if (first && off >= kCBytes) {
+            // V row j (= operand row) at (off - kCBytes) / 128; its 16-byte
+            // chunk holds panel rows 4 * ((chunk ^ j) & 7) .. + 3
+            const int vo = off - kCBytes;
+            const int j = vo >> 7;
+            const int r0 = 4 * ((((vo >> 4) & 7) ^ j) & 7);
+            float e[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-    for (int it = warp; it < ITER; it += 4) {
-        const int og = it / (kCQ / 4), qg = it % (kCQ / 4);
-        const int o = og * 8 + oc;
-        const int rq = qg * 4 + qi;  // row quad in the chunk
-        const int r = r0 + 4 * rq;
-        const bool valid = o < cols && r < rows;
-        const float *src = valid ? base + (int64_t)o * ld + r : base;
-        tc::cp_async16(dst + (og * kCQ + rq) * 128 + oc * 16, src, valid ? 16u : 0u);
-    }
-}
-
-// lo = x - trunc_tf32(x) over `bytes` of shared memory, elementwise
-__device__ __forceinline__ void make_lo(const unsigned char *raw, unsigned char *lo, int bytes, int tid)
-{
-#pragma unroll 4
-    for (int off = tid * 16; off < bytes; off += kThreads * 16) {
-        const float4 v = *reinterpret_cast<const float4 *>(raw + off);
+            for (int q = 0; q < 4; ++q)
+                if (r0 + q <= j) e[q] = (r0 + q == j) ? 1.0f : 0.0f;
+            v = make_float4(e[0], e[1], e[2], e[3]);
+            *reinterpret_cast<float4 *>(raw + off) = v;
+        }
         *reinterpret_cast<float4 *>(lo + off) =
             make_float4(tc::tf32_lo(v.x), tc::tf32_lo(v.y), tc::tf32_lo(v.z), tc::tf32_lo(v.w));
     }
@@ -123,105 +122,117 @@ __device__ __forceinline__ void stage_v_kmajor(const float *Vbase, int64_t ld, i
 }  // namespace
 
 __global__ void __launch_bounds__(kThreads, 2)
-trailing_tc_kernel(float *__restrict__ H, const float *__restrict__ Sws, const float *__restrict__ tau,
-                   int *__restrict__ status, int n, int k)
+trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmV,
+                   float *__restrict__ H, const float *__restrict__ Sws, const float *__restrict__ tau,
+                   int *__restrict__ status, int n, int k, int64_t b0)
 {
-    extern __shared__ __align__(1024) unsigned char smem[];
+    extern __shared__ unsigned char smem_raw[];
+    const uint32_t raw_addr = tc::smem_addr(smem_raw);
+    unsigned char *smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int64_t mat = blockIdx.y;
+    const int64_t mat = b0 + blockIdx.y;
     const int c0 = k + kPanel + blockIdx.x * kTN;  // first trailing column of the tile
     const int nct = min(kTN, n - c0);
     const int m = n - k;
     float *Hm = H + mat * (int64_t)n * n;
-    const float *Cbase = Hm + (int64_t)c0 * n + k;  // C(r, c) at Cbase[c * n + r]
     const float *Vbase = Hm + (int64_t)k * n + k;   // V(r, j) at Vbase[j * n + r]
 
-    uint64_t *bar = reinterpret_cast<uint64_t *>(smem + kOffBar);
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kOffBar + 8);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kOffBar);  // [kStages]
+    uint64_t *mmab = full + kStages;                                // [2]
+    uint64_t *cbar = full + kStages + 2;                            // phase C
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kOffBar + 48);
     float *Ts = reinterpret_cast<float *>(smem + kOffT);    // S(l, c) at c * 32 + l
     float *taus = reinterpret_cast<float *>(smem + kOffTau);
-
-    // phase-A prologue: the first kStages chunks start streaming at once
+    const uint32_t sbase = tc::smem_addr(smem);
     const int nchunks = (m + kRC - 1) / kRC;
-#pragma unroll
-    for (int s = 0; s < kStages; ++s) {
-        if (s < nchunks) {
-            unsigned char *st = smem + s * kStageBytes;
-            copy_block<kTN>(Cbase, n, s * kRC, m, nct, st, warp, lane);
-            copy_block<kPanel>(Vbase, n, s * kRC, m, kPanel, st + kTN * kRC * 4, warp, lane);
-        }
-        tc::cp_async_commit();
-    }
 
+    // thread 0: barriers, then the first kStages chunks (and S with chunk 0)
+    // start streaming at once
+    if (tid == 0) {
+        tc::prefetch_tensormap(&tmC);
+        tc::prefetch_tensormap(&tmV);
+        for (int i = 0; i < kStages + 3; ++i) tc::mbar_init(&full[i], 1);
+        tc::fence_mbar_init();
+        for (int s = 0; s < kStages && s < nchunks; ++s) {
+            unsigned char *st = smem + s * kStageBytes;
+            tc::mbar_expect_tx(&full[s], kStageBytes + (s == 0 ? 4096u : 0u));
+            tc::tma_load_3d(st, &tmC, k + s * kRC, c0, (int)mat, &full[s]);
+            tc::tma_load_3d(st + kCBytes, &tmV, k + s * kRC, k, (int)mat, &full[s]);
+            if (s == 0) tc::bulk_load(smem + kOffT, Sws + mat * (kPanel * kPanel), 4096u, &full[0]);
+        }
+    }
+    float tau_r = 0.0f;
+    if (tid < kPanel) tau_r = tau[mat * n + k + tid];  // stored to shared memory after phase A
     if (warp == 0) {
         tc::tmem_alloc(tmem_slot, kTmemCols);
         tc::tmem_relinquish();
     }
-    if (tid == 0) {
-        tc::mbar_init(bar, 1);
-        tc::fence_mbar_init();
-    }
-    const float *Sm = Sws + mat * (kPanel * kPanel);
-    for (int i = tid; i < kPanel * kPanel; i += kThreads) Ts[i] = Sm[i];
-    if (tid < kPanel) taus[tid] = tau[mat * n + k + tid];
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
     const uint32_t tmem = *tmem_slot;
-    uint32_t phase = 0;
-    bool ok = true;
-    const uint32_t sbase = tc::smem_addr(smem);
+    // copies and MMA groups issued / waited for per barrier (the same in
+    // every thread; thread 0 uses them to drain after a timeout)
+    int loads = kStages < nchunks ? kStages : nchunks;  // chunks whose TMA was issued
+    uint32_t mma_issued[2] = {0, 0}, mma_waited[2] = {0, 0};
+    bool ok = true, bad = false;  // bad: this thread saw an MMA wait give up
 
-    // ---- phase A: W^T = C^T V over all rows, kStages chunks in flight -----
-    for (int i = 0; i < nchunks && ok; ++i) {
-        const int sidx = i % kStages;
+    // ---- phase A: W^T = C^T V over all rows --------------------------------
+    // Every exit from the loop is uniform: it happens only at the CTA-wide
+    // __syncthreads_or, which also folds in an MMA wait that gave up in the
+    // previous iteration.
+    for (int i = 0; i < nchunks; ++i) {
+        const int sidx = i % kStages, b = i & 1;
         unsigned char *st = smem + sidx * kStageBytes;
-        tc::cp_async_wait_pending<kStages - 1>();  // chunk i has landed
-        __syncthreads();
-        if (i == 0) {
-            // V is unit lower triangular: panel rows r < j are 0, row j is 1
-            for (int e = tid; e < kPanel * kPanel; e += kThreads) {
-                const int j = e >> 5, r = e & 31;
-                if (r <= j) {
-                    const int off = ((j >> 3) * kCQ + (r >> 2)) * 128 + (j & 7) * 16 + (r & 3) * 4;
-                    *reinterpret_cast<float *>(st + kTN * kRC * 4 + off) = r == j ? 1.0f : 0.0f;
-                }
-            }
-            __syncthreads();
-        }
-        make_lo(st, smem + kOffLoC, kTN * kRC * 4, tid);
-        make_lo(st + kTN * kRC * 4, smem + kOffLoV, kPanel * kRC * 4, tid);
+        const bool landed = tc::mbar_wait(&full[sidx], (uint32_t)(i / kStages) & 1u, kWaitLimit);
+        if (landed && !bad) split_stage(st, smem + kOffLo + b * kStageBytes, i == 0, tid);
         tc::fence_proxy_async_smem();
-        __syncthreads();
+        ok = !__syncthreads_or(!landed || bad);
+        if (!ok) break;
         if (tid == 0) {
             tc::fence_after_sync();
-            const uint32_t sC = sbase + sidx * kStageBytes, sV = sC + kTN * kRC * 4;
+            const uint32_t sC = sbase + sidx * kStageBytes, sV = sC + kCBytes;
+            const uint32_t lC = sbase + kOffLo + b * kStageBytes, lV = lC + kCBytes;
 #pragma unroll
             for (int s = 0; s < kRC / 8; ++s) {
-                const uint32_t ko = (uint32_t)s * 256;  // 8 rows = 2 cores along K
-                const uint64_t ah = tc::smem_desc(sC + ko, 128, kCQ * 128);
-                const uint64_t al = tc::smem_desc(sbase + kOffLoC + ko, 128, kCQ * 128);
-                const uint64_t bh = tc::smem_desc(sV + ko, 128, kCQ * 128);
-                const uint64_t bl = tc::smem_desc(sbase + kOffLoV + ko, 128, kCQ * 128);
+                const uint32_t ko = (uint32_t)s * 32;  // 8 K elements inside the swizzle atom
+                const uint64_t ah = tc::smem_desc_sw128(sC + ko), al = tc::smem_desc_sw128(lC + ko);
+                const uint64_t bh = tc::smem_desc_sw128(sV + ko), bl = tc::smem_desc_sw128(lV + ko);
                 const uint32_t acc = (i > 0 || s > 0) ? 1u : 0u;
                 tc::mma_tf32(tmem + kDA, al, bh, kIdescA, acc);
                 tc::mma_tf32(tmem + kDA, ah, bl, kIdescA, 1u);
                 tc::mma_tf32(tmem + kDA, ah, bh, kIdescA, 1u);
             }
-            tc::mma_commit(bar);
+            tc::mma_commit(&mmab[b]);
         }
-        const bool done = tc::mbar_wait(bar, phase, kWaitLimit);
-        phase ^= 1u;
-        ok = !__syncthreads_or(!done);
-        // this chunk's stage and the lo buffers are free again: refill
-        const int nx = i + kStages;
-        if (nx < nchunks) {
-            copy_block<kTN>(Cbase, n, nx * kRC, m, nct, st, warp, lane);
-            copy_block<kPanel>(Vbase, n, nx * kRC, m, kPanel, st + kTN * kRC * 4, warp, lane);
+        ++mma_issued[b];
+        if (i >= 1) {
+            // chunk i-1's MMAs: afterwards its ring stage and lo buffer are free
+            const int pb = b ^ 1;
+            const bool done = tc::mbar_wait(&mmab[pb], mma_waited[pb] & 1u, kWaitLimit);
+            if (done) ++mma_waited[pb];
+            const int nx = i - 1 + kStages;
+            if (!done) {
+                bad = true;  // made uniform by the next __syncthreads_or
+            } else if (tid == 0 && nx < nchunks) {
+                unsigned char *fr = smem + ((i - 1) % kStages) * kStageBytes;
+                uint64_t *fb = &full[(i - 1) % kStages];
+                tc::mbar_expect_tx(fb, kStageBytes);
+                tc::tma_load_3d(fr, &tmC, k + nx * kRC, c0, (int)mat, fb);
+                tc::tma_load_3d(fr + kCBytes, &tmV, k + nx * kRC, k, (int)mat, fb);
+            }
+            if (done && nx < nchunks) ++loads;
         }
-        tc::cp_async_commit();
     }
-    tc::cp_async_wait_all();
+    ok = !__syncthreads_or(!ok || bad);
+    if (ok) {
+        const int lb = (nchunks - 1) & 1;  // the last chunk's MMAs
+        const bool done = tc::mbar_wait(&mmab[lb], mma_waited[lb] & 1u, kWaitLimit);
+        if (done) ++mma_waited[lb];
+        ok = !__syncthreads_or(!done);
+    }
+    if (tid < kPanel) taus[tid] = tau_r;
+    __syncthreads();
 
     // ---- phase B: Y = T^T W, thread = tile column c ------------------------
     if (ok) {
@@ -255,6 +266,7 @@ trailing_tc_kernel(float *__restrict__ H, const float *__restrict__ Sws, const f
     }
 
     // ---- phase C: C -= V Y, 128 rows per chunk -----------------------------
+    uint32_t c_issued = 0, c_waited = 0;
     for (int r0 = 0; r0 < m && ok; r0 += kRCC) {
         stage_v_kmajor(Vbase, n, r0, m, smem + kOffVCraw, smem + kOffVClo, tid);
         tc::fence_proxy_async_smem();
@@ -273,8 +285,9 @@ trailing_tc_kernel(float *__restrict__ H, const float *__restrict__ Sws, const f
                 tc::mma_tf32(tmem + kDC, ah, bl, kIdescC, 1u);
                 tc::mma_tf32(tmem + kDC, ah, bh, kIdescC, 1u);
             }
-            tc::mma_commit(bar);
+            tc::mma_commit(cbar);
         }
+        ++c_issued;
         // epilogue: thread = row r0 + 32 warp + lane.  The first 16 columns of
         // C are loaded while the MMA runs; each later group is loaded before
         // the previous one is stored.
@@ -284,8 +297,8 @@ trailing_tc_kernel(float *__restrict__ H, const float *__restrict__ Sws, const f
         float cv[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) cv[i] = (rv && i < nct) ? Crow[(int64_t)i * n] : 0.0f;
-        const bool done = tc::mbar_wait(bar, phase, kWaitLimit);
-        phase ^= 1u;
+        const bool done = tc::mbar_wait(cbar, c_waited & 1u, kWaitLimit);
+        if (done) ++c_waited;
         ok = !__syncthreads_or(!done);
         if (!ok) break;
         tc::fence_after_sync();
@@ -315,9 +328,19 @@ trailing_tc_kernel(float *__restrict__ H, const float *__restrict__ Sws, const f
 
     if (!ok && tid == 0) {
         atomicOr(status, 1);
-        // let the MMA group that did not signal in time drain (bounded)
-        // before its tensor memory is released
-        tc::mbar_wait(bar, phase ^ 1u, kWaitLimit);
+        // let copies and MMA groups that did not signal in time drain
+        // (bounded) before the shared and tensor memory is released
+        for (int i = 0; i < loads; ++i) {
+            // full[s] completes once per chunk issued into stage s; waiting on
+            // the parity of the last one covers the earlier ones
+            if (i + kStages >= loads)
+                tc::mbar_wait(&full[i % kStages], (uint32_t)(i / kStages) & 1u, kWaitLimit);
+        }
+        for (int b = 0; b < 2; ++b)
+            while (mma_waited[b] < mma_issued[b])
+                if (!tc::mbar_wait(&mmab[b], mma_waited[b]++ & 1u, kWaitLimit)) break;
+        while (c_waited < c_issued)
+            if (!tc::mbar_wait(cbar, c_waited++ & 1u, kWaitLimit)) break;
     }
     __syncthreads();
     if (warp == 0) {
@@ -331,8 +354,46 @@ bool trailing_tc_supported(int n)
     return n % 4 == 0 && n >= 128;
 }
 
-cudaError_t launch_trailing_tc(float *H, const float *Sws, const float *tau, int *status, int64_t batch,
-                               int n, int k, cudaStream_t st)
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder()
+{
+    static std::once_flag once;
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+        else
+            cudaGetLastError();
+    });
+    return fn;
+}
+
+}  // namespace
+
+cudaError_t prepare_trailing_tc(float *H, int64_t batch, int n, TrailingMaps *maps)
+{
+    PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+    if (!enc) return cudaErrorNotSupported;
+    // H as a 3-D tensor: x = row (contiguous), y = column, z = matrix
+    const cuuint64_t dims[3] = {(cuuint64_t)n, (cuuint64_t)n, (cuuint64_t)batch};
+    const cuuint64_t strides[2] = {(cuuint64_t)n * 4, (cuuint64_t)n * (cuuint64_t)n * 4};
+    const cuuint32_t box_c[3] = {kRC, kTN, 1}, box_v[3] = {kRC, kPanel, 1}, unit[3] = {1, 1, 1};
+    if (enc(&maps->c, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, H, dims, strides, box_c, unit,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS ||
+        enc(&maps->v, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, H, dims, strides, box_v, unit,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return cudaErrorInvalidValue;
+    return cudaSuccess;
+}
+
+cudaError_t launch_trailing_tc(const TrailingMaps &maps, float *H, const float *Sws, const float *tau,
+                               int *status, int64_t batch, int n, int k, cudaStream_t st)
 {
     const int nc = n - k - kPanel;
     if (nc <= 0) return cudaSuccess;
@@ -343,9 +404,7 @@ cudaError_t launch_trailing_tc(float *H, const float *Sws, const float *tau, int
     for (int64_t b0 = 0; b0 < batch; b0 += 65535) {
         const int64_t nb = (batch - b0) < 65535 ? (batch - b0) : 65535;
         dim3 grid(tiles, (unsigned)nb);
-        trailing_tc_kernel<<<grid, kThreads, kSmem, st>>>(H + b0 * (int64_t)n * n,
-                                                          Sws + b0 * kPanel * kPanel, tau + b0 * n,
-                                                          status, n, k);
+        trailing_tc_kernel<<<grid, kThreads, kSmem, st>>>(maps.c, maps.v, H, Sws, tau, status, n, k, b0);
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }

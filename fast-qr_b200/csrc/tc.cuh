@@ -99,6 +99,31 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint
     return d;
 }
 
+// Descriptor of a K-major operand in the 128-byte swizzle layout: each M/N
+// row holds 32 consecutive 32-bit K elements (128 bytes) with its 16-byte
+// chunks permuted by XOR with (row % 8); 8-row atoms of 1024 bytes, which
+// must start 1024-byte aligned.  The leading byte offset is unused for this
+// layout; the stride byte offset is the 1024-byte atom pitch.  A K step of
+// 8 elements advances the start address by 32 bytes inside the atom.  This
+// is the layout a TMA load with CU_TENSOR_MAP_SWIZZLE_128B and a 128-byte
+// inner box writes.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr)
+{
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)1 << 16;            // leading byte offset: 16 B (unused)
+    d |= (uint64_t)(1024 >> 4) << 32;  // stride byte offset: 1024 B
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)2 << 61;            // 128-byte swizzle
+    return d;
+}
+// Byte offset of 32-bit element (row, e) (e < 32) in a 128-byte-swizzled
+// tile whose rows are 128 bytes apart.
+__host__ __device__ constexpr uint32_t sw128_offset(int row, int e)
+{
+    return (uint32_t)(row * 128 + ((((e >> 2) ^ row) & 7) << 4) + (e & 3) * 4);
+}
+
 // Instruction descriptor: kind::tf32, D = f32, A = B = tf32, dense.
 // a_mn / b_mn select MN-major operands (0 = K-major).
 __host__ __device__ constexpr uint32_t idesc_tf32(int M, int N, int a_mn, int b_mn)
@@ -167,6 +192,40 @@ __device__ __forceinline__ void tmem_ld_32x16(uint32_t taddr, float (&v)[16])
 __device__ __forceinline__ void tmem_ld_wait()
 {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// --- TMA and bulk copies (async proxy; completion counted in bytes) -------
+// The issuing thread announces the bytes the barrier's current phase waits
+// for; every copy below then completes `bytes` of that count.
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *mbar, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
+                 :: "r"(smem_addr(mbar)), "r"(bytes) : "memory");
+}
+// 3-D tiled tensor load (no multicast) of the box at coordinates (x, y, z)
+// into this CTA's shared memory.  x * 4 bytes must be a multiple of 16.
+__device__ __forceinline__ void tma_load_3d(void *dst_smem, const void *tmap, int x, int y, int z,
+                                            uint64_t *mbar)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3, %4}], [%5];"
+        :: "r"(smem_addr(dst_smem)), "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z),
+           "r"(smem_addr(mbar))
+        : "memory");
+}
+// Contiguous bulk copy global -> shared; both addresses 16-byte aligned,
+// bytes a multiple of 16.
+__device__ __forceinline__ void bulk_load(void *dst_smem, const void *src, uint32_t bytes, uint64_t *mbar)
+{
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        :: "r"(smem_addr(dst_smem)), "l"(src), "r"(bytes), "r"(smem_addr(mbar))
+        : "memory");
+}
+__device__ __forceinline__ void prefetch_tensormap(const void *tmap)
+{
+    asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }
 
 // --- asynchronous 16-byte global -> shared copies (cp.async, L2 only) -----
