@@ -30,7 +30,8 @@ cudaError_t launch_trailing(float *H, const float *Sws, const float *tau, int64_
 bool trailing_tc_supported(int n);
 struct TrailingMaps {
     CUtensorMap c;  // 32 rows x 128 trailing columns, 128-byte swizzle
-    CUtensorMap v;  // 32 rows x 32 panel columns, 128-byte swizzle
+    CUtensorMap v;   // 32 rows x 32 panel columns, 128-byte swizzle
+    CUtensorMap cq;  // 128 rows x 32 trailing columns, no swizzle (phase C)
 };
 cudaError_t prepare_trailing_tc(float *H, int64_t batch, int n, TrailingMaps *maps);
 cudaError_t launch_trailing_tc(const TrailingMaps &maps, float *H, const float *Sws, const float *tau,

@@ -17,7 +17,10 @@
 //            forward substitution with S = V^T V (strict upper) and tau:
 //            T = D (I + S D)^-1, so (I + D S^T) Y = D W
 //   phase C  P[r][c] = sum_j V(r, j) Y(j, c)      tcgen05.mma M=128 (r) N=128 (c)
-//            K = 32 per 128-row chunk; epilogue C(r, c) -= P from TMEM
+//            K = 32 per 128-row chunk, into two TMEM accumulators in turn so
+//            that the next chunk's MMA runs during this chunk's epilogue;
+//            the epilogue C(r, c) -= P streams C through shared memory in
+//            32-column quarters, loaded and stored by TMA
 // The raw fp32 data is the hi operand (the tensor core truncates it to TF32);
 // threads write lo = x - trunc_tf32(x) into a second buffer of the same
 // layout.  Phase C's V and Y operands are staged by threads in the
@@ -43,8 +46,9 @@ constexpr int kStages = 3;        // phase-A ring of raw chunks
 constexpr int kRCC = 128;         // rows per phase-C chunk (MMA M)
 constexpr int kThreads = 128;
 constexpr uint32_t kTmemCols = 256;
-constexpr uint32_t kDA = 0;       // TMEM column of W^T (32 columns)
-constexpr uint32_t kDC = 128;     // TMEM column of P (128 columns)
+constexpr uint32_t kDA = 0;       // TMEM column of W^T (32 columns, phase A)
+constexpr uint32_t kDP0 = 0;      // P of even phase-C chunks (128 columns; W is dead by then)
+constexpr uint32_t kDP1 = 128;    // P of odd phase-C chunks
 constexpr uint64_t kWaitLimit = 1000000000ull;  // 1 s of wall time per wait
 
 // shared memory map (bytes, from a 1024-byte aligned base).  Phase A: a ring
@@ -56,16 +60,22 @@ constexpr int kStageBytes = kCBytes + kPanel * kRC * 4;  // 20 KB
 constexpr int kOffLo = kStages * kStageBytes;            // 60 KB
 constexpr int kOffT = kOffLo + 2 * kStageBytes;          // 100 KB: S, column-major 32 x 32 (4 KB)
 constexpr int kOffTau = kOffT + 4096;                    // tau of the panel (128 B)
-constexpr int kOffBar = kOffTau + 128;  // mbarriers: full[3], mma[2], phase C; TMEM address
-constexpr int kSmemUsed = kOffBar + 64;
+constexpr int kOffBar = kOffTau + 128;  // mbarriers: full[3], mma[2], phase C, C ring[2]; TMEM address
+constexpr int kSmemUsed = kOffBar + 128;
 constexpr int kSmem = kSmemUsed + 1024;                  // + alignment slack: ~105 KB, 2 CTAs per SM
 // Phase C (reuses the phase-A area): V chunk as the K-major A operand
-// (128 r x 32 j) and Y as the K-major B operand (128 c x 32 j), raw + lo.
+// (128 r x 32 j) and Y as the K-major B operand (128 c x 32 j), raw + lo, and
+// a ring of two C quarters (128 rows x 32 columns as they sit in H, [c][r])
+// that TMA loads and stores.
 constexpr int kOffVCraw = 0;
 constexpr int kOffVClo = 16384;
 constexpr int kOffYraw = 32768;
 constexpr int kOffYlo = 49152;
-static_assert(kOffYlo + 16384 <= kOffT, "phase-C buffers overlap S");
+constexpr int kOffCQ = 65536;
+constexpr int kCQCols = 32;
+constexpr int kCQBytes = kRCC * kCQCols * 4;  // 16 KB
+constexpr int kQuarters = kTN / kCQCols;
+static_assert(kOffCQ + 2 * kCQBytes <= kOffT, "phase-C buffers overlap S");
 static_assert(kStageBytes % 1024 == 0 && kCBytes % 1024 == 0, "swizzle atoms need 1024-byte alignment");
 
 constexpr uint32_t kIdescA = tc::idesc_tf32(128, 32, 0, 0);   // A = C^T (M = c), B = V (N = j)
@@ -97,18 +107,23 @@ __device__ __forceinline__ void split_stage(unsigned char *raw, unsigned char *l
     }
 }
 
-// V chunk as the K-major A operand of phase C (M = rows, K = the 32 panel
-// columns): core (r/8, j/4) at ((r/8) * 8 + j/4) * 128 bytes, row r%8 at
-// +16 * (r%8).  Thread = row: 4 column loads (coalesced across the warp) per
-// 16-byte store; a warp's stores cover 4 contiguous 128-byte cores.
-__device__ __forceinline__ void stage_v_kmajor(const float *Vbase, int64_t ld, int r0, int rows,
-                                               unsigned char *raw, unsigned char *lo, int tid)
+// V rows r0 + tid of a phase-C chunk, one per thread, into registers (32
+// loads, coalesced across the warp); panel rows r <= j get the unit lower
+// triangle (H holds R and beta there), rows past the matrix get 0.
+__device__ __forceinline__ void load_v_rows(const float *Vbase, int64_t ld, int r0, int rows, int tid,
+                                            float (&e)[kPanel])
 {
     const int r = r0 + tid;  // panel row
-    float e[kPanel];
 #pragma unroll
     for (int j = 0; j < kPanel; ++j)
         e[j] = (r < rows && r > j) ? __ldg(Vbase + (int64_t)j * ld + r) : (r == j ? 1.0f : 0.0f);
+}
+// ... then as the K-major A operand of phase C (M = rows, K = the 32 panel
+// columns): core (r/8, j/4) at ((r/8) * 8 + j/4) * 128 bytes, row r%8 at
+// +16 * (r%8); a warp's 16-byte stores cover 4 contiguous 128-byte cores.
+__device__ __forceinline__ void store_v_rows(const float (&e)[kPanel], unsigned char *raw, unsigned char *lo,
+                                             int tid)
+{
 #pragma unroll
     for (int jq = 0; jq < kPanel / 4; ++jq) {
         const uint32_t off = (uint32_t)(((tid >> 3) * 8 + jq) * 128 + (tid & 7) * 16);
@@ -123,7 +138,7 @@ __device__ __forceinline__ void stage_v_kmajor(const float *Vbase, int64_t ld, i
 
 __global__ void __launch_bounds__(kThreads, 2)
 trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmV,
-                   float *__restrict__ H, const float *__restrict__ Sws, const float *__restrict__ tau,
+                   const __grid_constant__ CUtensorMap tmCQ, float *__restrict__ H, const float *__restrict__ Sws, const float *__restrict__ tau,
                    int *__restrict__ status, int n, int k, int64_t b0)
 {
     extern __shared__ unsigned char smem_raw[];
@@ -139,8 +154,9 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
 
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + kOffBar);  // [kStages]
     uint64_t *mmab = full + kStages;                                // [2]
-    uint64_t *cbar = full + kStages + 2;                            // phase C
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kOffBar + 48);
+    uint64_t *cbar = full + kStages + 2;                            // phase-C MMA
+    uint64_t *cfull = full + kStages + 3;                           // [2] C quarter ring
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kOffBar + 64);
     float *Ts = reinterpret_cast<float *>(smem + kOffT);    // S(l, c) at c * 32 + l
     float *taus = reinterpret_cast<float *>(smem + kOffTau);
     const uint32_t sbase = tc::smem_addr(smem);
@@ -151,7 +167,8 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
     if (tid == 0) {
         tc::prefetch_tensormap(&tmC);
         tc::prefetch_tensormap(&tmV);
-        for (int i = 0; i < kStages + 3; ++i) tc::mbar_init(&full[i], 1);
+        tc::prefetch_tensormap(&tmCQ);
+        for (int i = 0; i < kStages + 5; ++i) tc::mbar_init(&full[i], 1);
         tc::fence_mbar_init();
         for (int s = 0; s < kStages && s < nchunks; ++s) {
             unsigned char *st = smem + s * kStageBytes;
@@ -234,6 +251,25 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
     if (tid < kPanel) taus[tid] = tau_r;
     __syncthreads();
 
+    // ---- phase C set-up: the first two C quarters start streaming now
+    const int ncc = (m + kRCC - 1) / kRCC;
+    const int nq = ncc * kQuarters;  // C quarters of the tile, in order (chunk, quarter)
+    int q_loads = 0;                 // quarters whose TMA load was issued
+    int q_used[2] = {0, 0};          // quarters consumed per ring buffer
+    auto load_quarter = [&](int u) {  // thread 0
+        unsigned char *cs = smem + kOffCQ + (u & 1) * kCQBytes;
+        tc::mbar_expect_tx(&cfull[u & 1], kCQBytes);
+        tc::tma_load_3d(cs, &tmCQ, k + kRCC * (u / kQuarters), c0 + kCQCols * (u % kQuarters), (int)mat,
+                        &cfull[u & 1]);
+    };
+    float e[kPanel];  // V rows of the next phase-C chunk
+    if (ok) {
+        if (tid == 0)
+            for (int u = 0; u < 2 && u < nq; ++u) load_quarter(u);
+        q_loads = nq < 2 ? nq : 2;
+        load_v_rows(Vbase, n, 0, m, tid, e);
+    }
+
     // ---- phase B: Y = T^T W, thread = tile column c ------------------------
     if (ok) {
         tc::fence_after_sync();
@@ -251,7 +287,6 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
             for (int l = 0; l < cc; ++l) a = fmaf(-Ts[cc * 32 + l], y[l], a);
             y[cc] = taus[cc] * a;
         }
-        __syncthreads();  // every thread is done with the phase-A buffers
         // Y as the K-major B operand of phase C: core (c/8, j/4) at
         // ((c/8) * 8 + j/4) * 128 bytes, column c%8 at +16 * (c%8)
 #pragma unroll
@@ -262,17 +297,21 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
             *reinterpret_cast<float4 *>(smem + kOffYlo + off) =
                 make_float4(tc::tf32_lo(v.x), tc::tf32_lo(v.y), tc::tf32_lo(v.z), tc::tf32_lo(v.w));
         }
-        tc::fence_before_sync();
+        store_v_rows(e, smem + kOffVCraw, smem + kOffVClo, tid);
+        tc::fence_proxy_async_smem();
+        tc::fence_before_sync();  // the W load precedes phase C's MMAs into the same columns
     }
 
     // ---- phase C: C -= V Y, 128 rows per chunk -----------------------------
+    // MMA(j) writes P[j % 2]; it is issued once MMA(j-1) has completed and
+    // chunk j's V rows (loaded into registers one chunk ahead) are staged, so
+    // it runs during the epilogue of chunk j-1.  The epilogue works in C
+    // quarters of 32 columns that TMA loads two ahead and stores back.
     uint32_t c_issued = 0, c_waited = 0;
-    for (int r0 = 0; r0 < m && ok; r0 += kRCC) {
-        stage_v_kmajor(Vbase, n, r0, m, smem + kOffVCraw, smem + kOffVClo, tid);
-        tc::fence_proxy_async_smem();
-        __syncthreads();
+    auto issue_c = [&](int j) {
         if (tid == 0) {
             tc::fence_after_sync();
+            const uint32_t d = tmem + ((j & 1) ? kDP1 : kDP0);
 #pragma unroll
             for (int s = 0; s < kPanel / 8; ++s) {
                 // A = V (K-major, M = rows), B = Y (K-major, N = columns):
@@ -281,50 +320,61 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
                 const uint64_t al = tc::smem_desc(sbase + kOffVClo + (uint32_t)s * 256, 128, 1024);
                 const uint64_t bh = tc::smem_desc(sbase + kOffYraw + (uint32_t)s * 256, 128, 1024);
                 const uint64_t bl = tc::smem_desc(sbase + kOffYlo + (uint32_t)s * 256, 128, 1024);
-                tc::mma_tf32(tmem + kDC, al, bh, kIdescC, s > 0 ? 1u : 0u);
-                tc::mma_tf32(tmem + kDC, ah, bl, kIdescC, 1u);
-                tc::mma_tf32(tmem + kDC, ah, bh, kIdescC, 1u);
+                tc::mma_tf32(d, al, bh, kIdescC, s > 0 ? 1u : 0u);
+                tc::mma_tf32(d, ah, bl, kIdescC, 1u);
+                tc::mma_tf32(d, ah, bh, kIdescC, 1u);
             }
             tc::mma_commit(cbar);
         }
         ++c_issued;
-        // epilogue: thread = row r0 + 32 warp + lane.  The first 16 columns of
-        // C are loaded while the MMA runs; each later group is loaded before
-        // the previous one is stored.
-        const int r = r0 + 32 * warp + lane;
-        float *Crow = Hm + (int64_t)c0 * n + k + r;
-        const bool rv = r < m;
-        float cv[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) cv[i] = (rv && i < nct) ? Crow[(int64_t)i * n] : 0.0f;
+    };
+    if (ok) {
+        ok = !__syncthreads_or(false);  // Y and V(0) staged
+        issue_c(0);
+        if (ncc > 1) load_v_rows(Vbase, n, kRCC, m, tid, e);
+    }
+    for (int j = 0; j < ncc && ok; ++j) {
         const bool done = tc::mbar_wait(cbar, c_waited & 1u, kWaitLimit);
         if (done) ++c_waited;
+        if (done && j + 1 < ncc) {
+            store_v_rows(e, smem + kOffVCraw, smem + kOffVClo, tid);
+            tc::fence_proxy_async_smem();
+        }
         ok = !__syncthreads_or(!done);
         if (!ok) break;
+        if (j + 1 < ncc) issue_c(j + 1);
+        if (j + 2 < ncc) load_v_rows(Vbase, n, (j + 2) * kRCC, m, tid, e);
         tc::fence_after_sync();
-#pragma unroll 1
-        for (int cg16 = 0; cg16 < kTN / 16; ++cg16) {
-            float pv[16];
-            tc::tmem_ld_32x16(tmem + ((uint32_t)(32 * warp) << 16) + kDC + 16 * cg16, pv);
+        const uint32_t pc = tmem + ((uint32_t)(32 * warp) << 16) + ((j & 1) ? kDP1 : kDP0);
+        // epilogue: thread = row j * 128 + tid of the tile
+        for (int q = 0; q < kQuarters; ++q) {
+            const int u = j * kQuarters + q, b = u & 1;
+            const bool landed = tc::mbar_wait(&cfull[b], (uint32_t)q_used[b] & 1u, kWaitLimit);
+            if (landed) ++q_used[b];
+            float pv[32];
+            tc::tmem_ld_32x32(pc + kCQCols * q, pv);
             tc::tmem_ld_wait();
-            float nxt[16];
-            const int nb = 16 * (cg16 + 1);
+            float *cs = reinterpret_cast<float *>(smem + kOffCQ + b * kCQBytes);
+            if (landed) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i)
-                nxt[i] = (rv && cg16 + 1 < kTN / 16 && nb + i < nct) ? Crow[(int64_t)(nb + i) * n] : 0.0f;
-            if (rv) {
-#pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const int c = 16 * cg16 + i;
-                    if (c < nct) Crow[(int64_t)c * n] = cv[i] - pv[i];
+                for (int c = 0; c < kCQCols; ++c) cs[c * kRCC + tid] -= pv[c];
+            }
+            tc::fence_proxy_async_smem();
+            ok = !__syncthreads_or(!landed);
+            if (!ok) break;
+            if (tid == 0) {
+                tc::tma_store_3d(&tmCQ, k + kRCC * j, c0 + kCQCols * q, (int)mat, cs);
+                tc::bulk_commit_group();
+                if (u + 2 < nq) {
+                    tc::bulk_wait_group_read<0>();  // the store has read the buffer
+                    load_quarter(u + 2);
                 }
             }
-#pragma unroll
-            for (int i = 0; i < 16; ++i) cv[i] = nxt[i];
+            if (u + 2 < nq) ++q_loads;
         }
         tc::fence_before_sync();
-        __syncthreads();
     }
+    if (tid == 0) tc::bulk_wait_group<0>();  // stores complete before shared memory goes away
 
     if (!ok && tid == 0) {
         atomicOr(status, 1);
@@ -341,6 +391,11 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
                 if (!tc::mbar_wait(&mmab[b], mma_waited[b]++ & 1u, kWaitLimit)) break;
         while (c_waited < c_issued)
             if (!tc::mbar_wait(cbar, c_waited++ & 1u, kWaitLimit)) break;
+        for (int b = 0; b < 2; ++b) {
+            const int issued_b = (q_loads + 1 - b) / 2;  // loads into ring buffer b
+            while (q_used[b] < issued_b)
+                if (!tc::mbar_wait(&cfull[b], (uint32_t)q_used[b]++ & 1u, kWaitLimit)) break;
+        }
     }
     __syncthreads();
     if (warp == 0) {
@@ -382,11 +437,15 @@ cudaError_t prepare_trailing_tc(float *H, int64_t batch, int n, TrailingMaps *ma
     const cuuint64_t dims[3] = {(cuuint64_t)n, (cuuint64_t)n, (cuuint64_t)batch};
     const cuuint64_t strides[2] = {(cuuint64_t)n * 4, (cuuint64_t)n * (cuuint64_t)n * 4};
     const cuuint32_t box_c[3] = {kRC, kTN, 1}, box_v[3] = {kRC, kPanel, 1}, unit[3] = {1, 1, 1};
+    const cuuint32_t box_cq[3] = {kRCC, kCQCols, 1};
     if (enc(&maps->c, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, H, dims, strides, box_c, unit,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS ||
         enc(&maps->v, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, H, dims, strides, box_v, unit,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS ||
+        enc(&maps->cq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, H, dims, strides, box_cq, unit,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return cudaErrorInvalidValue;
     return cudaSuccess;
@@ -404,7 +463,7 @@ cudaError_t launch_trailing_tc(const TrailingMaps &maps, float *H, const float *
     for (int64_t b0 = 0; b0 < batch; b0 += 65535) {
         const int64_t nb = (batch - b0) < 65535 ? (batch - b0) : 65535;
         dim3 grid(tiles, (unsigned)nb);
-        trailing_tc_kernel<<<grid, kThreads, kSmem, st>>>(maps.c, maps.v, H, Sws, tau, status, n, k, b0);
+        trailing_tc_kernel<<<grid, kThreads, kSmem, st>>>(maps.c, maps.v, maps.cq, H, Sws, tau, status, n, k, b0);
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }

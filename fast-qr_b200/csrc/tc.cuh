@@ -223,6 +223,30 @@ __device__ __forceinline__ void bulk_load(void *dst_smem, const void *src, uint3
         :: "r"(smem_addr(dst_smem)), "l"(src), "r"(bytes), "r"(smem_addr(mbar))
         : "memory");
 }
+// 3-D tiled tensor store of a box from this CTA's shared memory; elements
+// outside the tensor are not written.  Completion is tracked by bulk groups.
+__device__ __forceinline__ void tma_store_3d(const void *tmap, int x, int y, int z, const void *src_smem)
+{
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];"
+                 :: "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(smem_addr(src_smem))
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group()
+{
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// wait until at most N bulk groups of this thread still read shared memory
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read()
+{
+    asm volatile("cp.async.bulk.wait_group.read %0;" :: "n"(N) : "memory");
+}
+// wait until at most N bulk groups of this thread are incomplete
+template <int N>
+__device__ __forceinline__ void bulk_wait_group()
+{
+    asm volatile("cp.async.bulk.wait_group %0;" :: "n"(N) : "memory");
+}
 __device__ __forceinline__ void prefetch_tensormap(const void *tmap)
 {
     asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
