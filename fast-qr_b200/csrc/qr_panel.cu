@@ -13,6 +13,10 @@ namespace cg = cooperative_groups;
 
 namespace fqr {
 
+namespace {
+constexpr int kStagePitch = 36;  // floats per row of a warp's 32 x 32 staging block
+}  // namespace
+
 // ---------------------------------------------------------------------------
 // Panel kernel.
 //
@@ -71,17 +75,42 @@ panel_kernel(float *__restrict__ H, float *__restrict__ tau, float *__restrict__
     const int w = m < kPanel ? m : kPanel;
     float *Hm = H + mat * (int64_t)n * n;
     const bool top = crank == 0 && wid == 0;  // holds panel rows 0..31
+    // per-warp staging of one 32 x 32 block, row-major with a 36-float pitch:
+    // 16-byte accesses by 8 consecutive lanes (one column group each, or one
+    // row each) hit 8 distinct 16-byte bank groups
+    extern __shared__ float4 panel_stage[];
+    float *stg = reinterpret_cast<float *>(panel_stage) + wid * (32 * kStagePitch);
 
     int row[NR];
     float p[NR][4];
 #pragma unroll
-    for (int q = 0; q < NR; ++q) {
-        row[q] = crank * ROWS + (q >> 3) * (NW * 32) + wid * 32 + 8 * rg + (q & 7);
+    for (int q = 0; q < NR; ++q) row[q] = crank * ROWS + (q >> 3) * (NW * 32) + wid * 32 + 8 * rg + (q & 7);
+    // load: lane = row, one coalesced 128-byte column segment per load, then
+    // each lane picks up its 8 rows x 4 columns
 #pragma unroll
-        for (int jj = 0; jj < 4; ++jj) {
-            const int col = 4 * cgp + jj;
-            p[q][jj] = (row[q] < m && col < w) ? Hm[(int64_t)(k + col) * n + k + row[q]] : 0.0f;
+    for (int b = 0; b < R; ++b) {
+        const int r = crank * ROWS + b * (NW * 32) + wid * 32 + lane;
+        const float *src = Hm + (int64_t)k * n + k + r;
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+            float v[4];
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+                const int col = 4 * t + jj;
+                v[jj] = (r < m && col < w) ? src[(int64_t)col * n] : 0.0f;
+            }
+            *reinterpret_cast<float4 *>(stg + lane * kStagePitch + 4 * t) = make_float4(v[0], v[1], v[2], v[3]);
         }
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float4 v = *reinterpret_cast<const float4 *>(stg + (8 * rg + i) * kStagePitch + 4 * cgp);
+            p[b * 8 + i][0] = v.x;
+            p[b * 8 + i][1] = v.y;
+            p[b * 8 + i][2] = v.z;
+            p[b * 8 + i][3] = v.w;
+        }
+        __syncwarp();
     }
 
     // Reduce-scatter of 4 per-lane values over the 4 row groups of a warp
@@ -274,19 +303,35 @@ panel_kernel(float *__restrict__ H, float *__restrict__ tau, float *__restrict__
         if (lane < w) tau[mat * n + k + lane] = tau_s[lane];
     }
 
+    // store: the reverse of the load (coalesced 128-byte column segments)
 #pragma unroll
-    for (int q = 0; q < NR; ++q) {
+    for (int b = 0; b < R; ++b) {
 #pragma unroll
-        for (int jj = 0; jj < 4; ++jj) {
-            const int col = 4 * cgp + jj;
-            if (row[q] < m && col < w) Hm[(int64_t)(k + col) * n + k + row[q]] = p[q][jj];
+        for (int i = 0; i < 8; ++i)
+            *reinterpret_cast<float4 *>(stg + (8 * rg + i) * kStagePitch + 4 * cgp) =
+                make_float4(p[b * 8 + i][0], p[b * 8 + i][1], p[b * 8 + i][2], p[b * 8 + i][3]);
+        __syncwarp();
+        const int r = crank * ROWS + b * (NW * 32) + wid * 32 + lane;
+        float *dst = Hm + (int64_t)k * n + k + r;
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+            const float4 v = *reinterpret_cast<const float4 *>(stg + lane * kStagePitch + 4 * t);
+            const float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+                const int col = 4 * t + jj;
+                if (r < m && col < w) dst[(int64_t)col * n] = e[jj];
+            }
         }
+        __syncwarp();
     }
     if constexpr (CLUSTER) {
         // keep every CTA's shared memory alive until all remote writes landed
         cg::this_cluster().sync();
     }
 }
+
+static size_t panel_stage_bytes(int nw) { return (size_t)nw * 32 * kStagePitch * sizeof(float); }
 
 PanelShape panel_shape(int m)
 {
@@ -303,14 +348,25 @@ template <int NW, int R>
 static cudaError_t launch_panel_t(float *H, float *tau, float *Tws, int64_t batch, int n, int k,
                                   int cluster, cudaStream_t st)
 {
+    const size_t dyn = panel_stage_bytes(NW);
     if (cluster <= 1) {
-        panel_kernel<NW, R, false><<<(unsigned)batch, NW * 32, 0, st>>>(H, tau, Tws, n, k);
+        if (dyn > 48 * 1024) {
+            cudaError_t e = cudaFuncSetAttribute(panel_kernel<NW, R, false>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);
+            if (e != cudaSuccess) return e;
+        }
+        panel_kernel<NW, R, false><<<(unsigned)batch, NW * 32, dyn, st>>>(H, tau, Tws, n, k);
         return cudaGetLastError();
+    }
+    if (dyn > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(panel_kernel<NW, R, true>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);
+        if (e != cudaSuccess) return e;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(batch * cluster), 1, 1);
     cfg.blockDim = dim3(NW * 32, 1, 1);
-    cfg.dynamicSmemBytes = 0;
+    cfg.dynamicSmemBytes = dyn;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
