@@ -334,7 +334,7 @@ def kernel_roofline(cfg_name, a, h, tau, ws, flush, steps, dev) -> dict:
     per_step_ms = {kname: v / steps for kname, v in tot.items()}
     dom = max(per_step_ms, key=per_step_ms.get)
     t = per_step_ms[dom] / 1e3
-    traffic = _traffic_from_profiles(cfg_name)
+    traffic = _traffic_from_profiles(cfg_name, dom)
     share = {kname: round(v / max(sum(per_step_ms.values()), 1e-12), 4) for kname, v in per_step_ms.items()}
     base = {"kernel": dom, "stage_ms_per_step": per_step_ms, "stage_share": share,
             "traffic": traffic, "peak_source": pk["source"]}
@@ -356,8 +356,10 @@ def kernel_roofline(cfg_name, a, h, tau, ws, flush, steps, dev) -> dict:
     return base
 
 
-def _traffic_from_profiles(cfg_name):
-    p = ROOT / "profiles" / f"traffic_{cfg_name}.txt"
+def _traffic_from_profiles(cfg_name, kernel):
+    """DRAM bytes per launch of `kernel` from the committed ncu summary
+    profiles/traffic_<config>_<kernel>.txt (None when there is none)."""
+    p = ROOT / "profiles" / f"traffic_{cfg_name}_{kernel}.txt"
     if not p.exists():
         return None
     for line in p.read_text().splitlines():
