@@ -10,6 +10,8 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <mutex>
+
 #include "../../include/fastqr.h"
 #include "internal.h"
 
@@ -132,11 +134,90 @@ struct StageTimer {
     }
 };
 
+// The blocked path for one batch range: copy-in, then per 32-column panel a
+// panel kernel and a trailing update, all on `st`.
+int enqueue_blocked(const float *A, int64_t batch, int n, int64_t a_bstride, int64_t a_rstride,
+                    int64_t a_cstride, float *H, float *tau, float *Tws, int *status, int clear, bool tc,
+                    cudaStream_t st, StageTimer *tm)
+{
+    fqr::TrailingMaps maps;
+    if (tc && fqr::prepare_trailing_tc(H, batch, n, &maps) != cudaSuccess) return FQR_ECUDA;
+    cudaError_t e;
+    if (tm) tm->begin(FQR_STAGE_COPY_IN);
+    e = fqr::launch_copy_in(A, batch, n, a_bstride, a_rstride, a_cstride, H, status, clear, st);
+    if (tm) tm->end();
+    if (e != cudaSuccess) return status_from(e);
+    for (int k = 0; k < n; k += fqr::kPanel) {
+        if (tm) tm->begin(FQR_STAGE_PANEL);
+        e = fqr::launch_panel(H, tau, Tws, batch, n, k, st);
+        if (tm) tm->end();
+        if (e != cudaSuccess) return status_from(e);
+        if (k + fqr::kPanel < n) {
+            if (tm) tm->begin(FQR_STAGE_TRAILING);
+            e = tc ? fqr::launch_trailing_tc(maps, H, Tws, tau, status, batch, n, k, st)
+                   : fqr::launch_trailing(H, Tws, tau, batch, n, k, st);
+            if (tm) tm->end();
+            if (e != cudaSuccess) return status_from(e);
+        }
+    }
+    return FQR_OK;
+}
+
+// Batches of two or more matrices run as two halves on two streams: the
+// caller's and an internal one per device, which first waits for everything
+// enqueued on the caller's stream before the call and which the caller's
+// stream waits for at the end, so the call orders like a single launch.  The
+// halves' kernels fill each other's idle SMs (the last, partial wave of every
+// trailing launch; the single-CTA-per-matrix panels).
+struct SplitStreams {
+    bool ready = false;
+    cudaStream_t side = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
+    std::mutex mu;
+};
+constexpr int kMaxDevices = 64;
+SplitStreams g_split[kMaxDevices];
+
+int enqueue_blocked_split(const float *A, int64_t batch, int n, int64_t a_bstride, int64_t a_rstride,
+                          int64_t a_cstride, float *H, float *tau, float *Tws, int *status, bool tc,
+                          cudaStream_t st)
+{
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return FQR_ECUDA;
+    SplitStreams &sp = g_split[dev];
+    std::lock_guard<std::mutex> lock(sp.mu);
+    if (!sp.ready) {
+        if (cudaStreamCreateWithFlags(&sp.side, cudaStreamNonBlocking) != cudaSuccess ||
+            cudaEventCreateWithFlags(&sp.fork, cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&sp.join, cudaEventDisableTiming) != cudaSuccess)
+            return FQR_ECUDA;
+        sp.ready = true;
+    }
+    const int64_t b0 = batch / 2;
+    const size_t nn = (size_t)n * (size_t)n;
+    if (cudaEventRecord(sp.fork, st) != cudaSuccess || cudaStreamWaitEvent(sp.side, sp.fork, 0) != cudaSuccess)
+        return FQR_ECUDA;
+    // each half its own status word (the copy-in of a half clears its word)
+    int rc1 = enqueue_blocked(A, b0, n, a_bstride, a_rstride, a_cstride, H, tau, Tws, status, 1, tc, st,
+                              nullptr);
+    int rc2 = enqueue_blocked(A + b0 * a_bstride, batch - b0, n, a_bstride, a_rstride, a_cstride,
+                              H + b0 * nn, tau + b0 * n, Tws + b0 * (fqr::kPanel * fqr::kPanel), status + 1,
+                              1, tc, sp.side, nullptr);
+    // join even after a failure, so nothing of this call stays unordered with
+    // later work on the caller's stream
+    cudaError_t j = cudaEventRecord(sp.join, sp.side);
+    if (j == cudaSuccess) j = cudaStreamWaitEvent(st, sp.join, 0);
+    if (rc1 != FQR_OK) return rc1;
+    if (rc2 != FQR_OK) return rc2;
+    return j == cudaSuccess ? FQR_OK : FQR_ECUDA;
+}
+
 // status_word: where the tensor-core kernels record a bounded wait that gave
-// up (NULL: the word after the T factors in the workspace).
+// up (NULL: the words after the S blocks in the workspace).  split: whether
+// a batch of two or more may run as two halves on two streams.
 int run_geqrf(const float *A, int64_t batch, int64_t n, int64_t a_bstride, int64_t a_rstride,
               int64_t a_cstride, float *H, float *tau, void *workspace, size_t workspace_bytes,
-              cudaStream_t st, StageTimer *tm, int *status_word = nullptr)
+              cudaStream_t st, StageTimer *tm, int *status_word = nullptr, bool split = true)
 {
     if (batch < 0 || n < 0) return FQR_EINVAL;
     if (batch == 0 || n == 0) return FQR_OK;
@@ -144,11 +225,10 @@ int run_geqrf(const float *A, int64_t batch, int64_t n, int64_t a_bstride, int64
     if (!A || !H || !tau) return FQR_EINVAL;
     if (a_rstride == 0 || a_cstride == 0 || (batch > 1 && a_bstride == 0)) return FQR_EINVAL;
     const int ni = (int)n;
-    cudaError_t e;
 
     if (small_path(n)) {
         if (tm) tm->begin(FQR_STAGE_SMALL);
-        e = fqr::launch_small(A, batch, ni, a_bstride, a_rstride, a_cstride, H, tau, st);
+        cudaError_t e = fqr::launch_small(A, batch, ni, a_bstride, a_rstride, a_cstride, H, tau, st);
         if (tm) tm->end();
         return status_from(e);
     }
@@ -160,27 +240,13 @@ int run_geqrf(const float *A, int64_t batch, int64_t n, int64_t a_bstride, int64
     int *status = status_word ? status_word
                               : (int *)((unsigned char *)workspace + fqr::ws_t_bytes(batch));
     const bool tc = use_tc(n) && ((uintptr_t)H % 16) == 0;
-    fqr::TrailingMaps maps;
-    if (tc && fqr::prepare_trailing_tc(H, batch, ni, &maps) != cudaSuccess) return FQR_ECUDA;
-
-    if (tm) tm->begin(FQR_STAGE_COPY_IN);
-    e = fqr::launch_copy_in(A, batch, ni, a_bstride, a_rstride, a_cstride, H, status, st);
-    if (tm) tm->end();
-    if (e != cudaSuccess) return status_from(e);
-    for (int k = 0; k < ni; k += fqr::kPanel) {
-        if (tm) tm->begin(FQR_STAGE_PANEL);
-        e = fqr::launch_panel(H, tau, Tws, batch, ni, k, st);
-        if (tm) tm->end();
-        if (e != cudaSuccess) return status_from(e);
-        if (k + fqr::kPanel < ni) {
-            if (tm) tm->begin(FQR_STAGE_TRAILING);
-            e = tc ? fqr::launch_trailing_tc(maps, H, Tws, tau, status, batch, ni, k, st)
-                   : fqr::launch_trailing(H, Tws, tau, batch, ni, k, st);
-            if (tm) tm->end();
-            if (e != cudaSuccess) return status_from(e);
-        }
-    }
-    return FQR_OK;
+    if (split && !tm && batch >= 2)
+        return enqueue_blocked_split(A, batch, ni, a_bstride, a_rstride, a_cstride, H, tau, Tws, status,
+                                     tc, st);
+    // an own status word (host entry, one per chunk) or both words of the
+    // workspace's status block
+    return enqueue_blocked(A, batch, ni, a_bstride, a_rstride, a_cstride, H, tau, Tws, status,
+                           status_word ? 1 : 2, tc, st, tm);
 }
 
 }  // namespace
@@ -199,7 +265,7 @@ int fqr::geqrf_enqueue_status(const float *A, int64_t batch, int64_t n, int64_t 
                               cudaStream_t st)
 {
     return run_geqrf(A, batch, n, a_bstride, a_rstride, a_cstride, H, tau, workspace,
-                     workspace_bytes, st, nullptr, status_word);
+                     workspace_bytes, st, nullptr, status_word, false);
 }
 
 extern "C" {
@@ -216,14 +282,14 @@ int fqr_check_status(const void *workspace, size_t workspace_bytes, int64_t batc
 {
     if (batch <= 0) return FQR_OK;
     const size_t t = fqr::ws_t_bytes(batch);
-    if (!workspace || workspace_bytes < t + sizeof(int)) return FQR_EINVAL;
-    int v = 0;
+    if (!workspace || workspace_bytes < t + 2 * sizeof(int)) return FQR_EINVAL;
+    int v[2] = {0, 0};  // one word per half of a batch split over two streams
     cudaStream_t st = (cudaStream_t)stream;
-    if (cudaMemcpyAsync(&v, (const unsigned char *)workspace + t, sizeof(int), cudaMemcpyDeviceToHost,
+    if (cudaMemcpyAsync(v, (const unsigned char *)workspace + t, sizeof(v), cudaMemcpyDeviceToHost,
                         st) != cudaSuccess)
         return FQR_ECUDA;
     if (cudaStreamSynchronize(st) != cudaSuccess) return FQR_ECUDA;
-    return v ? FQR_ETIMEOUT : FQR_OK;
+    return (v[0] | v[1]) ? FQR_ETIMEOUT : FQR_OK;
 }
 
 int fqr_geqrf_f32_profile(const float *A, int64_t batch, int64_t n, int64_t a_bstride,

@@ -16,8 +16,9 @@ cudaError_t launch_small(const float *A, int64_t batch, int n, int64_t bs, int64
                          float *H, float *tau, cudaStream_t st);
 
 // Blocked path pieces (n > 64).
+// Also clears status[0 .. clear-1] (the bounded-wait status words).
 cudaError_t launch_copy_in(const float *A, int64_t batch, int n, int64_t bs, int64_t rs, int64_t cs,
-                           float *H, int *status, cudaStream_t st);
+                           float *H, int *status, int clear, cudaStream_t st);
 cudaError_t launch_panel(float *H, float *tau, float *Tws, int64_t batch, int n, int k,
                          cudaStream_t st);
 cudaError_t launch_trailing(float *H, const float *Sws, const float *tau, int64_t batch, int n, int k,

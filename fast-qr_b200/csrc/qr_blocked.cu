@@ -34,10 +34,11 @@ namespace fqr {
 // memory so both the reads (rows) and the writes (columns) are coalesced.
 __global__ void __launch_bounds__(256)
 copy_in_rowmajor_kernel(const float *__restrict__ A, int64_t batch, int n, int64_t bs, int64_t rs,
-                        float *__restrict__ H, int *__restrict__ status)
+                        float *__restrict__ H, int *__restrict__ status, int clear)
 {
     __shared__ float tile[32][33];
-    if (status && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && threadIdx.x == 0) *status = 0;
+    if (status && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && threadIdx.x < clear)
+        status[threadIdx.x] = 0;
     const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
     const int j0 = blockIdx.x * 32, i0 = blockIdx.y * 32;
     for (int64_t b = blockIdx.z; b < batch; b += gridDim.z) {
@@ -62,9 +63,9 @@ copy_in_rowmajor_kernel(const float *__restrict__ A, int64_t batch, int n, int64
 // writes coalesced along columns of H.
 __global__ void __launch_bounds__(256)
 copy_in_strided_kernel(const float *__restrict__ A, int64_t batch, int n, int64_t bs, int64_t rs,
-                       int64_t cs, float *__restrict__ H, int *__restrict__ status)
+                       int64_t cs, float *__restrict__ H, int *__restrict__ status, int clear)
 {
-    if (status && blockIdx.x == 0 && threadIdx.x == 0) *status = 0;
+    if (status && blockIdx.x == 0 && threadIdx.x < clear) status[threadIdx.x] = 0;
     const int64_t nn = (int64_t)n * n;
     const int64_t total = batch * nn;
     for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
@@ -77,17 +78,17 @@ copy_in_strided_kernel(const float *__restrict__ A, int64_t batch, int n, int64_
 }
 
 cudaError_t launch_copy_in(const float *A, int64_t batch, int n, int64_t bs, int64_t rs, int64_t cs,
-                           float *H, int *status, cudaStream_t st)
+                           float *H, int *status, int clear, cudaStream_t st)
 {
     if (cs == 1) {
         const unsigned t = (unsigned)((n + 31) / 32);
         dim3 grid(t, t, (unsigned)(batch < 65535 ? batch : 65535));
-        copy_in_rowmajor_kernel<<<grid, 256, 0, st>>>(A, batch, n, bs, rs, H, status);
+        copy_in_rowmajor_kernel<<<grid, 256, 0, st>>>(A, batch, n, bs, rs, H, status, clear);
     } else {
         const int64_t total = batch * (int64_t)n * n;
         int64_t blocks = (total + 255) / 256;
         if (blocks > 148 * 64) blocks = 148 * 64;
-        copy_in_strided_kernel<<<(unsigned)blocks, 256, 0, st>>>(A, batch, n, bs, rs, cs, H, status);
+        copy_in_strided_kernel<<<(unsigned)blocks, 256, 0, st>>>(A, batch, n, bs, rs, cs, H, status, clear);
     }
     return cudaGetLastError();
 }

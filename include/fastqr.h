@@ -6,8 +6,11 @@
  * cudaStream_t passed as void*.  All calls are asynchronous on `stream`: they
  * validate arguments on the host, enqueue kernels and return.  The library
  * allocates no device memory on this path; scratch space is caller-owned
- * (see fqr_workspace_bytes).  Calls are reentrant: the only global state is a
- * per-device cache of SM count and kernel attributes.
+ * (see fqr_workspace_bytes).  Calls are reentrant: the only global state is
+ * per device -- a second stream and two events, created on first use, on
+ * which the blocked path runs half of a batch of two or more matrices (always
+ * ordered with the caller's stream: it waits for the caller's prior work and
+ * the caller's stream waits for it).
  *
  * Output layout (the contract of torch.geqrf, and of the reference's
  * `custom_kernel(data) -> (H, tau)`):
