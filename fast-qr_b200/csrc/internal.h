@@ -35,6 +35,16 @@ struct TrailingMaps {
     CUtensorMap cq;  // 128 rows x 32 trailing columns, no swizzle (phase C)
 };
 cudaError_t prepare_trailing_tc(float *H, int64_t batch, int n, TrailingMaps *maps);
+// Maps for applying the reflectors stored in H (n x n per matrix) to a
+// target C (n x c_cols per matrix, column-major, batch stride n * c_cols).
+cudaError_t prepare_apply_maps(const float *H, int n, float *C, int64_t c_cols, int64_t batch,
+                               TrailingMaps *maps);
+// C[k:n, c_begin:c_end] := (I - V T^T V^T) C (apply_t) or (I - V T V^T) C,
+// V = the unit-lower reflectors of columns k .. k+31 of H (fewer at the end),
+// T = D (I + S D)^-1 from S blocks at Sws + mat * s_stride (floats) and tau.
+cudaError_t launch_apply_tc(const TrailingMaps &maps, const float *H, const float *Sws, int64_t s_stride,
+                            const float *tau, int *status, int64_t batch, int n, int k, int c_begin,
+                            int c_end, bool apply_t, cudaStream_t st);
 cudaError_t launch_trailing_tc(const TrailingMaps &maps, float *H, const float *Sws, const float *tau,
                                int *status, int64_t batch, int n, int k, cudaStream_t st);
 

@@ -110,13 +110,13 @@ __device__ __forceinline__ void split_stage(unsigned char *raw, unsigned char *l
 // V rows r0 + tid of a phase-C chunk, one per thread, into registers (32
 // loads, coalesced across the warp); panel rows r <= j get the unit lower
 // triangle (H holds R and beta there), rows past the matrix get 0.
-__device__ __forceinline__ void load_v_rows(const float *Vbase, int64_t ld, int r0, int rows, int tid,
+__device__ __forceinline__ void load_v_rows(const float *Vbase, int64_t ld, int r0, int rows, int wv, int tid,
                                             float (&e)[kPanel])
 {
     const int r = r0 + tid;  // panel row
 #pragma unroll
     for (int j = 0; j < kPanel; ++j)
-        e[j] = (r < rows && r > j) ? __ldg(Vbase + (int64_t)j * ld + r) : (r == j ? 1.0f : 0.0f);
+        e[j] = (j < wv && r < rows && r > j) ? __ldg(Vbase + (int64_t)j * ld + r) : (r == j ? 1.0f : 0.0f);
 }
 // ... then as the K-major A operand of phase C (M = rows, K = the 32 panel
 // columns): core (r/8, j/4) at ((r/8) * 8 + j/4) * 128 bytes, row r%8 at
@@ -136,20 +136,26 @@ __device__ __forceinline__ void store_v_rows(const float (&e)[kPanel], unsigned 
 
 }  // namespace
 
+template <bool ApplyT>
 __global__ void __launch_bounds__(kThreads, 2)
 trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmV,
-                   const __grid_constant__ CUtensorMap tmCQ, float *__restrict__ H, const float *__restrict__ Sws, const float *__restrict__ tau,
-                   int *__restrict__ status, int n, int k, int64_t b0)
+                   const __grid_constant__ CUtensorMap tmCQ, const float *__restrict__ H,
+                   const float *__restrict__ Sws, int64_t s_stride, const float *__restrict__ tau,
+                   int *__restrict__ status, int n, int k, int c_begin, int c_end, int64_t b0)
 {
     extern __shared__ unsigned char smem_raw[];
     const uint32_t raw_addr = tc::smem_addr(smem_raw);
     unsigned char *smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int64_t mat = b0 + blockIdx.y;
-    const int c0 = k + kPanel + blockIdx.x * kTN;  // first trailing column of the tile
-    const int nct = min(kTN, n - c0);
-    const int m = n - k;
-    float *Hm = H + mat * (int64_t)n * n;
+    // tile = kTN columns of [c_begin, c_end) of the target matrix; phase A
+    // reads the whole kTN-wide box (its extra columns are never used), phase C
+    // touches only the tile's own columns
+    const int c0 = c_begin + blockIdx.x * kTN;  // first column of the tile
+    const int nct = min(kTN, c_end - c0);
+    const int m = n - k;                           // rows k .. n-1
+    const int wv = min(kPanel, m);                 // reflectors of the panel
+    const float *Hm = H + mat * (int64_t)n * n;
     const float *Vbase = Hm + (int64_t)k * n + k;   // V(r, j) at Vbase[j * n + r]
 
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + kOffBar);  // [kStages]
@@ -175,11 +181,11 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
             tc::mbar_expect_tx(&full[s], kStageBytes + (s == 0 ? 4096u : 0u));
             tc::tma_load_3d(st, &tmC, k + s * kRC, c0, (int)mat, &full[s]);
             tc::tma_load_3d(st + kCBytes, &tmV, k + s * kRC, k, (int)mat, &full[s]);
-            if (s == 0) tc::bulk_load(smem + kOffT, Sws + mat * (kPanel * kPanel), 4096u, &full[0]);
+            if (s == 0) tc::bulk_load(smem + kOffT, Sws + mat * s_stride, 4096u, &full[0]);
         }
     }
     float tau_r = 0.0f;
-    if (tid < kPanel) tau_r = tau[mat * n + k + tid];  // stored to shared memory after phase A
+    if (tid < wv) tau_r = tau[mat * n + k + tid];  // stored to shared memory after phase A
     if (warp == 0) {
         tc::tmem_alloc(tmem_slot, kTmemCols);
         tc::tmem_relinquish();
@@ -267,7 +273,7 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
         if (tid == 0)
             for (int u = 0; u < 2 && u < nq; ++u) load_quarter(u);
         q_loads = nq < 2 ? nq : 2;
-        load_v_rows(Vbase, n, 0, m, tid, e);
+        load_v_rows(Vbase, n, 0, m, wv, tid, e);
     }
 
     // ---- phase B: Y = T^T W, thread = tile column c ------------------------
@@ -277,15 +283,28 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
         tc::tmem_ld_32x32(tmem + ((uint32_t)(32 * warp) << 16) + kDA, w);
         tc::tmem_ld_wait();
         const int c = 32 * warp + lane;
-        // Y = T^T W with T = D (I + S D)^-1: forward substitution
-        //   y_c = tau_c (w_c - sum_{l < c} S(l, c) y_l)
+        // T = D (I + S D)^-1 with D = diag(tau), S = strict_upper(V^T V).
         float y[32];
+        if constexpr (ApplyT) {
+            // Y = T^T W (apply H^T): (I + D S^T) Y = D W, forward substitution
+            //   y_c = tau_c (w_c - sum_{l < c} S(l, c) y_l)
 #pragma unroll
-        for (int cc = 0; cc < 32; ++cc) {
-            float a = w[cc];
+            for (int cc = 0; cc < 32; ++cc) {
+                float a = w[cc];
 #pragma unroll
-            for (int l = 0; l < cc; ++l) a = fmaf(-Ts[cc * 32 + l], y[l], a);
-            y[cc] = taus[cc] * a;
+                for (int l = 0; l < cc; ++l) a = fmaf(-Ts[cc * 32 + l], y[l], a);
+                y[cc] = taus[cc] * a;
+            }
+        } else {
+            // Y = T W (apply H): (I + S D) Z = W, Y = D Z, back substitution
+            //   y_c = tau_c (w_c - sum_{l > c} S(c, l) y_l)
+#pragma unroll
+            for (int cc = 31; cc >= 0; --cc) {
+                float a = w[cc];
+#pragma unroll
+                for (int l = cc + 1; l < 32; ++l) a = fmaf(-Ts[l * 32 + cc], y[l], a);
+                y[cc] = taus[cc] * a;
+            }
         }
         // Y as the K-major B operand of phase C: core (c/8, j/4) at
         // ((c/8) * 8 + j/4) * 128 bytes, column c%8 at +16 * (c%8)
@@ -331,7 +350,7 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
     if (ok) {
         ok = !__syncthreads_or(false);  // Y and V(0) staged
         issue_c(0);
-        if (ncc > 1) load_v_rows(Vbase, n, kRCC, m, tid, e);
+        if (ncc > 1) load_v_rows(Vbase, n, kRCC, m, wv, tid, e);
     }
     for (int j = 0; j < ncc && ok; ++j) {
         const bool done = tc::mbar_wait(cbar, c_waited & 1u, kWaitLimit);
@@ -343,7 +362,7 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
         ok = !__syncthreads_or(!done);
         if (!ok) break;
         if (j + 1 < ncc) issue_c(j + 1);
-        if (j + 2 < ncc) load_v_rows(Vbase, n, (j + 2) * kRCC, m, tid, e);
+        if (j + 2 < ncc) load_v_rows(Vbase, n, (j + 2) * kRCC, m, wv, tid, e);
         tc::fence_after_sync();
         const uint32_t pc = tmem + ((uint32_t)(32 * warp) << 16) + ((j & 1) ? kDP1 : kDP0);
         // epilogue: thread = row j * 128 + tid of the tile
@@ -429,45 +448,61 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder()
 
 }  // namespace
 
-cudaError_t prepare_trailing_tc(float *H, int64_t batch, int n, TrailingMaps *maps)
+cudaError_t prepare_apply_maps(const float *H, int n, float *C, int64_t c_cols, int64_t batch,
+                               TrailingMaps *maps)
 {
     PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
     if (!enc) return cudaErrorNotSupported;
-    // H as a 3-D tensor: x = row (contiguous), y = column, z = matrix
-    const cuuint64_t dims[3] = {(cuuint64_t)n, (cuuint64_t)n, (cuuint64_t)batch};
-    const cuuint64_t strides[2] = {(cuuint64_t)n * 4, (cuuint64_t)n * (cuuint64_t)n * 4};
+    // H and C as 3-D tensors: x = row (contiguous), y = column, z = matrix
+    const cuuint64_t hdims[3] = {(cuuint64_t)n, (cuuint64_t)n, (cuuint64_t)batch};
+    const cuuint64_t hstrides[2] = {(cuuint64_t)n * 4, (cuuint64_t)n * (cuuint64_t)n * 4};
+    const cuuint64_t cdims[3] = {(cuuint64_t)n, (cuuint64_t)c_cols, (cuuint64_t)batch};
+    const cuuint64_t cstrides[2] = {(cuuint64_t)n * 4, (cuuint64_t)n * (cuuint64_t)c_cols * 4};
     const cuuint32_t box_c[3] = {kRC, kTN, 1}, box_v[3] = {kRC, kPanel, 1}, unit[3] = {1, 1, 1};
     const cuuint32_t box_cq[3] = {kRCC, kCQCols, 1};
-    if (enc(&maps->c, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, H, dims, strides, box_c, unit,
+    if (enc(&maps->c, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, C, cdims, cstrides, box_c, unit,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS ||
-        enc(&maps->v, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, H, dims, strides, box_v, unit,
+        enc(&maps->v, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(H), hdims, hstrides, box_v, unit,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS ||
-        enc(&maps->cq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, H, dims, strides, box_cq, unit,
+        enc(&maps->cq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, C, cdims, cstrides, box_cq, unit,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return cudaErrorInvalidValue;
     return cudaSuccess;
 }
 
-cudaError_t launch_trailing_tc(const TrailingMaps &maps, float *H, const float *Sws, const float *tau,
-                               int *status, int64_t batch, int n, int k, cudaStream_t st)
+cudaError_t prepare_trailing_tc(float *H, int64_t batch, int n, TrailingMaps *maps)
 {
-    const int nc = n - k - kPanel;
-    if (nc <= 0) return cudaSuccess;
-    cudaError_t e = cudaFuncSetAttribute(trailing_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kSmem);
+    return prepare_apply_maps(H, n, H, n, batch, maps);
+}
+
+cudaError_t launch_apply_tc(const TrailingMaps &maps, const float *H, const float *Sws, int64_t s_stride,
+                            const float *tau, int *status, int64_t batch, int n, int k, int c_begin,
+                            int c_end, bool apply_t, cudaStream_t st)
+{
+    if (c_end <= c_begin || k >= n) return cudaSuccess;
+    auto kern = apply_t ? trailing_tc_kernel<true> : trailing_tc_kernel<false>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
     if (e != cudaSuccess) return e;
-    const unsigned tiles = (unsigned)((nc + kTN - 1) / kTN);
+    const unsigned tiles = (unsigned)((c_end - c_begin + kTN - 1) / kTN);
     for (int64_t b0 = 0; b0 < batch; b0 += 65535) {
         const int64_t nb = (batch - b0) < 65535 ? (batch - b0) : 65535;
         dim3 grid(tiles, (unsigned)nb);
-        trailing_tc_kernel<<<grid, kThreads, kSmem, st>>>(maps.c, maps.v, maps.cq, H, Sws, tau, status, n, k, b0);
+        kern<<<grid, kThreads, kSmem, st>>>(maps.c, maps.v, maps.cq, H, Sws, s_stride, tau, status, n, k,
+                                            c_begin, c_end, b0);
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;
+}
+
+cudaError_t launch_trailing_tc(const TrailingMaps &maps, float *H, const float *Sws, const float *tau,
+                               int *status, int64_t batch, int n, int k, cudaStream_t st)
+{
+    if (n - k - kPanel <= 0) return cudaSuccess;
+    return launch_apply_tc(maps, H, Sws, kPanel * kPanel, tau, status, batch, n, k, k + kPanel, n, true, st);
 }
 
 }  // namespace fqr

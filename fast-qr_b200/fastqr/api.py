@@ -101,6 +101,78 @@ def geqrf(a: torch.Tensor, *, out: tuple[torch.Tensor, torch.Tensor] | None = No
     return h, tau
 
 
+def _colmajor(t: torch.Tensor) -> torch.Tensor:
+    """The batch with each matrix column-major (strides (rows*cols, 1, rows)), a copy if needed."""
+    b, r, c = t.shape
+    if t.stride() == (r * c, 1, r):
+        return t
+    return t.transpose(1, 2).contiguous().transpose(1, 2)
+
+
+def _check_factors(h: torch.Tensor, tau: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    h = _check_input(h)
+    batch, n, _ = h.shape
+    if tau.device != h.device or tau.dtype != torch.float32 or tuple(tau.shape[-1:]) != (n,):
+        raise ValueError("tau must be a float32 (batch, n) tensor on H's device")
+    return _colmajor(h), tau.reshape(batch, n).contiguous()
+
+
+def orgqr_workspace_bytes(batch: int, n: int) -> int:
+    return int(load().fqr_orgqr_workspace_bytes(batch, n))
+
+
+def householder_product(h: torch.Tensor, tau: torch.Tensor, *, workspace: torch.Tensor | None = None
+                        ) -> torch.Tensor:
+    """Q = H_0 H_1 ... H_{n-1} from geqrf's compact (H, tau), as
+    ``torch.linalg.householder_product(H, tau)`` for square float32 CUDA
+    batches (``fqr_orgqr_f32``).  Q is returned column-major per matrix."""
+    squeeze = h.ndim == 2
+    h, tau = _check_factors(h, tau)
+    batch, n, _ = h.shape
+    q = torch.empty_strided((batch, n, n), (n * n, 1, n), device=h.device, dtype=torch.float32)
+    lib = load()
+    need = int(lib.fqr_orgqr_workspace_bytes(batch, n))
+    if need and workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=h.device)
+    ws_ptr = workspace.data_ptr() if need else None
+    with torch.cuda.device(h.device):
+        stream = torch.cuda.current_stream(h.device).cuda_stream
+        rc = lib.fqr_orgqr_f32(h.data_ptr(), tau.data_ptr(), batch, n, q.data_ptr(), ws_ptr, need, stream)
+    if rc:
+        raise FastQRError(rc, "fqr_orgqr_f32")
+    return q[0] if squeeze else q
+
+
+def ormqr(h: torch.Tensor, tau: torch.Tensor, c: torch.Tensor, *, transpose: bool = False,
+          workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Q C (or Q^T C with ``transpose=True``) for the Q of geqrf's (H, tau), as
+    ``torch.ormqr(H, tau, C, left=True, transpose=transpose)`` for square
+    float32 CUDA batches (``fqr_ormqr_f32``).  C: (batch, n, ncols); the result
+    is a new column-major tensor."""
+    squeeze = h.ndim == 2
+    h, tau = _check_factors(h, tau)
+    batch, n, _ = h.shape
+    if c.ndim == 2:
+        c = c.unsqueeze(0)
+    if c.device != h.device or c.dtype != torch.float32 or c.ndim != 3 or c.shape[:2] != (batch, n):
+        raise ValueError("C must be a float32 (batch, n, ncols) tensor on H's device")
+    ncols = c.shape[2]
+    out = torch.empty_strided((batch, n, ncols), (n * ncols, 1, n), device=c.device, dtype=torch.float32)
+    out.copy_(c)
+    lib = load()
+    need = int(lib.fqr_orgqr_workspace_bytes(batch, n))
+    if need and workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=h.device)
+    ws_ptr = workspace.data_ptr() if need else None
+    with torch.cuda.device(h.device):
+        stream = torch.cuda.current_stream(h.device).cuda_stream
+        rc = lib.fqr_ormqr_f32(h.data_ptr(), tau.data_ptr(), batch, n, out.data_ptr(), ncols,
+                               1 if transpose else 0, ws_ptr, need, stream)
+    if rc:
+        raise FastQRError(rc, "fqr_ormqr_f32")
+    return out[0] if squeeze else out
+
+
 def host_workspace_bytes(batch: int, n: int) -> int:
     return int(load().fqr_host_workspace_bytes(batch, n))
 

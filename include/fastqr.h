@@ -144,6 +144,32 @@ int fqr_host_check_status(const void *workspace, size_t workspace_bytes, int64_t
                           void *stream);
 
 /*
+ * Q of a factorisation in compact form, Q = H_0 H_1 ... H_{n-1} with
+ * H_j = I - tau_j v_j v_j^T (v_j read from below the diagonal of column j of
+ * H, unit diagonal implied).  H and tau as fqr_geqrf_f32 returns them (device
+ * pointers; H column-major per matrix, tau [batch][n]); Q: batch x n x n,
+ * column-major like H.  workspace: fqr_orgqr_workspace_bytes(batch, n) bytes
+ * (0 when n % 4 != 0 or n < 128: those sizes, up to n = 512, take a
+ * reflector-by-reflector kernel; larger such n return FQR_EUNSUPPORTED).
+ * Replaces the reference's use of torch.linalg.householder_product in its
+ * checker (official/reference.py:199).
+ */
+size_t fqr_orgqr_workspace_bytes(int64_t batch, int64_t n);
+int fqr_orgqr_f32(const float *H, const float *tau, int64_t batch, int64_t n, float *Q,
+                  void *workspace, size_t workspace_bytes, void *stream);
+
+/*
+ * C := Q^T C (transpose != 0) or C := Q C, in place, for the Q of (H, tau)
+ * as in fqr_orgqr_f32.  C: batch x n x ncols, column-major per matrix
+ * (element (i, j) of matrix b at C[b*n*ncols + j*n + i]), device pointer.
+ * workspace: fqr_orgqr_workspace_bytes(batch, n) bytes.  Replaces the
+ * reference's torch.ormqr calls (submissions/candidate.py:7224-7242), left
+ * side.
+ */
+int fqr_ormqr_f32(const float *H, const float *tau, int64_t batch, int64_t n, float *C, int64_t ncols,
+                  int transpose, void *workspace, size_t workspace_bytes, void *stream);
+
+/*
  * Synchronizes `stream`, then reports whether the last fqr_geqrf_f32 that
  * used `workspace` (for `batch` matrices) hit a bounded device-side wait that
  * gave up: FQR_OK or FQR_ETIMEOUT.  The tensor-core kernels never spin

@@ -112,3 +112,19 @@ def test_host_api_rejects_cuda_tensors_and_bad_dtypes():
     import torch
     with pytest.raises(ValueError):
         fastqr.geqrf_host(torch.zeros(2, 8, 8, dtype=torch.float64))
+
+
+def test_orgqr_ormqr_validation_without_gpu():
+    lib = fastqr.load()
+    dummy = ctypes.c_void_p(256)
+    assert lib.fqr_orgqr_f32(None, None, -1, 8, None, None, 0, None) == 1
+    assert lib.fqr_orgqr_f32(None, None, 0, 8, None, None, 0, None) == 0
+    assert lib.fqr_orgqr_f32(dummy, dummy, 1, 8193, dummy, None, 0, None) == 2
+    # tensor-core sizes need the S workspace; odd sizes above 512 are unsupported
+    assert lib.fqr_orgqr_f32(dummy, dummy, 2, 256, dummy, None, 0, None) == 5
+    assert lib.fqr_orgqr_f32(dummy, dummy, 2, 514, dummy, None, 0, None) == 2
+    assert lib.fqr_ormqr_f32(dummy, dummy, 2, 256, dummy, 10, 1, None, 0, None) == 5
+    assert lib.fqr_ormqr_f32(None, dummy, 2, 256, dummy, 10, 1, None, 0, None) == 1
+    # one 32 x 32 S block per panel per matrix + a status block
+    assert fastqr.orgqr_workspace_bytes(16, 4096) == 16 * 128 * 4096 + 256
+    assert fastqr.orgqr_workspace_bytes(3, 100) == 0
