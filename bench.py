@@ -397,6 +397,107 @@ def end_to_end(a, n, batch, dev, steps) -> dict:
     return {"ms": ms, "h2d": batch * n * n * 4, "d2h": batch * (n * n + n) * 4}
 
 
+def run_apply_op(args) -> int:
+    """--op orgqr | ormqr: Q formation (householder_product) or Q^T C (ormqr,
+    C = A, i.e. the n x n input batch) from factors made by fastqr.geqrf
+    outside the timed region; one process, N=1 only."""
+    import fastqr
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = inputs.CONFIGS[args.config]
+    n, batch = cfg["n"], cfg["batch"]
+    steps = args.steps
+    a = inputs.baseline_input(args.config, args.seed, dev)
+    h, tau = fastqr.geqrf(a)
+    ws = torch.empty(max(1, fastqr.orgqr_workspace_bytes(batch, n)), dtype=torch.uint8, device=dev)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+
+    # outputs allocated once: Q, or the column-major copy of A that ormqr
+    # overwrites with Q^T A (the copy is part of the op)
+    res = torch.empty_strided((batch, n, n), (n * n, 1, n), device=dev, dtype=torch.float32)
+
+    def step():
+        if args.op == "orgqr":
+            return fastqr.householder_product(h, tau, out=res, workspace=ws)
+        return fastqr.ormqr(h, tau, a, transpose=True, out=res, workspace=ws)
+
+    for _ in range(args.warmup):
+        out = step()
+    torch.cuda.synchronize(dev)
+    # correctness (untimed): Q orthogonal and Q R = A, or Q^T A = R
+    chk = min(batch, 8)
+    r = torch.triu(h[:chk])
+    if args.op == "orgqr":
+        q = out[:chk]
+        eye = torch.eye(n, device=dev)
+        e1 = float((torch.linalg.matrix_norm(q.transpose(1, 2) @ q - eye) / n ** 0.5).max())
+        e2 = float((torch.linalg.matrix_norm(a[:chk] - q @ r) / torch.linalg.matrix_norm(a[:chk])).max())
+        gate = {"orth_rel_f": e1, "recon_rel_f": e2}
+        ok = e1 <= 1e-4 and e2 <= 1e-4
+    else:
+        e1 = float((torch.linalg.matrix_norm(out[:chk] - r) / torch.linalg.matrix_norm(r)).max())
+        gate = {"qta_minus_r_rel_f": e1}
+        ok = e1 <= 1e-4
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    stream = torch.cuda.current_stream(dev)
+    torch.cuda.synchronize(dev)
+    with ClockSampler(0) as clk:
+        for i in range(steps):
+            flush.fill_(float(i))
+            starts[i].record(stream)
+            step()
+            ends[i].record(stream)
+        torch.cuda.synchronize(dev)
+    clocks = clk.summary()
+    ms = sum(s_.elapsed_time(e_) for s_, e_ in zip(starts, ends)) / steps
+    mps = batch / (ms / 1e3)
+    # Householder application: 4n^3/3 flops per matrix for either op on square C
+    alg = batch * flops_per_matrix(n)
+    pk = peaks()
+    tf32 = pk["bf16_tflops"] / 2.0
+    ach = alg / (ms / 1e3) / 1e12
+    cpu = None
+    if not args.no_cpu:
+        threads = os.cpu_count() or 1
+        torch.set_num_threads(threads)
+        hc, tc = h[:min(batch, 32)].cpu(), tau[:min(batch, 32)].cpu()
+        ac = a[:hc.shape[0]].cpu()
+        fn = (lambda: torch.linalg.householder_product(hc, tc)) if args.op == "orgqr" else \
+             (lambda: torch.ormqr(hc, tc, ac, left=True, transpose=True))
+        fn()
+        times = []
+        t_start = time.perf_counter()
+        while len(times) < 3 or time.perf_counter() - t_start < 5.0:
+            t0 = time.perf_counter()
+            fn()
+            times.append(time.perf_counter() - t0)
+            if time.perf_counter() - t_start > 20.0:
+                break
+        per = statistics.median(times)
+        name = "torch.linalg.householder_product" if args.op == "orgqr" else "torch.ormqr"
+        cpu = {"value": hc.shape[0] / per, "unit": "matrices/s", "cores": threads, "kind": "reference",
+               "sample": f"{name} (host LAPACK) on {hc.shape[0]} of the {batch} {n}x{n} factorisations, "
+                         f"median of {len(times)} reps"}
+    launches = 1 + (2 + (n + 31) // 32 if fastqr.orgqr_workspace_bytes(batch, n) else 1)
+    line = {
+        "metric": f"matrices/s ({args.config} {args.op})", "value": mps, "unit": "matrices/s", "n_gpus": 1,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded, the reference generator's distributions); factors from fastqr.geqrf",
+        "config": {"workload": f"{args.config}: {cfg['desc']}", "op": args.op, "n": n, "batch_per_gpu": batch,
+                   "l2": f"flushed before every step ({L2_FLUSH_BYTES >> 20} MiB write)"},
+        "verified": ok, "gate": gate,
+        "roofline": {"kernel": "apply (whole op)", "bound": "tensor", "achieved": ach, "peak": tf32,
+                     "unit": "TFLOP/s", "frac": ach / tf32, "traffic": None,
+                     "peak_source": pk["source"] + "; TF32 dense peak taken as measured bf16 / 2"},
+        "cpu_baseline": cpu, "e2e": None, "gpu_launches": steps * launches, "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+    return 0 if ok else 1
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -406,12 +507,16 @@ def main() -> int:
     ap.add_argument("--impl", default="fastqr", choices=["fastqr", "reference"])
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--op", default="geqrf", choices=["geqrf", "orgqr", "ormqr"],
+                    help="geqrf (the headline); orgqr / ormqr time Q formation / Q^T A from geqrf's factors")
     args = ap.parse_args()
     if args.steps is None:
         args.steps = DEFAULT_STEPS[args.config]
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         return run_reference(args)
+    if args.op != "geqrf":
+        return run_apply_op(args)
     return run_fastqr(args)
 
 

@@ -117,24 +117,40 @@ def _check_factors(h: torch.Tensor, tau: torch.Tensor) -> tuple[torch.Tensor, to
     return _colmajor(h), tau.reshape(batch, n).contiguous()
 
 
+def _apply_workspace(lib, batch, n, workspace, device):
+    """(pointer, bytes) of the S-block workspace for orgqr/ormqr; allocated when not given."""
+    need = int(lib.fqr_orgqr_workspace_bytes(batch, n))
+    if not need:
+        return None, 0
+    if workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=device)
+    elif workspace.numel() * workspace.element_size() < need or workspace.device != device:
+        raise ValueError(f"workspace needs {need} bytes on {device}")
+    return workspace.data_ptr(), workspace.numel() * workspace.element_size()
+
+
 def orgqr_workspace_bytes(batch: int, n: int) -> int:
     return int(load().fqr_orgqr_workspace_bytes(batch, n))
 
 
-def householder_product(h: torch.Tensor, tau: torch.Tensor, *, workspace: torch.Tensor | None = None
-                        ) -> torch.Tensor:
+def householder_product(h: torch.Tensor, tau: torch.Tensor, *, out: torch.Tensor | None = None,
+                        workspace: torch.Tensor | None = None) -> torch.Tensor:
     """Q = H_0 H_1 ... H_{n-1} from geqrf's compact (H, tau), as
     ``torch.linalg.householder_product(H, tau)`` for square float32 CUDA
-    batches (``fqr_orgqr_f32``).  Q is returned column-major per matrix."""
+    batches (``fqr_orgqr_f32``).  Q is returned column-major per matrix
+    (``out``, when given, must be such a tensor)."""
     squeeze = h.ndim == 2
     h, tau = _check_factors(h, tau)
     batch, n, _ = h.shape
-    q = torch.empty_strided((batch, n, n), (n * n, 1, n), device=h.device, dtype=torch.float32)
+    if out is None:
+        q = torch.empty_strided((batch, n, n), (n * n, 1, n), device=h.device, dtype=torch.float32)
+    else:
+        q = out.unsqueeze(0) if out.ndim == 2 else out
+        if q.shape != (batch, n, n) or q.stride() != (n * n, 1, n) or q.dtype != torch.float32 \
+                or q.device != h.device:
+            raise ValueError("out must be float32 (batch, n, n) with strides (n*n, 1, n) on H's device")
     lib = load()
-    need = int(lib.fqr_orgqr_workspace_bytes(batch, n))
-    if need and workspace is None:
-        workspace = torch.empty(need, dtype=torch.uint8, device=h.device)
-    ws_ptr = workspace.data_ptr() if need else None
+    ws_ptr, need = _apply_workspace(lib, batch, n, workspace, h.device)
     with torch.cuda.device(h.device):
         stream = torch.cuda.current_stream(h.device).cuda_stream
         rc = lib.fqr_orgqr_f32(h.data_ptr(), tau.data_ptr(), batch, n, q.data_ptr(), ws_ptr, need, stream)
@@ -144,11 +160,12 @@ def householder_product(h: torch.Tensor, tau: torch.Tensor, *, workspace: torch.
 
 
 def ormqr(h: torch.Tensor, tau: torch.Tensor, c: torch.Tensor, *, transpose: bool = False,
-          workspace: torch.Tensor | None = None) -> torch.Tensor:
+          out: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
     """Q C (or Q^T C with ``transpose=True``) for the Q of geqrf's (H, tau), as
     ``torch.ormqr(H, tau, C, left=True, transpose=transpose)`` for square
     float32 CUDA batches (``fqr_ormqr_f32``).  C: (batch, n, ncols); the result
-    is a new column-major tensor."""
+    is a column-major tensor (``out`` when given: column-major, and C itself
+    for an in-place update)."""
     squeeze = h.ndim == 2
     h, tau = _check_factors(h, tau)
     batch, n, _ = h.shape
@@ -157,13 +174,17 @@ def ormqr(h: torch.Tensor, tau: torch.Tensor, c: torch.Tensor, *, transpose: boo
     if c.device != h.device or c.dtype != torch.float32 or c.ndim != 3 or c.shape[:2] != (batch, n):
         raise ValueError("C must be a float32 (batch, n, ncols) tensor on H's device")
     ncols = c.shape[2]
-    out = torch.empty_strided((batch, n, ncols), (n * ncols, 1, n), device=c.device, dtype=torch.float32)
-    out.copy_(c)
+    if out is None:
+        out = torch.empty_strided((batch, n, ncols), (n * ncols, 1, n), device=c.device, dtype=torch.float32)
+    else:
+        out = out.unsqueeze(0) if out.ndim == 2 else out
+        if out.shape != (batch, n, ncols) or out.stride() != (n * ncols, 1, n) or out.dtype != torch.float32 \
+                or out.device != c.device:
+            raise ValueError("out must be float32 (batch, n, ncols) with strides (n*ncols, 1, n) on C's device")
+    if out.data_ptr() != c.data_ptr():
+        out.copy_(c)
     lib = load()
-    need = int(lib.fqr_orgqr_workspace_bytes(batch, n))
-    if need and workspace is None:
-        workspace = torch.empty(need, dtype=torch.uint8, device=h.device)
-    ws_ptr = workspace.data_ptr() if need else None
+    ws_ptr, need = _apply_workspace(lib, batch, n, workspace, h.device)
     with torch.cuda.device(h.device):
         stream = torch.cuda.current_stream(h.device).cuda_stream
         rc = lib.fqr_ormqr_f32(h.data_ptr(), tau.data_ptr(), batch, n, out.data_ptr(), ncols,
