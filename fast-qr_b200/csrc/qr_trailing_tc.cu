@@ -74,7 +74,6 @@ constexpr int kOffYlo = 49152;
 constexpr int kOffCQ = 65536;
 constexpr int kCQCols = 32;
 constexpr int kCQBytes = kRCC * kCQCols * 4;  // 16 KB
-constexpr int kQuarters = kTN / kCQCols;
 static_assert(kOffCQ + 2 * kCQBytes <= kOffT, "phase-C buffers overlap S");
 static_assert(kStageBytes % 1024 == 0 && kCBytes % 1024 == 0, "swizzle atoms need 1024-byte alignment");
 
@@ -259,14 +258,23 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
 
     // ---- phase C set-up: the first two C quarters start streaming now
     const int ncc = (m + kRCC - 1) / kRCC;
-    const int nq = ncc * kQuarters;  // C quarters of the tile, in order (chunk, quarter)
+    // quarters per chunk that hold tile columns: a tile narrower than kTN (the
+    // end of [c_begin, c_end)) must not store the quarters beyond c_end
+    const int nqc = (nct + kCQCols - 1) / kCQCols;
+    const int nq = ncc * nqc;        // C quarters of the tile, in order (chunk, quarter)
     int q_loads = 0;                 // quarters whose TMA load was issued
     int q_used[2] = {0, 0};          // quarters consumed per ring buffer
+    // the loads go in order u = 0, 1, ...: (chunk, quarter) of the next one
+    // as running counters (thread 0)
+    int ld_chunk = 0, ld_q = 0;
     auto load_quarter = [&](int u) {  // thread 0
         unsigned char *cs = smem + kOffCQ + (u & 1) * kCQBytes;
         tc::mbar_expect_tx(&cfull[u & 1], kCQBytes);
-        tc::tma_load_3d(cs, &tmCQ, k + kRCC * (u / kQuarters), c0 + kCQCols * (u % kQuarters), (int)mat,
-                        &cfull[u & 1]);
+        tc::tma_load_3d(cs, &tmCQ, k + kRCC * ld_chunk, c0 + kCQCols * ld_q, (int)mat, &cfull[u & 1]);
+        if (++ld_q == nqc) {
+            ld_q = 0;
+            ++ld_chunk;
+        }
     };
     float e[kPanel];  // V rows of the next phase-C chunk
     if (ok) {
@@ -366,8 +374,8 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
         tc::fence_after_sync();
         const uint32_t pc = tmem + ((uint32_t)(32 * warp) << 16) + ((j & 1) ? kDP1 : kDP0);
         // epilogue: thread = row j * 128 + tid of the tile
-        for (int q = 0; q < kQuarters; ++q) {
-            const int u = j * kQuarters + q, b = u & 1;
+        for (int q = 0; q < nqc; ++q) {
+            const int u = j * nqc + q, b = u & 1;
             const bool landed = tc::mbar_wait(&cfull[b], (uint32_t)q_used[b] & 1u, kWaitLimit);
             if (landed) ++q_used[b];
             float pv[32];

@@ -111,3 +111,15 @@ def test_row_major_factors_and_errors(dev):
         fastqr.householder_product(hb, torch.zeros(1, 514, device=dev))
     with pytest.raises(ValueError):
         fastqr.ormqr(h, tau, torch.zeros(2, 127, 3, device=dev))
+
+
+def test_column_range_update_leaves_other_columns(dev):
+    """ormqr on a C wider than one 128-column tile but not a multiple of 32
+    columns: every column is updated and none is written twice (the update
+    kernel stores only the quarters of its column range)."""
+    a, h, tau = factor(1, 256, 0, 21, dev)
+    c = torch.randn(1, 256, 200, device=dev)
+    out = fastqr.ormqr(h, tau, c, transpose=True)
+    q64 = oracle.orgqr_f64(h.cpu().numpy(), tau.cpu().numpy())
+    want = np.transpose(q64, (0, 2, 1)) @ c.cpu().double().numpy()
+    assert frob(out.cpu().double().numpy() - want) / frob(want) <= 1e-5
