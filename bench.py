@@ -58,6 +58,13 @@ def bytes_per_matrix(n: int) -> float:
     return 4.0 * (2 * n * n + n)
 
 
+def panel_bytes(n: int, b: int = 32) -> float:
+    """Algorithmic HBM bytes of all panel launches of one matrix: per panel k
+    the (n-k) x b column block is read and written back, and b tau values and
+    the b x b S block are written."""
+    return sum(8.0 * b * (n - k) + 4.0 * b + 4.0 * b * b for k in range(0, n, b))
+
+
 def trailing_flops(n: int, b: int = 32) -> float:
     """Algorithmic flops of all trailing updates of one matrix:
     per panel k: 4 (n-k) b (n-k-b) + b^2 (n-k-b)."""
@@ -338,17 +345,17 @@ def kernel_roofline(cfg_name, a, h, tau, ws, flush, steps, dev) -> dict:
     share = {kname: round(v / max(sum(per_step_ms.values()), 1e-12), 4) for kname, v in per_step_ms.items()}
     base = {"kernel": dom, "stage_ms_per_step": per_step_ms, "stage_share": share,
             "traffic": traffic, "peak_source": pk["source"]}
-    if dom in ("small", "copy_in"):
-        alg = batch * bytes_per_matrix(n) if dom == "small" else batch * 8.0 * n * n
+    if dom in ("small", "copy_in", "panel"):
+        # the panel does O(m b^2) flops on O(m b) data: it is framed by HBM
+        # bytes, and its limiter is the column-by-column dependency chain
+        alg = batch * {"small": bytes_per_matrix(n), "copy_in": 8.0 * n * n,
+                       "panel": panel_bytes(n)}[dom]
         ach = alg / t / 1e9
         base.update({"bound": "hbm", "achieved": ach, "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": ach / pk["hbm_gbs"], "alg_bytes_per_step": alg})
         return base
     tf32 = pk["bf16_tflops"] / 2.0
-    if dom == "trailing":
-        alg = batch * trailing_flops(n)
-    else:
-        alg = batch * (flops_per_matrix(n) - trailing_flops(n))
+    alg = batch * trailing_flops(n)
     ach = alg / t / 1e12
     base.update({"bound": "tensor", "achieved": ach, "peak": tf32, "unit": "TFLOP/s",
                  "frac": ach / tf32, "alg_flops_per_step": alg,

@@ -66,9 +66,14 @@ int fqr_launch_count(int64_t batch, int64_t n)
     if (n > FQR_MAX_N) return -1;
     if (small_path(n)) return 1;
     const int64_t panels = (n + fqr::kPanel - 1) / fqr::kPanel;
-    const int64_t chunks = (batch + 65534) / 65535;
     // copy-in + per panel (panel + trailing), the last panel has no trailing
-    return (int)(1 + panels + (panels - 1) * chunks);
+    auto range = [panels](int64_t b) {
+        const int64_t chunks = (b + 65534) / 65535;
+        return 1 + panels + (panels - 1) * chunks;
+    };
+    // a batch of two or more runs as two halves on two streams
+    if (batch >= 2) return (int)(range(batch / 2) + range(batch - batch / 2));
+    return (int)range(batch);
 }
 
 int fqr_plan_describe(int64_t batch, int64_t n, char *buf, size_t len)

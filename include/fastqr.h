@@ -88,7 +88,8 @@ const char *fqr_status_string(int status);
  * submissions/candidate.py:7779-8381, is deliberately absent). */
 int fqr_plan_describe(int64_t batch, int64_t n, char *buf, size_t len);
 
-/* Number of kernel launches fqr_geqrf_f32 enqueues for (batch, n). */
+/* Number of kernel launches fqr_geqrf_f32 enqueues for (batch, n), counting
+ * both halves of a batch of two or more on the blocked path (n > 64). */
 int fqr_launch_count(int64_t batch, int64_t n);
 
 /* Largest batch fqr_geqrf_f32_noalloc accepts when n > 64 (its static

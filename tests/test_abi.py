@@ -66,7 +66,9 @@ def test_workspace_and_plan_depend_on_shape_only():
     with pytest.raises(fastqr.FastQRError):
         fastqr.plan(1, 10000)
     assert fastqr.launch_count(1024, 32) == 1
-    assert fastqr.launch_count(256, 256) == 1 + 8 + 7
+    # two halves of a batch on two streams, each copy-in + 8 panels + 7 trailing
+    assert fastqr.launch_count(256, 256) == 2 * (1 + 8 + 7)
+    assert fastqr.launch_count(1, 256) == 1 + 8 + 7
 
 
 def test_python_api_rejects_cpu_tensors():
