@@ -343,8 +343,11 @@ def kernel_roofline(cfg_name, a, h, tau, ws, flush, steps, dev) -> dict:
     t = per_step_ms[dom] / 1e3
     traffic = _traffic_from_profiles(cfg_name, dom)
     share = {kname: round(v / max(sum(per_step_ms.values()), 1e-12), 4) for kname, v in per_step_ms.items()}
+    # launches of the dominant kernel class per profiled step (one stream)
+    panels = -(-n // 32)
+    per_step = {"small": 1, "copy_in": 1, "panel": panels, "trailing": panels - 1}[dom]
     base = {"kernel": dom, "stage_ms_per_step": per_step_ms, "stage_share": share,
-            "traffic": traffic, "peak_source": pk["source"]}
+            "traffic": traffic, "launches_per_step": per_step, "peak_source": pk["source"]}
     if dom in ("small", "copy_in", "panel"):
         # the panel does O(m b^2) flops on O(m b) data: it is framed by HBM
         # bytes, and its limiter is the column-by-column dependency chain
@@ -352,13 +355,14 @@ def kernel_roofline(cfg_name, a, h, tau, ws, flush, steps, dev) -> dict:
                        "panel": panel_bytes(n)}[dom]
         ach = alg / t / 1e9
         base.update({"bound": "hbm", "achieved": ach, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                     "frac": ach / pk["hbm_gbs"], "alg_bytes_per_step": alg})
+                     "frac": ach / pk["hbm_gbs"], "alg_bytes_per_step": alg,
+                     "alg_bytes_per_launch": alg / per_step})
         return base
     tf32 = pk["bf16_tflops"] / 2.0
     alg = batch * trailing_flops(n)
     ach = alg / t / 1e12
     base.update({"bound": "tensor", "achieved": ach, "peak": tf32, "unit": "TFLOP/s",
-                 "frac": ach / tf32, "alg_flops_per_step": alg,
+                 "frac": ach / tf32, "alg_flops_per_step": alg, "alg_flops_per_launch": alg / per_step,
                  "peak_source": pk["source"] + "; TF32 dense peak taken as measured bf16 / 2"})
     return base
 

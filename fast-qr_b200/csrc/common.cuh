@@ -8,6 +8,15 @@ namespace fqr {
 
 constexpr unsigned kFull = 0xffffffffu;
 
+// Programmatic dependent launch (kernels launched by launch_dependent):
+// pdl_wait blocks the calling thread until every kernel this one depends on
+// has completed and its memory operations are visible (a no-op when the
+// kernel was launched without the attribute); pdl_trigger lets the next
+// kernel on the stream be scheduled once every CTA of this one has issued it
+// or exited -- it carries no memory ordering.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Householder reflector for one column, LAPACK xLARFG semantics
 // (the reference's per-column step: submissions/candidate.py:176-196 in the
 // n=32 kernel, :2084-2098 in the blocked panel).  Given alpha = a(k,k) and

@@ -70,6 +70,31 @@ int geqrf_enqueue_status(const float *A, int64_t batch, int64_t n, int64_t a_bst
                          void *workspace, size_t workspace_bytes, int *status_word,
                          cudaStream_t st);
 
+// Launch with programmatic dependent launch: the kernel may be scheduled
+// while the previous kernel on `st` is still running (once every CTA of that
+// kernel has executed griddepcontrol.launch_dependents or exited) and must
+// execute griddepcontrol.wait (pdl_wait) before it touches memory the
+// previous kernels write or read.  Used only for kernels that do.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_dependent(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                             const cudaLaunchAttribute *extra, int n_extra, Args... args)
+{
+    cudaLaunchAttribute attr[4];
+    int na = 0;
+    for (int i = 0; i < n_extra && na < 3; ++i) attr[na++] = extra[i];
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = (unsigned)na;
+    return cudaLaunchKernelEx(&cfg, kern, ((KArgs)args)...);
+}
+
 // Panel plan for m remaining rows: threads per CTA and cluster size.
 struct PanelShape {
     int warps;

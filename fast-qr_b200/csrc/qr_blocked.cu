@@ -37,6 +37,7 @@ copy_in_rowmajor_kernel(const float *__restrict__ A, int64_t batch, int n, int64
                         float *__restrict__ H, int *__restrict__ status, int clear)
 {
     __shared__ float tile[32][33];
+    pdl_trigger();  // the first panel may be scheduled; it waits for this grid
     if (status && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && threadIdx.x < clear)
         status[threadIdx.x] = 0;
     const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
@@ -65,6 +66,7 @@ __global__ void __launch_bounds__(256)
 copy_in_strided_kernel(const float *__restrict__ A, int64_t batch, int n, int64_t bs, int64_t rs,
                        int64_t cs, float *__restrict__ H, int *__restrict__ status, int clear)
 {
+    pdl_trigger();
     if (status && blockIdx.x == 0 && threadIdx.x < clear) status[threadIdx.x] = 0;
     const int64_t nn = (int64_t)n * n;
     const int64_t total = batch * nn;
@@ -112,6 +114,7 @@ trailing_simt_kernel(float *__restrict__ H, const float *__restrict__ Sws, const
     const int nct = (n - c0) < 32 ? (n - c0) : 32;
     const int m = n - k;
     float *Hm = H + mat * (int64_t)n * n;
+    pdl_wait();  // the panel (and everything before it) has completed
 
     auto load_chunk = [&](int r0) {
         const int rr = r0 + lane;
@@ -166,6 +169,7 @@ trailing_simt_kernel(float *__restrict__ H, const float *__restrict__ Sws, const
 #pragma unroll
     for (int j = 0; j < 32; ++j) yreg[j] = Ws[j][lane];
 
+    pdl_trigger();
     // C -= V Y : staged per 32-row chunk, thread (c = lane, rows tg + 8i)
     for (int r0 = 0; r0 < m; r0 += 32) {
         load_chunk(r0);
@@ -198,9 +202,9 @@ cudaError_t launch_trailing(float *H, const float *Sws, const float *tau, int64_
     for (int64_t b0 = 0; b0 < batch; b0 += 65535) {
         const int64_t nb = (batch - b0) < 65535 ? (batch - b0) : 65535;
         dim3 grid(tiles, (unsigned)nb);
-        trailing_simt_kernel<<<grid, 256, 0, st>>>(H + b0 * (int64_t)n * n, Sws + b0 * kPanel * kPanel,
-                                                   tau + b0 * n, n, k);
-        cudaError_t e = cudaGetLastError();
+        cudaError_t e = launch_dependent(trailing_simt_kernel, grid, dim3(256), 0, st, nullptr, 0,
+                                         H + b0 * (int64_t)n * n, Sws + b0 * kPanel * kPanel, tau + b0 * n,
+                                         n, k);
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;

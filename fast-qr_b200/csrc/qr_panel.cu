@@ -81,6 +81,8 @@ panel_kernel(float *__restrict__ H, float *__restrict__ tau, float *__restrict__
     extern __shared__ float4 panel_stage[];
     float *stg = reinterpret_cast<float *>(panel_stage) + wid * (32 * kStagePitch);
 
+    pdl_wait();  // the previous trailing update (or copy-in) has completed
+
     int row[NR];
     float p[NR][4];
 #pragma unroll
@@ -291,6 +293,7 @@ panel_kernel(float *__restrict__ H, float *__restrict__ tau, float *__restrict__
         }
     }
     __syncthreads();
+    pdl_trigger();  // the trailing update may be scheduled (it waits for this grid)
 
     // The trailing update needs T only through Y = T^T W; since
     // T = D (I + S D)^-1 with D = diag(tau) and S(l, c) = v_l^T v_c (l < c),
@@ -355,27 +358,21 @@ static cudaError_t launch_panel_t(float *H, float *tau, float *Tws, int64_t batc
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);
             if (e != cudaSuccess) return e;
         }
-        panel_kernel<NW, R, false><<<(unsigned)batch, NW * 32, dyn, st>>>(H, tau, Tws, n, k);
-        return cudaGetLastError();
+        return launch_dependent(panel_kernel<NW, R, false>, dim3((unsigned)batch), dim3(NW * 32), dyn, st,
+                                nullptr, 0, H, tau, Tws, n, k);
     }
     if (dyn > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(panel_kernel<NW, R, true>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);
         if (e != cudaSuccess) return e;
     }
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)(batch * cluster), 1, 1);
-    cfg.blockDim = dim3(NW * 32, 1, 1);
-    cfg.dynamicSmemBytes = dyn;
-    cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = (unsigned)cluster;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, panel_kernel<NW, R, true>, H, tau, Tws, n, k);
+    return launch_dependent(panel_kernel<NW, R, true>, dim3((unsigned)(batch * cluster)), dim3(NW * 32), dyn,
+                            st, attr, 1, H, tau, Tws, n, k);
 }
 
 cudaError_t launch_panel(float *H, float *tau, float *Tws, int64_t batch, int n, int k,

@@ -140,7 +140,8 @@ __global__ void __launch_bounds__(kThreads, 2)
 trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmV,
                    const __grid_constant__ CUtensorMap tmCQ, const float *__restrict__ H,
                    const float *__restrict__ Sws, int64_t s_stride, const float *__restrict__ tau,
-                   int *__restrict__ status, int n, int k, int c_begin, int c_end, int64_t b0)
+                   int *__restrict__ status, int n, int k, int c_begin, int c_end, int64_t b0,
+                   int early_trigger)
 {
     extern __shared__ unsigned char smem_raw[];
     const uint32_t raw_addr = tc::smem_addr(smem_raw);
@@ -169,12 +170,23 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
 
     // thread 0: barriers, then the first kStages chunks (and S with chunk 0)
     // start streaming at once
+    // (barriers, tensor-map prefetch and the TMEM allocation overlap the end
+    // of the previous kernel; at most two CTAs of this kernel fit on an SM by
+    // shared memory, so the two 256-column allocations never wait)
     if (tid == 0) {
         tc::prefetch_tensormap(&tmC);
         tc::prefetch_tensormap(&tmV);
         tc::prefetch_tensormap(&tmCQ);
         for (int i = 0; i < kStages + 5; ++i) tc::mbar_init(&full[i], 1);
         tc::fence_mbar_init();
+    }
+    if (warp == 0) {
+        __syncwarp();
+        tc::tmem_alloc(tmem_slot, kTmemCols);
+        tc::tmem_relinquish();
+    }
+    pdl_wait();  // the panel (and everything before it) has completed
+    if (tid == 0) {
         for (int s = 0; s < kStages && s < nchunks; ++s) {
             unsigned char *st = smem + s * kStageBytes;
             tc::mbar_expect_tx(&full[s], kStageBytes + (s == 0 ? 4096u : 0u));
@@ -185,10 +197,6 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
     }
     float tau_r = 0.0f;
     if (tid < wv) tau_r = tau[mat * n + k + tid];  // stored to shared memory after phase A
-    if (warp == 0) {
-        tc::tmem_alloc(tmem_slot, kTmemCols);
-        tc::tmem_relinquish();
-    }
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
@@ -255,6 +263,12 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
     }
     if (tid < kPanel) taus[tid] = tau_r;
     __syncthreads();
+
+    // the next kernel may be scheduled (it waits for this grid): from here
+    // when the launch is large (the next panel's CTAs are placed while this
+    // grid's last wave finishes), else after phase C, so that waiting CTAs do
+    // not hold SMs the other half of a split batch could use
+    if (early_trigger) pdl_trigger();
 
     // ---- phase C set-up: the first two C quarters start streaming now
     const int ncc = (m + kRCC - 1) / kRCC;
@@ -401,6 +415,7 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
         }
         tc::fence_before_sync();
     }
+    if (!early_trigger) pdl_trigger();
     if (tid == 0) tc::bulk_wait_group<0>();  // stores complete before shared memory goes away
 
     if (!ok && tid == 0) {
@@ -498,9 +513,8 @@ cudaError_t launch_apply_tc(const TrailingMaps &maps, const float *H, const floa
     for (int64_t b0 = 0; b0 < batch; b0 += 65535) {
         const int64_t nb = (batch - b0) < 65535 ? (batch - b0) : 65535;
         dim3 grid(tiles, (unsigned)nb);
-        kern<<<grid, kThreads, kSmem, st>>>(maps.c, maps.v, maps.cq, H, Sws, s_stride, tau, status, n, k,
-                                            c_begin, c_end, b0);
-        e = cudaGetLastError();
+        e = launch_dependent(kern, grid, dim3(kThreads), kSmem, st, nullptr, 0, maps.c, maps.v, maps.cq, H, Sws,
+                             s_stride, tau, status, n, k, c_begin, c_end, b0, n > 256 ? 1 : 0);
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;
