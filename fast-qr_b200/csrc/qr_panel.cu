@@ -344,6 +344,10 @@ PanelShape panel_shape(int m)
     if (m <= 256) return {4, 2, 1};
     if (m <= 512) return {8, 2, 1};
     if (m <= 1024) return {16, 2, 1};
+    // taller panels: a cluster of 8-warp CTAs (512 rows each; the 16-warp
+    // shape is register-limited to 128 per thread and spills) up to the
+    // portable cluster size of 8
+    if (m <= 4096) return {8, 2, (m + 511) / 512};
     return {16, 2, (m + 1023) / 1024};
 }
 
@@ -351,21 +355,19 @@ template <int NW, int R>
 static cudaError_t launch_panel_t(float *H, float *tau, float *Tws, int64_t batch, int n, int k,
                                   int cluster, cudaStream_t st)
 {
+    // the limit covers static + dynamic shared memory beyond 48 KB, so it is
+    // raised for every shape rather than from the dynamic size alone
     const size_t dyn = panel_stage_bytes(NW);
     if (cluster <= 1) {
-        if (dyn > 48 * 1024) {
-            cudaError_t e = cudaFuncSetAttribute(panel_kernel<NW, R, false>,
-                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);
-            if (e != cudaSuccess) return e;
-        }
+        cudaError_t e = cudaFuncSetAttribute(panel_kernel<NW, R, false>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);
+        if (e != cudaSuccess) return e;
         return launch_dependent(panel_kernel<NW, R, false>, dim3((unsigned)batch), dim3(NW * 32), dyn, st,
                                 nullptr, 0, H, tau, Tws, n, k);
     }
-    if (dyn > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(panel_kernel<NW, R, true>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);
-        if (e != cudaSuccess) return e;
-    }
+    cudaError_t e = cudaFuncSetAttribute(panel_kernel<NW, R, true>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);
+    if (e != cudaSuccess) return e;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = (unsigned)cluster;
@@ -383,7 +385,7 @@ cudaError_t launch_panel(float *H, float *tau, float *Tws, int64_t batch, int n,
     if (s.warps == 4 && s.rows_per_thread_blocks == 1)
         return launch_panel_t<4, 1>(H, tau, Tws, batch, n, k, 1, st);
     if (s.warps == 4) return launch_panel_t<4, 2>(H, tau, Tws, batch, n, k, 1, st);
-    if (s.warps == 8) return launch_panel_t<8, 2>(H, tau, Tws, batch, n, k, 1, st);
+    if (s.warps == 8) return launch_panel_t<8, 2>(H, tau, Tws, batch, n, k, s.cluster, st);
     return launch_panel_t<16, 2>(H, tau, Tws, batch, n, k, s.cluster, st);
 }
 

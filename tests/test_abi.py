@@ -62,7 +62,7 @@ def test_workspace_and_plan_depend_on_shape_only():
     assert fastqr.workspace_bytes(3, 100) % 256 == 0
     assert fastqr.plan(1024, 32).startswith("small")
     assert fastqr.plan(256, 256).startswith("blocked")
-    assert "cluster 4" in fastqr.plan(16, 4096)
+    assert "cluster 8" in fastqr.plan(16, 4096)
     with pytest.raises(fastqr.FastQRError):
         fastqr.plan(1, 10000)
     assert fastqr.launch_count(1024, 32) == 1

@@ -231,6 +231,20 @@ def test_large_n_properties(n, batch, dev):
     assert g["ok"], g
 
 
+@pytest.mark.parametrize("n", [1100, 2100])
+def test_cluster_panel_columns(n, dev):
+    """Panels taller than 1024 rows run as thread-block clusters of 512-row
+    CTAs (the last one ragged: 1100 = 2 x 512 + 76, 2100 = 4 x 512 + 52);
+    H and tau per column against float64 geqrf."""
+    assert "cluster" in fastqr.plan(1, n)
+    a = inputs.generate_input(2, n, 1, 900 + n, device=dev)
+    h, t = fastqr.geqrf(a)
+    assert gates(a, h, t, chunk=1)["ok"]
+    h64, t64 = torch.geqrf(a.double())
+    he, te = column_errors(h, t, h64, t64)
+    assert float(he.max()) <= COL_TOL and float(te.max()) <= COL_TOL, (float(he.max()), float(te.max()))
+
+
 @pytest.mark.parametrize("n", [128, 256, 512, 1024])
 def test_tensor_core_path_reports_no_timeout(n, dev):
     """The tcgen05 trailing update records any bounded wait that gave up in
