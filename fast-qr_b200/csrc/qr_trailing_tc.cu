@@ -46,23 +46,31 @@ constexpr int kStages = 3;        // phase-A ring of raw chunks
 constexpr int kRCC = 128;         // rows per phase-C chunk (MMA M)
 constexpr int kThreads = 128;
 constexpr uint32_t kTmemCols = 256;
-constexpr uint32_t kDA = 0;       // TMEM column of W^T (32 columns, phase A)
+// phase A accumulates W^T in three parts: kDA holds C_hi^T [V_hi | V_lo]
+// (64 columns: the hi*hi then the hi*lo products), kDA2 holds C_lo^T V_hi
+constexpr uint32_t kDA = 0;
+constexpr uint32_t kDA2 = 64;
 constexpr uint32_t kDP0 = 0;      // P of even phase-C chunks (128 columns; W is dead by then)
 constexpr uint32_t kDP1 = 128;    // P of odd phase-C chunks
 constexpr uint64_t kWaitLimit = 1000000000ull;  // 1 s of wall time per wait
 
 // shared memory map (bytes, from a 1024-byte aligned base).  Phase A: a ring
-// of kStages chunks, each C^T (128 c x 32 r, 16 KB) then V (32 j x 32 r,
-// 4 KB) as raw fp32 in the 128-byte swizzle layout, and two lo buffers of the
-// same shape.
+// of kStages chunks, each C^T (128 c x 32 r, 16 KB), V (32 j x 32 r, 4 KB)
+// as raw fp32 in the 128-byte swizzle layout, then V's lo part (4 KB) right
+// after V, so that [V | V_lo] is one N = 64 operand; and two lo buffers of
+// C^T.  Reading C_hi once per K step for both of its products (instead of
+// twice) matters: phase A is bound by shared-memory bandwidth.
 constexpr int kCBytes = kTN * kRC * 4;                   // 16 KB
-constexpr int kStageBytes = kCBytes + kPanel * kRC * 4;  // 20 KB
-constexpr int kOffLo = kStages * kStageBytes;            // 60 KB
-constexpr int kOffT = kOffLo + 2 * kStageBytes;          // 100 KB: S, column-major 32 x 32 (4 KB)
+constexpr int kVBytes = kPanel * kRC * 4;                // 4 KB
+constexpr int kLoadBytes = kCBytes + kVBytes;            // 20 KB arrive by TMA per chunk
+constexpr int kStageBytes = kLoadBytes + kVBytes;        // 24 KB
+constexpr int kOffLo = kStages * kStageBytes;            // 72 KB
+constexpr int kOffT = kOffLo + 2 * kCBytes;              // 104 KB: S, column-major 32 x 32 (4 KB)
 constexpr int kOffTau = kOffT + 4096;                    // tau of the panel (128 B)
 constexpr int kOffBar = kOffTau + 128;  // mbarriers: full[3], mma[2], phase C, C ring[2]; TMEM address
 constexpr int kSmemUsed = kOffBar + 128;
-constexpr int kSmem = kSmemUsed + 1024;                  // + alignment slack: ~105 KB, 2 CTAs per SM
+constexpr int kSmem = kSmemUsed + 1024;                  // + alignment slack: ~109 KB, 2 CTAs per SM
+static_assert(2 * (kSmem + 1024) <= 228 * 1024, "two CTAs per SM");
 // Phase C (reuses the phase-A area): V chunk as the K-major A operand
 // (128 r x 32 j) and Y as the K-major B operand (128 c x 32 j), raw + lo, and
 // a ring of two C quarters (128 rows x 32 columns as they sit in H, [c][r])
@@ -77,16 +85,18 @@ constexpr int kCQBytes = kRCC * kCQCols * 4;  // 16 KB
 static_assert(kOffCQ + 2 * kCQBytes <= kOffT, "phase-C buffers overlap S");
 static_assert(kStageBytes % 1024 == 0 && kCBytes % 1024 == 0, "swizzle atoms need 1024-byte alignment");
 
-constexpr uint32_t kIdescA = tc::idesc_tf32(128, 32, 0, 0);   // A = C^T (M = c), B = V (N = j)
+constexpr uint32_t kIdescA = tc::idesc_tf32(128, 64, 0, 0);   // A = C^T (M = c), B = [V | V_lo] (N = 2 x j)
+constexpr uint32_t kIdescA2 = tc::idesc_tf32(128, 32, 0, 0);  // A = C_lo^T, B = V
 constexpr uint32_t kIdescC = tc::idesc_tf32(128, 128, 0, 0);  // A = V (M = r), B = Y (N = c)
 
-// lo = x - trunc_tf32(x) over one stage (C then V, elementwise: the layout
-// does not matter).  For the first chunk the V part is also made unit lower
-// triangular in place (panel rows r < j hold R, row j holds beta).
+// lo = x - trunc_tf32(x) over one stage, elementwise (the layout does not
+// matter): C's into the lo buffer, V's into the slot after V.  For the first
+// chunk the V part is also made unit lower triangular in place (panel rows
+// r < j hold R, row j holds beta).
 __device__ __forceinline__ void split_stage(unsigned char *raw, unsigned char *lo, bool first, int tid)
 {
 #pragma unroll 2
-    for (int off = tid * 16; off < kStageBytes; off += kThreads * 16) {
+    for (int off = tid * 16; off < kLoadBytes; off += kThreads * 16) {
         float4 v = *reinterpret_cast<const float4 *>(raw + off);
         if (first && off >= kCBytes) {
             // V row j (= operand row) at (off - kCBytes) / 128; its 16-byte
@@ -101,7 +111,8 @@ __device__ __forceinline__ void split_stage(unsigned char *raw, unsigned char *l
             v = make_float4(e[0], e[1], e[2], e[3]);
             *reinterpret_cast<float4 *>(raw + off) = v;
         }
-        *reinterpret_cast<float4 *>(lo + off) =
+        unsigned char *dst = off < kCBytes ? lo + off : raw + kVBytes + off;
+        *reinterpret_cast<float4 *>(dst) =
             make_float4(tc::tf32_lo(v.x), tc::tf32_lo(v.y), tc::tf32_lo(v.z), tc::tf32_lo(v.w));
     }
 }
@@ -189,7 +200,7 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
     if (tid == 0) {
         for (int s = 0; s < kStages && s < nchunks; ++s) {
             unsigned char *st = smem + s * kStageBytes;
-            tc::mbar_expect_tx(&full[s], kStageBytes + (s == 0 ? 4096u : 0u));
+            tc::mbar_expect_tx(&full[s], kLoadBytes + (s == 0 ? 4096u : 0u));
             tc::tma_load_3d(st, &tmC, k + s * kRC, c0, (int)mat, &full[s]);
             tc::tma_load_3d(st + kCBytes, &tmV, k + s * kRC, k, (int)mat, &full[s]);
             if (s == 0) tc::bulk_load(smem + kOffT, Sws + mat * s_stride, 4096u, &full[0]);
@@ -215,23 +226,22 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
         const int sidx = i % kStages, b = i & 1;
         unsigned char *st = smem + sidx * kStageBytes;
         const bool landed = tc::mbar_wait(&full[sidx], (uint32_t)(i / kStages) & 1u, kWaitLimit);
-        if (landed && !bad) split_stage(st, smem + kOffLo + b * kStageBytes, i == 0, tid);
+        if (landed && !bad) split_stage(st, smem + kOffLo + b * kCBytes, i == 0, tid);
         tc::fence_proxy_async_smem();
         ok = !__syncthreads_or(!landed || bad);
         if (!ok) break;
         if (tid == 0) {
             tc::fence_after_sync();
             const uint32_t sC = sbase + sidx * kStageBytes, sV = sC + kCBytes;
-            const uint32_t lC = sbase + kOffLo + b * kStageBytes, lV = lC + kCBytes;
+            const uint32_t lC = sbase + kOffLo + b * kCBytes;
 #pragma unroll
             for (int s = 0; s < kRC / 8; ++s) {
                 const uint32_t ko = (uint32_t)s * 32;  // 8 K elements inside the swizzle atom
                 const uint64_t ah = tc::smem_desc_sw128(sC + ko), al = tc::smem_desc_sw128(lC + ko);
-                const uint64_t bh = tc::smem_desc_sw128(sV + ko), bl = tc::smem_desc_sw128(lV + ko);
+                const uint64_t bv = tc::smem_desc_sw128(sV + ko);  // V rows, then V_lo rows
                 const uint32_t acc = (i > 0 || s > 0) ? 1u : 0u;
-                tc::mma_tf32(tmem + kDA, al, bh, kIdescA, acc);
-                tc::mma_tf32(tmem + kDA, ah, bl, kIdescA, 1u);
-                tc::mma_tf32(tmem + kDA, ah, bh, kIdescA, 1u);
+                tc::mma_tf32(tmem + kDA, ah, bv, kIdescA, acc);
+                tc::mma_tf32(tmem + kDA2, al, bv, kIdescA2, acc);
             }
             tc::mma_commit(&mmab[b]);
         }
@@ -247,7 +257,7 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
             } else if (tid == 0 && nx < nchunks) {
                 unsigned char *fr = smem + ((i - 1) % kStages) * kStageBytes;
                 uint64_t *fb = &full[(i - 1) % kStages];
-                tc::mbar_expect_tx(fb, kStageBytes);
+                tc::mbar_expect_tx(fb, kLoadBytes);
                 tc::tma_load_3d(fr, &tmC, k + nx * kRC, c0, (int)mat, fb);
                 tc::tma_load_3d(fr + kCBytes, &tmV, k + nx * kRC, k, (int)mat, fb);
             }
@@ -301,12 +311,21 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
     // ---- phase B: Y = T^T W, thread = tile column c ------------------------
     if (ok) {
         tc::fence_after_sync();
-        float w[32];
-        tc::tmem_ld_32x32(tmem + ((uint32_t)(32 * warp) << 16) + kDA, w);
+        // W^T row c = hi*hi + hi*lo + lo*hi parts (three 32-column slices)
+        float w[32], y[32];
+        const uint32_t wrow = tmem + ((uint32_t)(32 * warp) << 16);
+        tc::tmem_ld_32x32(wrow + kDA, w);
         tc::tmem_ld_wait();
+        tc::tmem_ld_32x32(wrow + kDA + 32, y);
+        tc::tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) w[j] += y[j];
+        tc::tmem_ld_32x32(wrow + kDA2, y);
+        tc::tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) w[j] += y[j];
         const int c = 32 * warp + lane;
         // T = D (I + S D)^-1 with D = diag(tau), S = strict_upper(V^T V).
-        float y[32];
         if constexpr (ApplyT) {
             // Y = T^T W (apply H^T): (I + D S^T) Y = D W, forward substitution
             //   y_c = tau_c (w_c - sum_{l < c} S(l, c) y_l)
