@@ -53,6 +53,10 @@ constexpr uint32_t kDA2 = 64;
 constexpr uint32_t kDP0 = 0;      // P of even phase-C chunks (128 columns; W is dead by then)
 constexpr uint32_t kDP1 = 128;    // P of odd phase-C chunks
 constexpr uint64_t kWaitLimit = 1000000000ull;  // 1 s of wall time per wait
+// kernel flags: trigger the next kernel's launch at the start of phase C
+// (else after it); apply C -= P by TMA reduce-add (else load/subtract/store)
+constexpr int kFlagEarlyTrigger = 1;
+constexpr int kFlagReduceC = 2;
 
 // shared memory map (bytes, from a 1024-byte aligned base).  Phase A: a ring
 // of kStages chunks, each C^T (128 c x 32 r, 16 KB), V (32 j x 32 r, 4 KB)
@@ -152,8 +156,10 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
                    const __grid_constant__ CUtensorMap tmCQ, const float *__restrict__ H,
                    const float *__restrict__ Sws, int64_t s_stride, const float *__restrict__ tau,
                    int *__restrict__ status, int n, int k, int c_begin, int c_end, int64_t b0,
-                   int early_trigger)
+                   int flags)
 {
+    const bool early_trigger = flags & kFlagEarlyTrigger;
+    const bool reduce_c = flags & kFlagReduceC;
     extern __shared__ unsigned char smem_raw[];
     const uint32_t raw_addr = tc::smem_addr(smem_raw);
     unsigned char *smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
@@ -302,9 +308,11 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
     };
     float e[kPanel];  // V rows of the next phase-C chunk
     if (ok) {
-        if (tid == 0)
-            for (int u = 0; u < 2 && u < nq; ++u) load_quarter(u);
-        q_loads = nq < 2 ? nq : 2;
+        if (!reduce_c) {
+            if (tid == 0)
+                for (int u = 0; u < 2 && u < nq; ++u) load_quarter(u);
+            q_loads = nq < 2 ? nq : 2;
+        }
         load_v_rows(Vbase, n, 0, m, wv, tid, e);
     }
 
@@ -407,6 +415,30 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
         tc::fence_after_sync();
         const uint32_t pc = tmem + ((uint32_t)(32 * warp) << 16) + ((j & 1) ? kDP1 : kDP0);
         // epilogue: thread = row j * 128 + tid of the tile
+        if (reduce_c) {
+            // -P goes to a shared quarter that TMA adds into C at the L2: no
+            // load of C, half the shared-memory traffic of load/subtract/store
+            // (C - P and C + (-P) round identically)
+            for (int q = 0; q < nqc; ++q) {
+                const int u = j * nqc + q;
+                float pv[32];
+                tc::tmem_ld_32x32(pc + kCQCols * q, pv);
+                tc::tmem_ld_wait();
+                float *cs = reinterpret_cast<float *>(smem + kOffCQ + (u & 1) * kCQBytes);
+#pragma unroll
+                for (int c = 0; c < kCQCols; ++c) cs[c * kRCC + tid] = -pv[c];
+                tc::fence_proxy_async_smem();
+                // the reduce of quarter u-1 (the only one outstanding) has read
+                // its buffer before anyone passes this barrier: quarter u+1
+                // writes that buffer
+                if (tid == 0) tc::bulk_wait_group_read<0>();
+                __syncthreads();
+                if (tid == 0) {
+                    tc::tma_reduce_add_3d(&tmCQ, k + kRCC * j, c0 + kCQCols * q, (int)mat, cs);
+                    tc::bulk_commit_group();
+                }
+            }
+        } else
         for (int q = 0; q < nqc; ++q) {
             const int u = j * nqc + q, b = u & 1;
             const bool landed = tc::mbar_wait(&cfull[b], (uint32_t)q_used[b] & 1u, kWaitLimit);
@@ -520,6 +552,15 @@ cudaError_t prepare_trailing_tc(float *H, int64_t batch, int n, TrailingMaps *ma
     return prepare_apply_maps(H, n, H, n, batch, maps);
 }
 
+// Static plan by n: a large launch triggers the next kernel early (its CTAs
+// are placed while the last wave finishes); the reduce-add epilogue wins while
+// the trailing block stays in L2 and loses to prefetched loads when the L2
+// reduction has to fetch its lines from HBM (measured at n = 4096).
+static int trailing_flags(int n)
+{
+    return (n > 256 ? kFlagEarlyTrigger : 0) | (n <= 2048 ? kFlagReduceC : 0);
+}
+
 cudaError_t launch_apply_tc(const TrailingMaps &maps, const float *H, const float *Sws, int64_t s_stride,
                             const float *tau, int *status, int64_t batch, int n, int k, int c_begin,
                             int c_end, bool apply_t, cudaStream_t st)
@@ -533,7 +574,7 @@ cudaError_t launch_apply_tc(const TrailingMaps &maps, const float *H, const floa
         const int64_t nb = (batch - b0) < 65535 ? (batch - b0) : 65535;
         dim3 grid(tiles, (unsigned)nb);
         e = launch_dependent(kern, grid, dim3(kThreads), kSmem, st, nullptr, 0, maps.c, maps.v, maps.cq, H, Sws,
-                             s_stride, tau, status, n, k, c_begin, c_end, b0, n > 256 ? 1 : 0);
+                             s_stride, tau, status, n, k, c_begin, c_end, b0, trailing_flags(n));
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;

@@ -231,6 +231,13 @@ __device__ __forceinline__ void tma_store_3d(const void *tmap, int x, int y, int
                  :: "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(smem_addr(src_smem))
                  : "memory");
 }
+// global tile += shared tile (fp32 add at the L2), bulk-group completion
+__device__ __forceinline__ void tma_reduce_add_3d(const void *tmap, int x, int y, int z, const void *src_smem)
+{
+    asm volatile("cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group [%0, {%1, %2, %3}], [%4];"
+                 :: "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(smem_addr(src_smem))
+                 : "memory");
+}
 __device__ __forceinline__ void bulk_commit_group()
 {
     asm volatile("cp.async.bulk.commit_group;" ::: "memory");
