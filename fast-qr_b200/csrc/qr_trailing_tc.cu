@@ -7,20 +7,23 @@
 //
 // One CTA (4 warps, two CTAs per SM) owns a tile of kTN = 128 trailing
 // columns of one matrix:
-//   phase A  W^T[c][j] = sum_r C(r, c) V(r, j)    tcgen05.mma M=128 (c) N=32 (j),
-//            K = rows, accumulated over 32-row chunks into TMEM.  Thread 0
+//   phase A  W^T[c][j] = sum_r C(r, c) V(r, j)    tcgen05.mma M=128 (c), K = rows,
+//            accumulated over 32-row chunks into TMEM: C_hi against
+//            [V_hi | V_lo] (N=64) and C_lo against V_hi (N=32).  Thread 0
 //            streams the chunks by TMA (tensor maps over H, 128-byte
 //            swizzle: each column's 32 rows are one 128-byte operand row)
 //            through a 3-stage ring; all threads split chunk i into its lo
-//            buffer (two, alternating) while the MMAs of chunk i-1 run.
+//            buffers while the MMAs of chunk i-1 run.  This phase is bound by
+//            shared-memory bandwidth (TMA writes, the split's loads and
+//            stores, the MMAs' operand reads).
 //   phase B  Y = T^T W                            per thread (one column c), by
 //            forward substitution with S = V^T V (strict upper) and tau:
 //            T = D (I + S D)^-1, so (I + D S^T) Y = D W
 //   phase C  P[r][c] = sum_j V(r, j) Y(j, c)      tcgen05.mma M=128 (r) N=128 (c)
 //            K = 32 per 128-row chunk, into two TMEM accumulators in turn so
 //            that the next chunk's MMA runs during this chunk's epilogue;
-//            the epilogue C(r, c) -= P streams C through shared memory in
-//            32-column quarters, loaded and stored by TMA
+//            the epilogue writes -P in 32-column quarters to shared memory
+//            and TMA reduce-adds them into C
 // The raw fp32 data is the hi operand (the tensor core truncates it to TF32);
 // threads write lo = x - trunc_tf32(x) into a second buffer of the same
 // layout.  Phase C's V and Y operands are staged by threads in the
@@ -54,9 +57,8 @@ constexpr uint32_t kDP0 = 0;      // P of even phase-C chunks (128 columns; W is
 constexpr uint32_t kDP1 = 128;    // P of odd phase-C chunks
 constexpr uint64_t kWaitLimit = 1000000000ull;  // 1 s of wall time per wait
 // kernel flags: trigger the next kernel's launch at the start of phase C
-// (else after it); apply C -= P by TMA reduce-add (else load/subtract/store)
+// (else after it)
 constexpr int kFlagEarlyTrigger = 1;
-constexpr int kFlagReduceC = 2;
 
 // shared memory map (bytes, from a 1024-byte aligned base).  Phase A: a ring
 // of kStages chunks, each C^T (128 c x 32 r, 16 KB), V (32 j x 32 r, 4 KB)
@@ -71,14 +73,14 @@ constexpr int kStageBytes = kLoadBytes + kVBytes;        // 24 KB
 constexpr int kOffLo = kStages * kStageBytes;            // 72 KB
 constexpr int kOffT = kOffLo + 2 * kCBytes;              // 104 KB: S, column-major 32 x 32 (4 KB)
 constexpr int kOffTau = kOffT + 4096;                    // tau of the panel (128 B)
-constexpr int kOffBar = kOffTau + 128;  // mbarriers: full[3], mma[2], phase C, C ring[2]; TMEM address
+constexpr int kOffBar = kOffTau + 128;  // mbarriers: full[3], mma[2], phase C; TMEM address
 constexpr int kSmemUsed = kOffBar + 128;
 constexpr int kSmem = kSmemUsed + 1024;                  // + alignment slack: ~109 KB, 2 CTAs per SM
 static_assert(2 * (kSmem + 1024) <= 228 * 1024, "two CTAs per SM");
 // Phase C (reuses the phase-A area): V chunk as the K-major A operand
 // (128 r x 32 j) and Y as the K-major B operand (128 c x 32 j), raw + lo, and
-// a ring of two C quarters (128 rows x 32 columns as they sit in H, [c][r])
-// that TMA loads and stores.
+// two -P quarters (128 rows x 32 columns as they sit in H, [c][r]) that TMA
+// reduce-adds into C.
 constexpr int kOffVCraw = 0;
 constexpr int kOffVClo = 16384;
 constexpr int kOffYraw = 32768;
@@ -159,7 +161,6 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
                    int flags)
 {
     const bool early_trigger = flags & kFlagEarlyTrigger;
-    const bool reduce_c = flags & kFlagReduceC;
     extern __shared__ unsigned char smem_raw[];
     const uint32_t raw_addr = tc::smem_addr(smem_raw);
     unsigned char *smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
@@ -178,7 +179,6 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + kOffBar);  // [kStages]
     uint64_t *mmab = full + kStages;                                // [2]
     uint64_t *cbar = full + kStages + 2;                            // phase-C MMA
-    uint64_t *cfull = full + kStages + 3;                           // [2] C quarter ring
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kOffBar + 64);
     float *Ts = reinterpret_cast<float *>(smem + kOffT);    // S(l, c) at c * 32 + l
     float *taus = reinterpret_cast<float *>(smem + kOffTau);
@@ -194,7 +194,7 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
         tc::prefetch_tensormap(&tmC);
         tc::prefetch_tensormap(&tmV);
         tc::prefetch_tensormap(&tmCQ);
-        for (int i = 0; i < kStages + 5; ++i) tc::mbar_init(&full[i], 1);
+        for (int i = 0; i < kStages + 3; ++i) tc::mbar_init(&full[i], 1);
         tc::fence_mbar_init();
     }
     if (warp == 0) {
@@ -286,35 +286,13 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
     // not hold SMs the other half of a split batch could use
     if (early_trigger) pdl_trigger();
 
-    // ---- phase C set-up: the first two C quarters start streaming now
+    // ---- phase C set-up
     const int ncc = (m + kRCC - 1) / kRCC;
     // quarters per chunk that hold tile columns: a tile narrower than kTN (the
-    // end of [c_begin, c_end)) must not store the quarters beyond c_end
+    // end of [c_begin, c_end)) must not touch the quarters beyond c_end
     const int nqc = (nct + kCQCols - 1) / kCQCols;
-    const int nq = ncc * nqc;        // C quarters of the tile, in order (chunk, quarter)
-    int q_loads = 0;                 // quarters whose TMA load was issued
-    int q_used[2] = {0, 0};          // quarters consumed per ring buffer
-    // the loads go in order u = 0, 1, ...: (chunk, quarter) of the next one
-    // as running counters (thread 0)
-    int ld_chunk = 0, ld_q = 0;
-    auto load_quarter = [&](int u) {  // thread 0
-        unsigned char *cs = smem + kOffCQ + (u & 1) * kCQBytes;
-        tc::mbar_expect_tx(&cfull[u & 1], kCQBytes);
-        tc::tma_load_3d(cs, &tmCQ, k + kRCC * ld_chunk, c0 + kCQCols * ld_q, (int)mat, &cfull[u & 1]);
-        if (++ld_q == nqc) {
-            ld_q = 0;
-            ++ld_chunk;
-        }
-    };
     float e[kPanel];  // V rows of the next phase-C chunk
-    if (ok) {
-        if (!reduce_c) {
-            if (tid == 0)
-                for (int u = 0; u < 2 && u < nq; ++u) load_quarter(u);
-            q_loads = nq < 2 ? nq : 2;
-        }
-        load_v_rows(Vbase, n, 0, m, wv, tid, e);
-    }
+    if (ok) load_v_rows(Vbase, n, 0, m, wv, tid, e);
 
     // ---- phase B: Y = T^T W, thread = tile column c ------------------------
     if (ok) {
@@ -414,60 +392,34 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
         if (j + 2 < ncc) load_v_rows(Vbase, n, (j + 2) * kRCC, m, wv, tid, e);
         tc::fence_after_sync();
         const uint32_t pc = tmem + ((uint32_t)(32 * warp) << 16) + ((j & 1) ? kDP1 : kDP0);
-        // epilogue: thread = row j * 128 + tid of the tile
-        if (reduce_c) {
-            // -P goes to a shared quarter that TMA adds into C at the L2: no
-            // load of C, half the shared-memory traffic of load/subtract/store
-            // (C - P and C + (-P) round identically)
-            for (int q = 0; q < nqc; ++q) {
-                const int u = j * nqc + q;
-                float pv[32];
-                tc::tmem_ld_32x32(pc + kCQCols * q, pv);
-                tc::tmem_ld_wait();
-                float *cs = reinterpret_cast<float *>(smem + kOffCQ + (u & 1) * kCQBytes);
-#pragma unroll
-                for (int c = 0; c < kCQCols; ++c) cs[c * kRCC + tid] = -pv[c];
-                tc::fence_proxy_async_smem();
-                // the reduce of quarter u-1 (the only one outstanding) has read
-                // its buffer before anyone passes this barrier: quarter u+1
-                // writes that buffer
-                if (tid == 0) tc::bulk_wait_group_read<0>();
-                __syncthreads();
-                if (tid == 0) {
-                    tc::tma_reduce_add_3d(&tmCQ, k + kRCC * j, c0 + kCQCols * q, (int)mat, cs);
-                    tc::bulk_commit_group();
-                }
-            }
-        } else
+        // epilogue: thread = row j * 128 + tid of the tile.  -P goes to a
+        // shared quarter (32 columns) that TMA adds into C at the L2: no load
+        // of C, half the shared-memory traffic of load/subtract/store, and
+        // C - P and C + (-P) round identically.  Rows and columns past the
+        // end of C are outside the tensor map and are not written.
         for (int q = 0; q < nqc; ++q) {
-            const int u = j * nqc + q, b = u & 1;
-            const bool landed = tc::mbar_wait(&cfull[b], (uint32_t)q_used[b] & 1u, kWaitLimit);
-            if (landed) ++q_used[b];
+            const int u = j * nqc + q;
             float pv[32];
             tc::tmem_ld_32x32(pc + kCQCols * q, pv);
             tc::tmem_ld_wait();
-            float *cs = reinterpret_cast<float *>(smem + kOffCQ + b * kCQBytes);
-            if (landed) {
+            float *cs = reinterpret_cast<float *>(smem + kOffCQ + (u & 1) * kCQBytes);
 #pragma unroll
-                for (int c = 0; c < kCQCols; ++c) cs[c * kRCC + tid] -= pv[c];
-            }
+            for (int c = 0; c < kCQCols; ++c) cs[c * kRCC + tid] = -pv[c];
             tc::fence_proxy_async_smem();
-            ok = !__syncthreads_or(!landed);
-            if (!ok) break;
+            // the reduce of quarter u-1 (the only one outstanding) has read
+            // its buffer before anyone passes this barrier: quarter u+1
+            // writes that buffer
+            if (tid == 0) tc::bulk_wait_group_read<0>();
+            __syncthreads();
             if (tid == 0) {
-                tc::tma_store_3d(&tmCQ, k + kRCC * j, c0 + kCQCols * q, (int)mat, cs);
+                tc::tma_reduce_add_3d(&tmCQ, k + kRCC * j, c0 + kCQCols * q, (int)mat, cs);
                 tc::bulk_commit_group();
-                if (u + 2 < nq) {
-                    tc::bulk_wait_group_read<0>();  // the store has read the buffer
-                    load_quarter(u + 2);
-                }
             }
-            if (u + 2 < nq) ++q_loads;
         }
         tc::fence_before_sync();
     }
     if (!early_trigger) pdl_trigger();
-    if (tid == 0) tc::bulk_wait_group<0>();  // stores complete before shared memory goes away
+    if (tid == 0) tc::bulk_wait_group<0>();  // reduces complete before shared memory goes away
 
     if (!ok && tid == 0) {
         atomicOr(status, 1);
@@ -484,11 +436,6 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
                 if (!tc::mbar_wait(&mmab[b], mma_waited[b]++ & 1u, kWaitLimit)) break;
         while (c_waited < c_issued)
             if (!tc::mbar_wait(cbar, c_waited++ & 1u, kWaitLimit)) break;
-        for (int b = 0; b < 2; ++b) {
-            const int issued_b = (q_loads + 1 - b) / 2;  // loads into ring buffer b
-            while (q_used[b] < issued_b)
-                if (!tc::mbar_wait(&cfull[b], (uint32_t)q_used[b]++ & 1u, kWaitLimit)) break;
-        }
     }
     __syncthreads();
     if (warp == 0) {
@@ -553,13 +500,8 @@ cudaError_t prepare_trailing_tc(float *H, int64_t batch, int n, TrailingMaps *ma
 }
 
 // Static plan by n: a large launch triggers the next kernel early (its CTAs
-// are placed while the last wave finishes); the reduce-add epilogue wins while
-// the trailing block stays in L2 and loses to prefetched loads when the L2
-// reduction has to fetch its lines from HBM (measured at n = 4096).
-static int trailing_flags(int n)
-{
-    return (n > 256 ? kFlagEarlyTrigger : 0) | (n <= 2048 ? kFlagReduceC : 0);
-}
+// are placed while the last wave finishes).
+static int trailing_flags(int n) { return n > 256 ? kFlagEarlyTrigger : 0; }
 
 cudaError_t launch_apply_tc(const TrailingMaps &maps, const float *H, const float *Sws, int64_t s_stride,
                             const float *tau, int *status, int64_t batch, int n, int k, int c_begin,
