@@ -1,9 +1,10 @@
 // C ABI of libfastqr.so (declared in include/fastqr.h).
 //
-// Static dispatch on (batch, n) only:
-//   n <= 64  : one warp per matrix, registers (qr_small.cu)
-//   n >  64  : blocked compact-WY: copy-in, then per 32-column panel a panel
-//              kernel and a trailing-update kernel (qr_blocked.cu)
+// Static dispatch on (batch, m, n) only:
+//   m == n <= 64 : one warp per matrix, registers (qr_small.cu)
+//   otherwise    : blocked compact-WY: copy-in, then per 32-column panel a
+//                  panel kernel and a trailing-update kernel (qr_blocked.cu);
+//                  rectangular m x n (m > n) always takes this path
 // No path inspects matrix values and there is no CPU fallback: a failed
 // launch is reported as a status code.
 #include <cuda_runtime.h>
@@ -139,28 +140,28 @@ struct StageTimer {
     }
 };
 
-// The blocked path for one batch range: copy-in, then per 32-column panel a
-// panel kernel and a trailing update, all on `st`.
-int enqueue_blocked(const float *A, int64_t batch, int n, int64_t a_bstride, int64_t a_rstride,
+// The blocked path for one batch range of m x n matrices (m >= n): copy-in,
+// then per 32-column panel a panel kernel and a trailing update, all on `st`.
+int enqueue_blocked(const float *A, int64_t batch, int m, int n, int64_t a_bstride, int64_t a_rstride,
                     int64_t a_cstride, float *H, float *tau, float *Tws, int *status, int clear, bool tc,
                     cudaStream_t st, StageTimer *tm)
 {
     fqr::TrailingMaps maps;
-    if (tc && fqr::prepare_trailing_tc(H, batch, n, &maps) != cudaSuccess) return FQR_ECUDA;
+    if (tc && fqr::prepare_trailing_tc(H, batch, m, n, &maps) != cudaSuccess) return FQR_ECUDA;
     cudaError_t e;
     if (tm) tm->begin(FQR_STAGE_COPY_IN);
-    e = fqr::launch_copy_in(A, batch, n, a_bstride, a_rstride, a_cstride, H, status, clear, st);
+    e = fqr::launch_copy_in(A, batch, m, n, a_bstride, a_rstride, a_cstride, H, status, clear, st);
     if (tm) tm->end();
     if (e != cudaSuccess) return status_from(e);
     for (int k = 0; k < n; k += fqr::kPanel) {
         if (tm) tm->begin(FQR_STAGE_PANEL);
-        e = fqr::launch_panel(H, tau, Tws, batch, n, k, st);
+        e = fqr::launch_panel(H, tau, Tws, batch, m, n, k, st);
         if (tm) tm->end();
         if (e != cudaSuccess) return status_from(e);
         if (k + fqr::kPanel < n) {
             if (tm) tm->begin(FQR_STAGE_TRAILING);
-            e = tc ? fqr::launch_trailing_tc(maps, H, Tws, tau, status, batch, n, k, st)
-                   : fqr::launch_trailing(H, Tws, tau, batch, n, k, st);
+            e = tc ? fqr::launch_trailing_tc(maps, H, Tws, tau, status, batch, m, n, k, st)
+                   : fqr::launch_trailing(H, Tws, tau, batch, m, n, k, st);
             if (tm) tm->end();
             if (e != cudaSuccess) return status_from(e);
         }
@@ -183,7 +184,7 @@ struct SplitStreams {
 constexpr int kMaxDevices = 64;
 SplitStreams g_split[kMaxDevices];
 
-int enqueue_blocked_split(const float *A, int64_t batch, int n, int64_t a_bstride, int64_t a_rstride,
+int enqueue_blocked_split(const float *A, int64_t batch, int m, int n, int64_t a_bstride, int64_t a_rstride,
                           int64_t a_cstride, float *H, float *tau, float *Tws, int *status, bool tc,
                           cudaStream_t st)
 {
@@ -199,14 +200,14 @@ int enqueue_blocked_split(const float *A, int64_t batch, int n, int64_t a_bstrid
         sp.ready = true;
     }
     const int64_t b0 = batch / 2;
-    const size_t nn = (size_t)n * (size_t)n;
+    const size_t mn = (size_t)m * (size_t)n;
     if (cudaEventRecord(sp.fork, st) != cudaSuccess || cudaStreamWaitEvent(sp.side, sp.fork, 0) != cudaSuccess)
         return FQR_ECUDA;
     // each half its own status word (the copy-in of a half clears its word)
-    int rc1 = enqueue_blocked(A, b0, n, a_bstride, a_rstride, a_cstride, H, tau, Tws, status, 1, tc, st,
+    int rc1 = enqueue_blocked(A, b0, m, n, a_bstride, a_rstride, a_cstride, H, tau, Tws, status, 1, tc, st,
                               nullptr);
-    int rc2 = enqueue_blocked(A + b0 * a_bstride, batch - b0, n, a_bstride, a_rstride, a_cstride,
-                              H + b0 * nn, tau + b0 * n, Tws + b0 * (fqr::kPanel * fqr::kPanel), status + 1,
+    int rc2 = enqueue_blocked(A + b0 * a_bstride, batch - b0, m, n, a_bstride, a_rstride, a_cstride,
+                              H + b0 * mn, tau + b0 * n, Tws + b0 * (fqr::kPanel * fqr::kPanel), status + 1,
                               1, tc, sp.side, nullptr);
     // join even after a failure, so nothing of this call stays unordered with
     // later work on the caller's stream
@@ -220,37 +221,39 @@ int enqueue_blocked_split(const float *A, int64_t batch, int n, int64_t a_bstrid
 // status_word: where the tensor-core kernels record a bounded wait that gave
 // up (NULL: the words after the S blocks in the workspace).  split: whether
 // a batch of two or more may run as two halves on two streams.
-int run_geqrf(const float *A, int64_t batch, int64_t n, int64_t a_bstride, int64_t a_rstride,
+// m: rows (m >= n; m == n for the square entry points).
+int run_geqrf(const float *A, int64_t batch, int64_t m, int64_t n, int64_t a_bstride, int64_t a_rstride,
               int64_t a_cstride, float *H, float *tau, void *workspace, size_t workspace_bytes,
               cudaStream_t st, StageTimer *tm, int *status_word = nullptr, bool split = true)
 {
-    if (batch < 0 || n < 0) return FQR_EINVAL;
+    if (batch < 0 || n < 0 || m < 0) return FQR_EINVAL;
     if (batch == 0 || n == 0) return FQR_OK;
-    if (n > FQR_MAX_N) return FQR_EUNSUPPORTED;
+    if (m > FQR_MAX_N || n > FQR_MAX_N || m < n) return FQR_EUNSUPPORTED;
+    if ((int64_t)m * n > (int64_t)FQR_MAX_N * FQR_MAX_N) return FQR_EUNSUPPORTED;
     if (!A || !H || !tau) return FQR_EINVAL;
     if (a_rstride == 0 || a_cstride == 0 || (batch > 1 && a_bstride == 0)) return FQR_EINVAL;
-    const int ni = (int)n;
+    const int ni = (int)n, mi = (int)m;
 
-    if (small_path(n)) {
+    if (m == n && small_path(n)) {
         if (tm) tm->begin(FQR_STAGE_SMALL);
         cudaError_t e = fqr::launch_small(A, batch, ni, a_bstride, a_rstride, a_cstride, H, tau, st);
         if (tm) tm->end();
         return status_from(e);
     }
 
-    const size_t need = fqr_workspace_bytes(batch, n);
+    const size_t need = fqr::ws_total_bytes(batch);
     if (!workspace || workspace_bytes < need) return FQR_EWORKSPACE;
     if (((uintptr_t)workspace) % kWsAlign) return FQR_EINVAL;
     float *Tws = (float *)workspace;
     int *status = status_word ? status_word
                               : (int *)((unsigned char *)workspace + fqr::ws_t_bytes(batch));
-    const bool tc = use_tc(n) && ((uintptr_t)H % 16) == 0;
+    const bool tc = use_tc(m) && ((uintptr_t)H % 16) == 0;
     if (split && !tm && batch >= 2)
-        return enqueue_blocked_split(A, batch, ni, a_bstride, a_rstride, a_cstride, H, tau, Tws, status,
+        return enqueue_blocked_split(A, batch, mi, ni, a_bstride, a_rstride, a_cstride, H, tau, Tws, status,
                                      tc, st);
     // an own status word (host entry, one per chunk) or both words of the
     // workspace's status block
-    return enqueue_blocked(A, batch, ni, a_bstride, a_rstride, a_cstride, H, tau, Tws, status,
+    return enqueue_blocked(A, batch, mi, ni, a_bstride, a_rstride, a_cstride, H, tau, Tws, status,
                            status_word ? 1 : 2, tc, st, tm);
 }
 
@@ -260,7 +263,7 @@ int fqr::geqrf_enqueue(const float *A, int64_t batch, int64_t n, int64_t a_bstri
                        int64_t a_rstride, int64_t a_cstride, float *H, float *tau, void *workspace,
                        size_t workspace_bytes, cudaStream_t st)
 {
-    return run_geqrf(A, batch, n, a_bstride, a_rstride, a_cstride, H, tau, workspace,
+    return run_geqrf(A, batch, n, n, a_bstride, a_rstride, a_cstride, H, tau, workspace,
                      workspace_bytes, st, nullptr);
 }
 
@@ -269,7 +272,7 @@ int fqr::geqrf_enqueue_status(const float *A, int64_t batch, int64_t n, int64_t 
                               void *workspace, size_t workspace_bytes, int *status_word,
                               cudaStream_t st)
 {
-    return run_geqrf(A, batch, n, a_bstride, a_rstride, a_cstride, H, tau, workspace,
+    return run_geqrf(A, batch, n, n, a_bstride, a_rstride, a_cstride, H, tau, workspace,
                      workspace_bytes, st, nullptr, status_word, false);
 }
 
@@ -279,8 +282,23 @@ int fqr_geqrf_f32(const float *A, int64_t batch, int64_t n, int64_t a_bstride, i
                   int64_t a_cstride, float *H, float *tau, void *workspace, size_t workspace_bytes,
                   void *stream)
 {
-    return run_geqrf(A, batch, n, a_bstride, a_rstride, a_cstride, H, tau, workspace,
+    return run_geqrf(A, batch, n, n, a_bstride, a_rstride, a_cstride, H, tau, workspace,
                      workspace_bytes, (cudaStream_t)stream, nullptr);
+}
+
+size_t fqr_geqrf_rect_workspace_bytes(int64_t batch, int64_t m, int64_t n)
+{
+    if (batch <= 0 || n <= 0 || m < n || m > FQR_MAX_N) return 0;
+    if (m == n) return fqr_workspace_bytes(batch, n);
+    return fqr::ws_total_bytes(batch);
+}
+
+int fqr_geqrf_rect_f32(const float *A, int64_t batch, int64_t m, int64_t n, int64_t a_bstride,
+                       int64_t a_rstride, int64_t a_cstride, float *H, float *tau, void *workspace,
+                       size_t workspace_bytes, void *stream)
+{
+    return run_geqrf(A, batch, m, n, a_bstride, a_rstride, a_cstride, H, tau, workspace, workspace_bytes,
+                     (cudaStream_t)stream, nullptr);
 }
 
 int fqr_check_status(const void *workspace, size_t workspace_bytes, int64_t batch, void *stream)
@@ -304,7 +322,7 @@ int fqr_geqrf_f32_profile(const float *A, int64_t batch, int64_t n, int64_t a_bs
     if (!stage_ms) return FQR_EINVAL;
     StageTimer *tm = new StageTimer();
     tm->st = (cudaStream_t)stream;
-    int rc = run_geqrf(A, batch, n, a_bstride, a_rstride, a_cstride, H, tau, workspace,
+    int rc = run_geqrf(A, batch, n, n, a_bstride, a_rstride, a_cstride, H, tau, workspace,
                        workspace_bytes, (cudaStream_t)stream, tm);
     int rc2 = tm->finish(stage_ms, FQR_NUM_STAGES);
     delete tm;

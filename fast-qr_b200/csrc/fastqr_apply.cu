@@ -182,14 +182,14 @@ int run_apply(const float *H, const float *tau, int64_t batch, int64_t n, float 
         if ((e = cudaGetLastError()) != cudaSuccess) return status_of(e);
     }
     TrailingMaps maps;
-    if (prepare_apply_maps(H, ni, C, mode == 0 ? n : ncols, batch, &maps) != cudaSuccess) return FQR_ECUDA;
+    if (prepare_apply_maps(H, ni, ni, C, mode == 0 ? n : ncols, batch, &maps) != cudaSuccess) return FQR_ECUDA;
     const int64_t s_stride = (int64_t)panels * kPanel * kPanel;
     for (int s = 0; s < panels; ++s) {
         const int p = mode == 1 ? s : panels - 1 - s;
         const int k = p * kPanel;
         const int cb = mode == 0 ? k : 0, ce = mode == 0 ? ni : (int)ncols;
-        e = launch_apply_tc(maps, H, S + (int64_t)p * kPanel * kPanel, s_stride, tau, status, batch, ni, k, cb,
-                            ce, mode == 1, st);
+        e = launch_apply_tc(maps, H, S + (int64_t)p * kPanel * kPanel, s_stride, tau, status, batch, ni, ni, k,
+                            cb, ce, mode == 1, st);
         if (e != cudaSuccess) return status_of(e);
     }
     return FQR_OK;

@@ -15,38 +15,41 @@ constexpr int kPanel = 32;
 cudaError_t launch_small(const float *A, int64_t batch, int n, int64_t bs, int64_t rs, int64_t cs,
                          float *H, float *tau, cudaStream_t st);
 
-// Blocked path pieces (n > 64).
+// Blocked path pieces (n > 64, or any m x n with m >= n).  H holds m x n
+// column-major per matrix (column length m), tau n values per matrix.
 // Also clears status[0 .. clear-1] (the bounded-wait status words).
-cudaError_t launch_copy_in(const float *A, int64_t batch, int n, int64_t bs, int64_t rs, int64_t cs,
+cudaError_t launch_copy_in(const float *A, int64_t batch, int m, int n, int64_t bs, int64_t rs, int64_t cs,
                            float *H, int *status, int clear, cudaStream_t st);
-cudaError_t launch_panel(float *H, float *tau, float *Tws, int64_t batch, int n, int k,
+cudaError_t launch_panel(float *H, float *tau, float *Tws, int64_t batch, int m, int n, int k,
                          cudaStream_t st);
-cudaError_t launch_trailing(float *H, const float *Sws, const float *tau, int64_t batch, int n, int k,
+cudaError_t launch_trailing(float *H, const float *Sws, const float *tau, int64_t batch, int m, int n, int k,
                             cudaStream_t st);
 
-// Tensor-core (tcgen05, 3xTF32) trailing update; needs n % 4 == 0, n >= 128
-// and a 16-byte aligned H.  Sets *status to nonzero if a bounded wait gave up.
+// Tensor-core (tcgen05, 3xTF32) trailing update; needs a row count m with
+// m % 4 == 0, m >= 128 and a 16-byte aligned H.  Sets *status to nonzero if a bounded wait gave up.
 // Its phase-A operands arrive by TMA through two tensor maps of H, encoded
 // once per call by prepare_trailing_tc (they depend on H, n and batch only).
-bool trailing_tc_supported(int n);
+bool trailing_tc_supported(int m);
 struct TrailingMaps {
     CUtensorMap c;  // 32 rows x 128 trailing columns, 128-byte swizzle
     CUtensorMap v;   // 32 rows x 32 panel columns, 128-byte swizzle
     CUtensorMap cq;  // 128 rows x 32 trailing columns, no swizzle (phase C)
 };
-cudaError_t prepare_trailing_tc(float *H, int64_t batch, int n, TrailingMaps *maps);
+cudaError_t prepare_trailing_tc(float *H, int64_t batch, int m, int n, TrailingMaps *maps);
 // Maps for applying the reflectors stored in H (n x n per matrix) to a
-// target C (n x c_cols per matrix, column-major, batch stride n * c_cols).
-cudaError_t prepare_apply_maps(const float *H, int n, float *C, int64_t c_cols, int64_t batch,
+// target C (m x c_cols per matrix, column-major, batch stride m * c_cols);
+// H is m x hcols (column length m).
+cudaError_t prepare_apply_maps(const float *H, int m, int hcols, float *C, int64_t c_cols, int64_t batch,
                                TrailingMaps *maps);
-// C[k:n, c_begin:c_end] := (I - V T^T V^T) C (apply_t) or (I - V T V^T) C,
-// V = the unit-lower reflectors of columns k .. k+31 of H (fewer at the end),
+// C[k:m, c_begin:c_end] := (I - V T^T V^T) C (apply_t) or (I - V T V^T) C,
+// V = the unit-lower reflectors of columns k .. k+31 of H (fewer at the end;
+// H is m x hcols, tau hcols values per matrix),
 // T = D (I + S D)^-1 from S blocks at Sws + mat * s_stride (floats) and tau.
 cudaError_t launch_apply_tc(const TrailingMaps &maps, const float *H, const float *Sws, int64_t s_stride,
-                            const float *tau, int *status, int64_t batch, int n, int k, int c_begin,
-                            int c_end, bool apply_t, cudaStream_t st);
+                            const float *tau, int *status, int64_t batch, int m, int hcols, int k,
+                            int c_begin, int c_end, bool apply_t, cudaStream_t st);
 cudaError_t launch_trailing_tc(const TrailingMaps &maps, float *H, const float *Sws, const float *tau,
-                               int *status, int64_t batch, int n, int k, cudaStream_t st);
+                               int *status, int64_t batch, int m, int n, int k, cudaStream_t st);
 
 // Workspace layout: one 32 x 32 float block per matrix holding the panel's
 // S = V^T V (strictly upper; the compact-WY T factor is T = D (I + S D)^-1,

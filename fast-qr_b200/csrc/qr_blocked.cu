@@ -33,7 +33,7 @@ namespace fqr {
 // Row-major contiguous rows (a_cstride == 1): 32x32 tiles through shared
 // memory so both the reads (rows) and the writes (columns) are coalesced.
 __global__ void __launch_bounds__(256)
-copy_in_rowmajor_kernel(const float *__restrict__ A, int64_t batch, int n, int64_t bs, int64_t rs,
+copy_in_rowmajor_kernel(const float *__restrict__ A, int64_t batch, int m, int n, int64_t bs, int64_t rs,
                         float *__restrict__ H, int *__restrict__ status, int clear)
 {
     __shared__ float tile[32][33];
@@ -44,17 +44,17 @@ copy_in_rowmajor_kernel(const float *__restrict__ A, int64_t batch, int n, int64
     const int j0 = blockIdx.x * 32, i0 = blockIdx.y * 32;
     for (int64_t b = blockIdx.z; b < batch; b += gridDim.z) {
         const float *Am = A + b * bs;
-        float *Hm = H + b * (int64_t)n * n;
+        float *Hm = H + b * (int64_t)m * n;
 #pragma unroll
         for (int r = ty; r < 32; r += 8) {
             const int i = i0 + r, j = j0 + tx;
-            tile[r][tx] = (i < n && j < n) ? __ldg(Am + (int64_t)i * rs + j) : 0.0f;
+            tile[r][tx] = (i < m && j < n) ? __ldg(Am + (int64_t)i * rs + j) : 0.0f;
         }
         __syncthreads();
 #pragma unroll
         for (int r = ty; r < 32; r += 8) {
             const int j = j0 + r, i = i0 + tx;
-            if (i < n && j < n) Hm[(int64_t)j * n + i] = tile[tx][r];
+            if (i < m && j < n) Hm[(int64_t)j * m + i] = tile[tx][r];
         }
         __syncthreads();
     }
@@ -63,34 +63,33 @@ copy_in_rowmajor_kernel(const float *__restrict__ A, int64_t batch, int n, int64
 // Any other strides (column-major input included): one thread per element,
 // writes coalesced along columns of H.
 __global__ void __launch_bounds__(256)
-copy_in_strided_kernel(const float *__restrict__ A, int64_t batch, int n, int64_t bs, int64_t rs,
+copy_in_strided_kernel(const float *__restrict__ A, int64_t batch, int m, int n, int64_t bs, int64_t rs,
                        int64_t cs, float *__restrict__ H, int *__restrict__ status, int clear)
 {
     pdl_trigger();
     if (status && blockIdx.x == 0 && threadIdx.x < clear) status[threadIdx.x] = 0;
-    const int64_t nn = (int64_t)n * n;
-    const int64_t total = batch * nn;
+    const int64_t mn = (int64_t)m * n;
+    const int64_t total = batch * mn;
     for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
          e += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t b = e / nn;
-        const int64_t r = e - b * nn;
-        const int64_t j = r / n, i = r - j * n;
+        const int64_t b = e / mn;
+        const int64_t r = e - b * mn;
+        const int64_t j = r / m, i = r - j * m;
         H[e] = __ldg(A + b * bs + i * rs + j * cs);
     }
 }
 
-cudaError_t launch_copy_in(const float *A, int64_t batch, int n, int64_t bs, int64_t rs, int64_t cs,
+cudaError_t launch_copy_in(const float *A, int64_t batch, int m, int n, int64_t bs, int64_t rs, int64_t cs,
                            float *H, int *status, int clear, cudaStream_t st)
 {
     if (cs == 1) {
-        const unsigned t = (unsigned)((n + 31) / 32);
-        dim3 grid(t, t, (unsigned)(batch < 65535 ? batch : 65535));
-        copy_in_rowmajor_kernel<<<grid, 256, 0, st>>>(A, batch, n, bs, rs, H, status, clear);
+        dim3 grid((unsigned)((n + 31) / 32), (unsigned)((m + 31) / 32), (unsigned)(batch < 65535 ? batch : 65535));
+        copy_in_rowmajor_kernel<<<grid, 256, 0, st>>>(A, batch, m, n, bs, rs, H, status, clear);
     } else {
-        const int64_t total = batch * (int64_t)n * n;
+        const int64_t total = batch * (int64_t)m * n;
         int64_t blocks = (total + 255) / 256;
         if (blocks > 148 * 64) blocks = 148 * 64;
-        copy_in_strided_kernel<<<(unsigned)blocks, 256, 0, st>>>(A, batch, n, bs, rs, cs, H, status, clear);
+        copy_in_strided_kernel<<<(unsigned)blocks, 256, 0, st>>>(A, batch, m, n, bs, rs, cs, H, status, clear);
     }
     return cudaGetLastError();
 }
@@ -102,7 +101,7 @@ cudaError_t launch_copy_in(const float *A, int64_t batch, int n, int64_t bs, int
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256)
 trailing_simt_kernel(float *__restrict__ H, const float *__restrict__ Sws, const float *__restrict__ tau,
-                     int n, int k)
+                     int ld, int n, int k)
 {
     __shared__ float Vs[32][33];
     __shared__ float Cs[32][33];
@@ -112,8 +111,8 @@ trailing_simt_kernel(float *__restrict__ H, const float *__restrict__ Sws, const
     const int64_t mat = blockIdx.y;
     const int c0 = k + kPanel + blockIdx.x * 32;
     const int nct = (n - c0) < 32 ? (n - c0) : 32;
-    const int m = n - k;
-    float *Hm = H + mat * (int64_t)n * n;
+    const int m = ld - k;  // rows k .. ld-1 (ld = the matrix's row count)
+    float *Hm = H + mat * (int64_t)ld * n;
     pdl_wait();  // the panel (and everything before it) has completed
 
     auto load_chunk = [&](int r0) {
@@ -122,9 +121,9 @@ trailing_simt_kernel(float *__restrict__ H, const float *__restrict__ Sws, const
         for (int i = 0; i < 4; ++i) {
             const int j = tg + 8 * i;
             float v = 0.0f;
-            if (rr < m) v = rr > j ? Hm[(int64_t)(k + j) * n + k + rr] : (rr == j ? 1.0f : 0.0f);
+            if (rr < m) v = rr > j ? Hm[(int64_t)(k + j) * ld + k + rr] : (rr == j ? 1.0f : 0.0f);
             Vs[lane][j] = v;
-            Cs[lane][j] = (rr < m && j < nct) ? Hm[(int64_t)(c0 + j) * n + k + rr] : 0.0f;
+            Cs[lane][j] = (rr < m && j < nct) ? Hm[(int64_t)(c0 + j) * ld + k + rr] : 0.0f;
         }
     };
 
@@ -187,13 +186,13 @@ trailing_simt_kernel(float *__restrict__ H, const float *__restrict__ Sws, const
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const int j = tg + 8 * i;
-            if (rr < m && j < nct) Hm[(int64_t)(c0 + j) * n + k + rr] = Cs[lane][j];
+            if (rr < m && j < nct) Hm[(int64_t)(c0 + j) * ld + k + rr] = Cs[lane][j];
         }
         __syncthreads();
     }
 }
 
-cudaError_t launch_trailing(float *H, const float *Sws, const float *tau, int64_t batch, int n, int k,
+cudaError_t launch_trailing(float *H, const float *Sws, const float *tau, int64_t batch, int m, int n, int k,
                             cudaStream_t st)
 {
     const int nc = n - k - kPanel;
@@ -203,8 +202,8 @@ cudaError_t launch_trailing(float *H, const float *Sws, const float *tau, int64_
         const int64_t nb = (batch - b0) < 65535 ? (batch - b0) : 65535;
         dim3 grid(tiles, (unsigned)nb);
         cudaError_t e = launch_dependent(trailing_simt_kernel, grid, dim3(256), 0, st, nullptr, 0,
-                                         H + b0 * (int64_t)n * n, Sws + b0 * kPanel * kPanel, tau + b0 * n,
-                                         n, k);
+                                         H + b0 * (int64_t)m * n, Sws + b0 * kPanel * kPanel, tau + b0 * n,
+                                         m, n, k);
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;

@@ -1,4 +1,4 @@
-// Panel factorisation of the blocked QR: 32 columns, n - k rows, one CTA per
+// Panel factorisation of the blocked QR: 32 columns, m - k rows, one CTA per
 // matrix (a thread-block cluster for panels taller than 1024 rows).
 // The reference's panel_factor_kernel (submissions/candidate.py:2404-2505)
 // works column by column on global memory with block-wide reductions and
@@ -46,7 +46,7 @@ constexpr int kStagePitch = 36;  // floats per row of a warp's 32 x 32 staging b
 // ---------------------------------------------------------------------------
 template <int NW, int R, bool CLUSTER>
 __global__ void __launch_bounds__(NW * 32, 1)
-panel_kernel(float *__restrict__ H, float *__restrict__ tau, float *__restrict__ Tws, int n, int k)
+panel_kernel(float *__restrict__ H, float *__restrict__ tau, float *__restrict__ Tws, int ld, int n, int k)
 {
     constexpr int ROWS = NW * 32 * R;  // panel rows held by one CTA
     constexpr int NR = 8 * R;          // rows per thread
@@ -71,9 +71,11 @@ panel_kernel(float *__restrict__ H, float *__restrict__ tau, float *__restrict__
         ncl = (int)cl.num_blocks();
     }
     const int64_t mat = blockIdx.x / ncl;
-    const int m = n - k;
-    const int w = m < kPanel ? m : kPanel;
-    float *Hm = H + mat * (int64_t)n * n;
+    const int m = ld - k;  // panel rows (ld = the matrix's row count, >= n)
+    // reflectors of this panel: the columns left, at most 32 (and never more
+    // than the rows)
+    const int w = min(kPanel, min(m, n - k));
+    float *Hm = H + mat * (int64_t)ld * n;
     const bool top = crank == 0 && wid == 0;  // holds panel rows 0..31
     // per-warp staging of one 32 x 32 block, row-major with a 36-float pitch:
     // 16-byte accesses by 8 consecutive lanes (one column group each, or one
@@ -92,14 +94,14 @@ panel_kernel(float *__restrict__ H, float *__restrict__ tau, float *__restrict__
 #pragma unroll
     for (int b = 0; b < R; ++b) {
         const int r = crank * ROWS + b * (NW * 32) + wid * 32 + lane;
-        const float *src = Hm + (int64_t)k * n + k + r;
+        const float *src = Hm + (int64_t)k * ld + k + r;
 #pragma unroll
         for (int t = 0; t < 8; ++t) {
             float v[4];
 #pragma unroll
             for (int jj = 0; jj < 4; ++jj) {
                 const int col = 4 * t + jj;
-                v[jj] = (r < m && col < w) ? src[(int64_t)col * n] : 0.0f;
+                v[jj] = (r < m && col < w) ? src[(int64_t)col * ld] : 0.0f;
             }
             *reinterpret_cast<float4 *>(stg + lane * kStagePitch + 4 * t) = make_float4(v[0], v[1], v[2], v[3]);
         }
@@ -315,7 +317,7 @@ panel_kernel(float *__restrict__ H, float *__restrict__ tau, float *__restrict__
                 make_float4(p[b * 8 + i][0], p[b * 8 + i][1], p[b * 8 + i][2], p[b * 8 + i][3]);
         __syncwarp();
         const int r = crank * ROWS + b * (NW * 32) + wid * 32 + lane;
-        float *dst = Hm + (int64_t)k * n + k + r;
+        float *dst = Hm + (int64_t)k * ld + k + r;
 #pragma unroll
         for (int t = 0; t < 8; ++t) {
             const float4 v = *reinterpret_cast<const float4 *>(stg + lane * kStagePitch + 4 * t);
@@ -323,7 +325,7 @@ panel_kernel(float *__restrict__ H, float *__restrict__ tau, float *__restrict__
 #pragma unroll
             for (int jj = 0; jj < 4; ++jj) {
                 const int col = 4 * t + jj;
-                if (r < m && col < w) dst[(int64_t)col * n] = e[jj];
+                if (r < m && col < w) dst[(int64_t)col * ld] = e[jj];
             }
         }
         __syncwarp();
@@ -352,7 +354,7 @@ PanelShape panel_shape(int m)
 }
 
 template <int NW, int R>
-static cudaError_t launch_panel_t(float *H, float *tau, float *Tws, int64_t batch, int n, int k,
+static cudaError_t launch_panel_t(float *H, float *tau, float *Tws, int64_t batch, int ld, int n, int k,
                                   int cluster, cudaStream_t st)
 {
     // the limit covers static + dynamic shared memory beyond 48 KB, so it is
@@ -363,7 +365,7 @@ static cudaError_t launch_panel_t(float *H, float *tau, float *Tws, int64_t batc
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);
         if (e != cudaSuccess) return e;
         return launch_dependent(panel_kernel<NW, R, false>, dim3((unsigned)batch), dim3(NW * 32), dyn, st,
-                                nullptr, 0, H, tau, Tws, n, k);
+                                nullptr, 0, H, tau, Tws, ld, n, k);
     }
     cudaError_t e = cudaFuncSetAttribute(panel_kernel<NW, R, true>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);
@@ -374,19 +376,19 @@ static cudaError_t launch_panel_t(float *H, float *tau, float *Tws, int64_t batc
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     return launch_dependent(panel_kernel<NW, R, true>, dim3((unsigned)(batch * cluster)), dim3(NW * 32), dyn,
-                            st, attr, 1, H, tau, Tws, n, k);
+                            st, attr, 1, H, tau, Tws, ld, n, k);
 }
 
-cudaError_t launch_panel(float *H, float *tau, float *Tws, int64_t batch, int n, int k,
+cudaError_t launch_panel(float *H, float *tau, float *Tws, int64_t batch, int ld, int n, int k,
                          cudaStream_t st)
 {
-    const PanelShape s = panel_shape(n - k);
+    const PanelShape s = panel_shape(ld - k);
     if (s.cluster > 8) return cudaErrorInvalidValue;
     if (s.warps == 4 && s.rows_per_thread_blocks == 1)
-        return launch_panel_t<4, 1>(H, tau, Tws, batch, n, k, 1, st);
-    if (s.warps == 4) return launch_panel_t<4, 2>(H, tau, Tws, batch, n, k, 1, st);
-    if (s.warps == 8) return launch_panel_t<8, 2>(H, tau, Tws, batch, n, k, s.cluster, st);
-    return launch_panel_t<16, 2>(H, tau, Tws, batch, n, k, s.cluster, st);
+        return launch_panel_t<4, 1>(H, tau, Tws, batch, ld, n, k, 1, st);
+    if (s.warps == 4) return launch_panel_t<4, 2>(H, tau, Tws, batch, ld, n, k, 1, st);
+    if (s.warps == 8) return launch_panel_t<8, 2>(H, tau, Tws, batch, ld, n, k, s.cluster, st);
+    return launch_panel_t<16, 2>(H, tau, Tws, batch, ld, n, k, s.cluster, st);
 }
 
 }  // namespace fqr

@@ -157,7 +157,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmV,
                    const __grid_constant__ CUtensorMap tmCQ, const float *__restrict__ H,
                    const float *__restrict__ Sws, int64_t s_stride, const float *__restrict__ tau,
-                   int *__restrict__ status, int n, int k, int c_begin, int c_end, int64_t b0,
+                   int *__restrict__ status, int ld, int hcols, int k, int c_begin, int c_end, int64_t b0,
                    int flags)
 {
     const bool early_trigger = flags & kFlagEarlyTrigger;
@@ -171,10 +171,12 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
     // touches only the tile's own columns
     const int c0 = c_begin + blockIdx.x * kTN;  // first column of the tile
     const int nct = min(kTN, c_end - c0);
-    const int m = n - k;                           // rows k .. n-1
-    const int wv = min(kPanel, m);                 // reflectors of the panel
-    const float *Hm = H + mat * (int64_t)n * n;
-    const float *Vbase = Hm + (int64_t)k * n + k;   // V(r, j) at Vbase[j * n + r]
+    // H: ld rows x hcols columns per matrix (column-major); the reflectors of
+    // columns k .. k+31 (fewer at the end), tau hcols values per matrix
+    const int m = ld - k;                          // rows k .. ld-1
+    const int wv = min(kPanel, min(m, hcols - k));  // reflectors of the panel
+    const float *Hm = H + mat * (int64_t)ld * hcols;
+    const float *Vbase = Hm + (int64_t)k * ld + k;  // V(r, j) at Vbase[j * ld + r]
 
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + kOffBar);  // [kStages]
     uint64_t *mmab = full + kStages;                                // [2]
@@ -213,7 +215,7 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
         }
     }
     float tau_r = 0.0f;
-    if (tid < wv) tau_r = tau[mat * n + k + tid];  // stored to shared memory after phase A
+    if (tid < wv) tau_r = tau[mat * hcols + k + tid];  // stored to shared memory after phase A
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
@@ -292,7 +294,7 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
     // end of [c_begin, c_end)) must not touch the quarters beyond c_end
     const int nqc = (nct + kCQCols - 1) / kCQCols;
     float e[kPanel];  // V rows of the next phase-C chunk
-    if (ok) load_v_rows(Vbase, n, 0, m, wv, tid, e);
+    if (ok) load_v_rows(Vbase, ld, 0, m, wv, tid, e);
 
     // ---- phase B: Y = T^T W, thread = tile column c ------------------------
     if (ok) {
@@ -377,7 +379,7 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
     if (ok) {
         ok = !__syncthreads_or(false);  // Y and V(0) staged
         issue_c(0);
-        if (ncc > 1) load_v_rows(Vbase, n, kRCC, m, wv, tid, e);
+        if (ncc > 1) load_v_rows(Vbase, ld, kRCC, m, wv, tid, e);
     }
     for (int j = 0; j < ncc && ok; ++j) {
         const bool done = tc::mbar_wait(cbar, c_waited & 1u, kWaitLimit);
@@ -389,7 +391,7 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
         ok = !__syncthreads_or(!done);
         if (!ok) break;
         if (j + 1 < ncc) issue_c(j + 1);
-        if (j + 2 < ncc) load_v_rows(Vbase, n, (j + 2) * kRCC, m, wv, tid, e);
+        if (j + 2 < ncc) load_v_rows(Vbase, ld, (j + 2) * kRCC, m, wv, tid, e);
         tc::fence_after_sync();
         const uint32_t pc = tmem + ((uint32_t)(32 * warp) << 16) + ((j & 1) ? kDP1 : kDP0);
         // epilogue: thread = row j * 128 + tid of the tile.  -P goes to a
@@ -444,9 +446,9 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
     }
 }
 
-bool trailing_tc_supported(int n)
+bool trailing_tc_supported(int ld)
 {
-    return n % 4 == 0 && n >= 128;
+    return ld % 4 == 0 && ld >= 128;
 }
 
 namespace {
@@ -469,16 +471,16 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder()
 
 }  // namespace
 
-cudaError_t prepare_apply_maps(const float *H, int n, float *C, int64_t c_cols, int64_t batch,
+cudaError_t prepare_apply_maps(const float *H, int ld, int hcols, float *C, int64_t c_cols, int64_t batch,
                                TrailingMaps *maps)
 {
     PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
     if (!enc) return cudaErrorNotSupported;
     // H and C as 3-D tensors: x = row (contiguous), y = column, z = matrix
-    const cuuint64_t hdims[3] = {(cuuint64_t)n, (cuuint64_t)n, (cuuint64_t)batch};
-    const cuuint64_t hstrides[2] = {(cuuint64_t)n * 4, (cuuint64_t)n * (cuuint64_t)n * 4};
-    const cuuint64_t cdims[3] = {(cuuint64_t)n, (cuuint64_t)c_cols, (cuuint64_t)batch};
-    const cuuint64_t cstrides[2] = {(cuuint64_t)n * 4, (cuuint64_t)n * (cuuint64_t)c_cols * 4};
+    const cuuint64_t hdims[3] = {(cuuint64_t)ld, (cuuint64_t)hcols, (cuuint64_t)batch};
+    const cuuint64_t hstrides[2] = {(cuuint64_t)ld * 4, (cuuint64_t)ld * (cuuint64_t)hcols * 4};
+    const cuuint64_t cdims[3] = {(cuuint64_t)ld, (cuuint64_t)c_cols, (cuuint64_t)batch};
+    const cuuint64_t cstrides[2] = {(cuuint64_t)ld * 4, (cuuint64_t)ld * (cuuint64_t)c_cols * 4};
     const cuuint32_t box_c[3] = {kRC, kTN, 1}, box_v[3] = {kRC, kPanel, 1}, unit[3] = {1, 1, 1};
     const cuuint32_t box_cq[3] = {kRCC, kCQCols, 1};
     if (enc(&maps->c, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, C, cdims, cstrides, box_c, unit,
@@ -494,20 +496,20 @@ cudaError_t prepare_apply_maps(const float *H, int n, float *C, int64_t c_cols, 
     return cudaSuccess;
 }
 
-cudaError_t prepare_trailing_tc(float *H, int64_t batch, int n, TrailingMaps *maps)
+cudaError_t prepare_trailing_tc(float *H, int64_t batch, int m, int n, TrailingMaps *maps)
 {
-    return prepare_apply_maps(H, n, H, n, batch, maps);
+    return prepare_apply_maps(H, m, n, H, n, batch, maps);
 }
 
 // Static plan by n: a large launch triggers the next kernel early (its CTAs
 // are placed while the last wave finishes).
-static int trailing_flags(int n) { return n > 256 ? kFlagEarlyTrigger : 0; }
+static int trailing_flags(int ld) { return ld > 256 ? kFlagEarlyTrigger : 0; }
 
 cudaError_t launch_apply_tc(const TrailingMaps &maps, const float *H, const float *Sws, int64_t s_stride,
-                            const float *tau, int *status, int64_t batch, int n, int k, int c_begin,
+                            const float *tau, int *status, int64_t batch, int ld, int hcols, int k, int c_begin,
                             int c_end, bool apply_t, cudaStream_t st)
 {
-    if (c_end <= c_begin || k >= n) return cudaSuccess;
+    if (c_end <= c_begin || k >= hcols || k >= ld) return cudaSuccess;
     auto kern = apply_t ? trailing_tc_kernel<true> : trailing_tc_kernel<false>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
     if (e != cudaSuccess) return e;
@@ -516,17 +518,17 @@ cudaError_t launch_apply_tc(const TrailingMaps &maps, const float *H, const floa
         const int64_t nb = (batch - b0) < 65535 ? (batch - b0) : 65535;
         dim3 grid(tiles, (unsigned)nb);
         e = launch_dependent(kern, grid, dim3(kThreads), kSmem, st, nullptr, 0, maps.c, maps.v, maps.cq, H, Sws,
-                             s_stride, tau, status, n, k, c_begin, c_end, b0, trailing_flags(n));
+                             s_stride, tau, status, ld, hcols, k, c_begin, c_end, b0, trailing_flags(ld));
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;
 }
 
 cudaError_t launch_trailing_tc(const TrailingMaps &maps, float *H, const float *Sws, const float *tau,
-                               int *status, int64_t batch, int n, int k, cudaStream_t st)
+                               int *status, int64_t batch, int m, int n, int k, cudaStream_t st)
 {
     if (n - k - kPanel <= 0) return cudaSuccess;
-    return launch_apply_tc(maps, H, Sws, kPanel * kPanel, tau, status, batch, n, k, k + kPanel, n, true, st);
+    return launch_apply_tc(maps, H, Sws, kPanel * kPanel, tau, status, batch, m, n, k, k + kPanel, n, true, st);
 }
 
 }  // namespace fqr

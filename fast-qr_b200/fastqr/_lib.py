@@ -24,6 +24,9 @@ SIGNATURES = {
     "fqr_host_workspace_bytes": (ctypes.c_size_t, [_i64, _i64]),
     "fqr_host_check_status": (ctypes.c_int, [_p, ctypes.c_size_t, _i64, _i64, _p]),
     "fqr_workspace_bytes": (ctypes.c_size_t, [_i64, _i64]),
+    "fqr_geqrf_rect_workspace_bytes": (ctypes.c_size_t, [_i64, _i64, _i64]),
+    "fqr_geqrf_rect_f32": (ctypes.c_int, [_p, _i64, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, ctypes.c_size_t,
+                                          _p]),
     "fqr_orgqr_workspace_bytes": (ctypes.c_size_t, [_i64, _i64]),
     "fqr_orgqr_f32": (ctypes.c_int, [_p, _p, _i64, _i64, _p, _p, ctypes.c_size_t, _p]),
     "fqr_ormqr_f32": (ctypes.c_int, [_p, _p, _i64, _i64, _p, _i64, ctypes.c_int, _p, ctypes.c_size_t, _p]),

@@ -20,7 +20,7 @@ import torch
 from ._lib import FastQRError, load
 
 
-def _check_input(a: torch.Tensor) -> torch.Tensor:
+def _check_input(a: torch.Tensor, square: bool = True) -> torch.Tensor:
     if not isinstance(a, torch.Tensor):
         raise TypeError("input must be a torch.Tensor")
     if a.device.type != "cuda":
@@ -29,13 +29,19 @@ def _check_input(a: torch.Tensor) -> torch.Tensor:
         raise ValueError(f"input dtype must be torch.float32, got {a.dtype}")
     if a.ndim == 2:
         a = a.unsqueeze(0)
-    if a.ndim != 3 or a.shape[-1] != a.shape[-2]:
+    if square and (a.ndim != 3 or a.shape[-1] != a.shape[-2]):
         raise ValueError(f"input must have shape (batch, n, n), got {tuple(a.shape)}")
+    if not square and (a.ndim != 3 or a.shape[-2] < a.shape[-1]):
+        raise ValueError(f"input must have shape (batch, m, n) with m >= n, got {tuple(a.shape)}")
     return a
 
 
-def workspace_bytes(batch: int, n: int) -> int:
-    return int(load().fqr_workspace_bytes(batch, n))
+def workspace_bytes(batch: int, n: int, m: int | None = None) -> int:
+    """Device workspace of geqrf for (batch, n, n), or for (batch, m, n) when
+    ``m`` is given."""
+    if m is None or m == n:
+        return int(load().fqr_workspace_bytes(batch, n))
+    return int(load().fqr_geqrf_rect_workspace_bytes(batch, m, n))
 
 
 def plan(batch: int, n: int) -> str:
@@ -60,27 +66,31 @@ def empty_outputs(batch: int, n: int, device) -> tuple[torch.Tensor, torch.Tenso
 
 def geqrf(a: torch.Tensor, *, out: tuple[torch.Tensor, torch.Tensor] | None = None,
           workspace: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
-    """Batched Householder QR of square float32 CUDA matrices.
+    """Batched Householder QR of float32 CUDA matrices, square (batch, n, n)
+    (``fqr_geqrf_f32``) or tall (batch, m, n) with m > n
+    (``fqr_geqrf_rect_f32``).
 
-    Returns ``(H, tau)`` as torch.geqrf does.  ``out`` may supply
-    preallocated outputs (H must have strides (n*n, 1, n)); ``workspace`` a
-    uint8 CUDA tensor of at least ``workspace_bytes(batch, n)`` bytes.
+    Returns ``(H, tau)`` as torch.geqrf does: H (batch, m, n) column-major
+    (strides (m*n, 1, m)), tau (batch, n).  ``out`` may supply preallocated
+    outputs of that layout; ``workspace`` a uint8 CUDA tensor of at least
+    ``workspace_bytes(batch, n, m)`` bytes.  Wide inputs (m < n) raise.
     """
     squeeze = a.ndim == 2
-    a = _check_input(a)
-    batch, n, _ = a.shape
+    a = _check_input(a, square=False)
+    batch, m, n = a.shape
     lib = load()
     if out is None:
-        h, tau = empty_outputs(batch, n, a.device)
+        h = torch.empty_strided((batch, m, n), (m * n, 1, m), device=a.device, dtype=torch.float32)
+        tau = torch.empty((batch, n), device=a.device, dtype=torch.float32)
     else:
         h, tau = out
-        if h.shape != (batch, n, n) or h.stride() != (n * n, 1, n) or h.dtype != torch.float32:
-            raise ValueError("out H must be float32 (batch, n, n) with strides (n*n, 1, n)")
+        if h.shape != (batch, m, n) or h.stride() != (m * n, 1, m) or h.dtype != torch.float32:
+            raise ValueError("out H must be float32 (batch, m, n) with strides (m*n, 1, m)")
         if tau.shape != (batch, n) or not tau.is_contiguous() or tau.dtype != torch.float32:
             raise ValueError("out tau must be contiguous float32 (batch, n)")
         if h.device != a.device or tau.device != a.device:
             raise ValueError("outputs must be on the input's device")
-    need = int(lib.fqr_workspace_bytes(batch, n))
+    need = workspace_bytes(batch, n, m)
     if need:
         if workspace is None:
             workspace = torch.empty(need, dtype=torch.uint8, device=a.device)
@@ -92,8 +102,12 @@ def geqrf(a: torch.Tensor, *, out: tuple[torch.Tensor, torch.Tensor] | None = No
     with torch.cuda.device(a.device):
         stream = torch.cuda.current_stream(a.device).cuda_stream
         bs, rs, cs = a.stride()
-        rc = lib.fqr_geqrf_f32(a.data_ptr(), batch, n, bs, rs, cs, h.data_ptr(), tau.data_ptr(),
-                               ws_ptr, ws_len, stream)
+        if m == n:
+            rc = lib.fqr_geqrf_f32(a.data_ptr(), batch, n, bs, rs, cs, h.data_ptr(), tau.data_ptr(),
+                                   ws_ptr, ws_len, stream)
+        else:
+            rc = lib.fqr_geqrf_rect_f32(a.data_ptr(), batch, m, n, bs, rs, cs, h.data_ptr(), tau.data_ptr(),
+                                        ws_ptr, ws_len, stream)
     if rc:
         raise FastQRError(rc)
     if squeeze:

@@ -171,6 +171,23 @@ int fqr_ormqr_f32(const float *H, const float *tau, int64_t batch, int64_t n, fl
                   int transpose, void *workspace, size_t workspace_bytes, void *stream);
 
 /*
+ * Rectangular batched QR, m >= n: torch.geqrf on [batch, m, n].  Replaces the
+ * reference's tall-block geqrf, torch.geqrf(data[:, :, :cols]) in
+ * _embedded_rectangular_geqrf (submissions/candidate.py:7204-7214).
+ *   A:   any strides, element (b, i, j) at A[b*a_bstride + i*a_rstride + j*a_cstride]
+ *   H:   m x n column-major per matrix, H[b*m*n + j*m + i] (strides (m*n, 1, m))
+ *   tau: [batch][n]
+ * m == n is exactly fqr_geqrf_f32.  m < n returns FQR_EUNSUPPORTED.  Both
+ * m and n are at most FQR_MAX_N.  The workspace is
+ * fqr_geqrf_rect_workspace_bytes(batch, m, n) bytes, 256-byte aligned; the
+ * status word for fqr_check_status sits in it as for fqr_geqrf_f32.
+ */
+size_t fqr_geqrf_rect_workspace_bytes(int64_t batch, int64_t m, int64_t n);
+int fqr_geqrf_rect_f32(const float *A, int64_t batch, int64_t m, int64_t n, int64_t a_bstride,
+                       int64_t a_rstride, int64_t a_cstride, float *H, float *tau, void *workspace,
+                       size_t workspace_bytes, void *stream);
+
+/*
  * Synchronizes `stream`, then reports whether the last fqr_geqrf_f32 that
  * used `workspace` (for `batch` matrices) hit a bounded device-side wait that
  * gave up: FQR_OK or FQR_ETIMEOUT.  The tensor-core kernels never spin

@@ -11,7 +11,9 @@ wheel: LAPACK xGEQRF as shipped by MKL 2024.2 in torch 2.11):
 * ``geqrf_f64`` / ``geqrf_f32``: unblocked Householder QR, LAPACK xGEQR2 +
   xLARFG semantics -- the arithmetic behind ``torch.geqrf``, which is the
   reference's own contract (official/reference.py:125-127 ``ref_kernel``,
-  submissions/baseline_geqrf.py:5-6).
+  submissions/baseline_geqrf.py:5-6).  ``geqrf_rect_f64``: the same for
+  m x n matrices (the reference's embedded rectangular geqrf routes,
+  submissions/candidate.py:7204-7214), pinned against numpy's LAPACK.
 * ``geqrf_blocked_f64``: the compact-WY blocked variant of
   tools/blocked_qr_reference.py:98-122,192-262 (the algorithm the GPU
   blocked path executes).
@@ -60,6 +62,8 @@ def _load():
         fn = getattr(lib, name)
         fn.argtypes = [_i64, _i64, _p, _i64, _i64, _i64, _p, _p]
         fn.restype = ctypes.c_int
+    lib.oracle_geqrf_rect_f64.argtypes = [_i64, _i64, _i64, _p, _i64, _i64, _i64, _p, _p]
+    lib.oracle_geqrf_rect_f64.restype = ctypes.c_int
     lib.oracle_geqrf_blocked_f64.argtypes = [_i64, _i64, _i64, _p, _i64, _i64, _i64, _p, _p]
     lib.oracle_geqrf_blocked_f64.restype = ctypes.c_int
     for name in ("oracle_orgqr_f64", "oracle_orgqr_f32"):
@@ -110,6 +114,23 @@ def geqrf_f32(a):
     rc = _load().oracle_geqrf_f32(b, n, a.ctypes.data, bs, rs, cs, h.ctypes.data, tau.ctypes.data)
     if rc:
         raise RuntimeError(f"oracle_geqrf_f32 failed: {rc}")
+    return _colmajor(h), tau
+
+
+def geqrf_rect_f64(a):
+    """Householder QR of float32[b, m, n] (any m, n) in double arithmetic.
+    Returns (H float64 [b, m, n] logical view of column-major memory,
+    tau float64 [b, min(m, n)])."""
+    a = np.asarray(a)
+    if a.dtype != np.float32 or a.ndim != 3:
+        raise ValueError("A must be float32 with shape (batch, m, n)")
+    b, m, n = a.shape
+    h = np.empty((b, n, m), dtype=np.float64)  # [b][j][i]
+    tau = np.empty((b, min(m, n)), dtype=np.float64)
+    bs, rs, cs = _strides(a)
+    rc = _load().oracle_geqrf_rect_f64(b, m, n, a.ctypes.data, bs, rs, cs, h.ctypes.data, tau.ctypes.data)
+    if rc:
+        raise RuntimeError(f"oracle_geqrf_rect_f64 failed: {rc}")
     return _colmajor(h), tau
 
 

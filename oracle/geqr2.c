@@ -181,6 +181,29 @@ int oracle_geqrf_f32(int64_t batch, int64_t n, const float *A, int64_t a_bs, int
     return ORACLE_OK;
 }
 
+/* Batched geqrf of m x n matrices (any m, n) in double arithmetic, the   */
+/* same xGEQR2 steps (min(m, n) reflectors): H is column-major m x n per  */
+/* matrix (float64), tau holds min(m, n) values per matrix.               */
+int oracle_geqrf_rect_f64(int64_t batch, int64_t m, int64_t n, const float *A, int64_t a_bs,
+                          int64_t a_rs, int64_t a_cs, double *H, double *tau)
+{
+    if (batch < 0 || m < 0 || n < 0) return ORACLE_EINVAL;
+    if (batch > 0 && m > 0 && n > 0 && (!A || !H || !tau)) return ORACLE_EINVAL;
+    const int64_t kmax = m < n ? m : n;
+    double *work = (double *)malloc(sizeof(double) * (size_t)(2 * n + 1));
+    if (!work) return ORACLE_ENOMEM;
+    double *tk = work + n;  /* geqr2_d writes n tau values */
+    for (int64_t b = 0; b < batch; ++b) {
+        double *h = H + b * m * n;
+        for (int64_t j = 0; j < n; ++j)
+            for (int64_t i = 0; i < m; ++i) h[j * m + i] = (double)A[b * a_bs + i * a_rs + j * a_cs];
+        geqr2_d(m, n, h, m > 0 ? m : 1, tk, work);
+        for (int64_t k = 0; k < kmax; ++k) tau[b * kmax + k] = tk[k];
+    }
+    free(work);
+    return ORACLE_OK;
+}
+
 /* ---------------------------------------------------------------------- */
 /* Blocked compact-WY QR, double arithmetic.  The panel algorithm of      */
 /* tools/blocked_qr_reference.py:192-262 (update_mode="compact-wy"):      */

@@ -17,7 +17,10 @@ EPS32 = torch.finfo(torch.float32).eps
 
 @torch.no_grad()
 def gates(a: torch.Tensor, h: torch.Tensor, tau: torch.Tensor, chunk: int = 8) -> dict:
-    batch, n, _ = a.shape
+    """Square (batch, n, n) or tall (batch, m, n) inputs: Q is the m x n thin
+    factor, R the leading n x n upper triangle of H, and the official scales
+    use m (= n for the square case)."""
+    batch, m, n = a.shape
     worst = {"factor_scaled": 0.0, "orth_scaled": 0.0, "recon_rel_f": 0.0, "orth_rel_f": 0.0,
              "factor_ok": True, "finite": True}
     eye = torch.eye(n, device=a.device, dtype=torch.float64)
@@ -26,16 +29,16 @@ def gates(a: torch.Tensor, h: torch.Tensor, tau: torch.Tensor, chunk: int = 8) -
         hs, ts, as_ = h[s:e], tau[s:e], a[s:e].double()
         worst["finite"] &= bool(torch.isfinite(hs).all()) and bool(torch.isfinite(ts).all())
         q = torch.linalg.householder_product(hs, ts).double()
-        r = torch.triu(hs.double())
+        r = torch.triu(hs.double()[:, :n, :])
         proj = q.transpose(-1, -2) @ as_
         l1 = lambda x: torch.linalg.matrix_norm(x, ord=1, dim=(-2, -1))
         fres = l1(r - proj)
         fscale = l1(as_)
-        fscaled = fres / (EPS32 * n * fscale.clamp_min(1e-30))
-        worst["factor_ok"] &= bool((fres <= 20.0 * n * EPS32 * fscale).all())
+        fscaled = fres / (EPS32 * m * fscale.clamp_min(1e-30))
+        worst["factor_ok"] &= bool((fres <= 20.0 * m * EPS32 * fscale).all())
         worst["factor_scaled"] = max(worst["factor_scaled"], float(fscaled.max()))
         qtq = q.transpose(-1, -2) @ q - eye
-        worst["orth_scaled"] = max(worst["orth_scaled"], float(l1(qtq).max()) / (EPS32 * n))
+        worst["orth_scaled"] = max(worst["orth_scaled"], float(l1(qtq).max()) / (EPS32 * m))
         recon = (q @ r - as_).flatten(1).norm(dim=1) / as_.flatten(1).norm(dim=1).clamp_min(1e-300)
         worst["recon_rel_f"] = max(worst["recon_rel_f"], float(recon.max()))
         worst["orth_rel_f"] = max(worst["orth_rel_f"],

@@ -130,3 +130,28 @@ def test_orgqr_ormqr_validation_without_gpu():
     # one 32 x 32 S block per panel per matrix + a status block
     assert fastqr.orgqr_workspace_bytes(16, 4096) == 16 * 128 * 4096 + 256
     assert fastqr.orgqr_workspace_bytes(3, 100) == 0
+
+
+def test_rect_entry_validation_without_gpu():
+    lib = fastqr.load()
+    dummy = ctypes.c_void_p(16)
+    # wide matrices are not supported; sizes beyond the table neither
+    assert lib.fqr_geqrf_rect_f32(dummy, 1, 8, 16, 128, 16, 1, dummy, dummy, None, 0, None) == 2
+    assert lib.fqr_geqrf_rect_f32(dummy, 1, 8193, 16, 8193 * 16, 16, 1, dummy, dummy, None, 0, None) == 2
+    # null pointers, negative sizes, empty problems
+    assert lib.fqr_geqrf_rect_f32(None, 2, 100, 20, 2000, 20, 1, None, None, None, 0, None) == 1
+    assert lib.fqr_geqrf_rect_f32(None, 2, -1, 20, 2000, 20, 1, None, None, None, 0, None) == 1
+    assert lib.fqr_geqrf_rect_f32(None, 0, 100, 20, 2000, 20, 1, None, None, None, 0, None) == 0
+    # tall matrices always take the blocked path: a workspace is required,
+    # even for n <= 64
+    assert lib.fqr_geqrf_rect_f32(dummy, 1, 100, 20, 2000, 20, 1, dummy, dummy, None, 0, None) == 5
+    assert fastqr.workspace_bytes(4, 20, 100) == 4 * 32 * 32 * 4 + 256
+    assert fastqr.workspace_bytes(4, 20, 20) == 0  # square n <= 64: the small path
+    assert fastqr.workspace_bytes(4, 100, 100) == fastqr.workspace_bytes(4, 100)
+    assert lib.fqr_geqrf_rect_workspace_bytes(4, 10, 20) == 0
+
+
+def test_python_geqrf_rejects_wide_input():
+    import torch
+    with pytest.raises(ValueError):
+        fastqr.geqrf(torch.zeros(2, 8, 16))  # CPU tensor: rejected before any GPU call

@@ -161,3 +161,21 @@ def test_plain_tf32_trailing_update_fails_the_factor_gate(golden):
     rep = checker.check_qr(a, work.astype(np.float32), tau)
     assert not rep.ok
     assert "R - Q.T @ A is too large" in rep.message
+
+
+@pytest.mark.parametrize("b,m,n", [(3, 50, 20), (2, 129, 64), (2, 33, 33), (1, 300, 31), (2, 5, 9)])
+def test_rect_oracle_matches_numpy_lapack(b, m, n):
+    """The m x n restatement (xGEQR2 steps, min(m, n) reflectors) against
+    numpy's LAPACK dgeqrf (np.linalg.qr mode='raw'), and against the square
+    oracle bitwise when m == n."""
+    rng = np.random.default_rng(m * 1000 + n)
+    a = rng.standard_normal((b, m, n)).astype(np.float32)
+    h, t = oracle.geqrf_rect_f64(a)
+    assert h.shape == (b, m, n) and t.shape == (b, min(m, n))
+    for i in range(b):
+        hr, tr = np.linalg.qr(a[i].astype(np.float64), mode="raw")
+        assert np.abs(hr.T - h[i]).max() <= 1e-12 * max(1.0, np.abs(h[i]).max())
+        assert np.abs(tr[:min(m, n)] - t[i]).max() <= 1e-12
+    if m == n:
+        h2, t2 = oracle.geqrf_f64(a)
+        assert np.array_equal(h2, h) and np.array_equal(t2, t)

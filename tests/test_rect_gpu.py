@@ -1,0 +1,104 @@
+"""GPU parity of the rectangular entry (fqr_geqrf_rect_f32, fastqr.geqrf on
+(batch, m, n) with m > n) against the CPU oracle's m x n xGEQR2 restatement
+in float64 (pinned to numpy's LAPACK in tests/test_oracle.py), and the QR
+gates.  The reference calls torch.geqrf on such tall blocks
+(submissions/candidate.py:7204-7214).
+
+Tolerances: per-column relative error of H and tau <= 1e-3 against float64
+on well-conditioned N(0,1) inputs; ||A - QR||_F / ||A||_F <= 1e-4 and
+||Q^T Q - I||_F / sqrt(n) <= 1e-4 (Q the m x n thin factor).
+"""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+import fastqr
+import oracle
+from gpu_gates import column_errors, gates
+
+pytestmark = pytest.mark.gpu
+
+COL_TOL = 1e-3
+
+# small m (panel rows <= 128, SIMT update), m % 4 != 0 (SIMT update),
+# tensor-core update, clusters of panels (m > 1024), one panel (n <= 32)
+SHAPES = [(48, 32), (64, 17), (100, 64), (130, 96), (301, 256), (300, 256), (512, 384),
+          (1000, 128), (1500, 40), (2100, 96), (257, 250)]
+
+
+@pytest.fixture(scope="module")
+def dev():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    fastqr.load()
+    return torch.device("cuda:0")
+
+
+def tall(batch, m, n, seed):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn(batch, m, n, generator=g, dtype=torch.float32)
+
+
+@pytest.mark.parametrize("m,n", SHAPES)
+def test_rect_matches_oracle(m, n, dev):
+    a = tall(3, m, n, 1000 * m + n)
+    h, t = fastqr.geqrf(a.to(dev))
+    torch.cuda.synchronize()
+    assert h.shape == (3, m, n) and h.stride() == (m * n, 1, m) and t.shape == (3, n)
+    h64, t64 = oracle.geqrf_rect_f64(a.numpy())
+    he, te = column_errors(h.cpu(), t.cpu(), torch.from_numpy(np.ascontiguousarray(h64)),
+                           torch.from_numpy(t64))
+    assert float(he.max()) <= COL_TOL and float(te.max()) <= COL_TOL, (float(he.max()), float(te.max()))
+    g = gates(a.to(dev), h, t, chunk=3)
+    assert g["ok"], g
+
+
+@pytest.mark.parametrize("m,n", [(1024, 512), (4096, 256)])
+def test_rect_large_gates(m, n, dev):
+    a = tall(2, m, n, 77 + n).to(dev)
+    h, t = fastqr.geqrf(a)
+    g = gates(a, h, t, chunk=1)
+    assert g["ok"], g
+
+
+def test_rect_batch_split_and_strides(dev):
+    """Batches of two or more run as two halves on two streams; a
+    column-major input takes the strided copy-in; results equal per matrix."""
+    a = tall(5, 300, 200, 9).to(dev)
+    h, t = fastqr.geqrf(a)
+    h1, t1 = fastqr.geqrf(a[3:4])
+    assert torch.equal(h[3:4], h1) and torch.equal(t[3:4], t1)
+    acm = a.transpose(1, 2).contiguous().transpose(1, 2)  # column-major copy
+    h2, t2 = fastqr.geqrf(acm)
+    assert torch.equal(h, h2) and torch.equal(t, t2)
+
+
+def test_rect_entry_with_square_shape_is_the_square_path(dev):
+    a = tall(4, 160, 160, 5).to(dev)
+    h, t = fastqr.geqrf(a)
+    lib = fastqr.load()
+    h2 = torch.empty_strided((4, 160, 160), (160 * 160, 1, 160), device=dev)
+    t2 = torch.empty(4, 160, device=dev)
+    ws = torch.empty(fastqr.workspace_bytes(4, 160, 160), dtype=torch.uint8, device=dev)
+    bs, rs, cs = a.stride()
+    rc = lib.fqr_geqrf_rect_f32(a.data_ptr(), 4, 160, 160, bs, rs, cs, h2.data_ptr(), t2.data_ptr(),
+                                ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert rc == 0
+    assert torch.equal(h, h2) and torch.equal(t, t2)
+
+
+def test_rect_embedded_route_shape(dev):
+    """The reference's embedded route: geqrf of the first `cols` columns of
+    square matrices (a strided view, no copy)."""
+    a = tall(4, 512, 512, 3).to(dev)
+    cols = 384
+    h, t = fastqr.geqrf(a[:, :, :cols])
+    h64, t64 = oracle.geqrf_rect_f64(a[:, :, :cols].cpu().numpy())
+    he, te = column_errors(h.cpu(), t.cpu(), torch.from_numpy(np.ascontiguousarray(h64)),
+                           torch.from_numpy(t64))
+    assert float(he.max()) <= COL_TOL and float(te.max()) <= COL_TOL
+    # the leading columns of the square factorisation are the same reflectors
+    hs, ts = fastqr.geqrf(a)
+    assert float((hs[:, :, :cols] - h).abs().max()) <= 1e-4 * float(hs.abs().max())
