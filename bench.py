@@ -509,6 +509,100 @@ def run_apply_op(args) -> int:
     return 0 if ok else 1
 
 
+def run_rect_op(args) -> int:
+    """--op rect: geqrf of tall m x cols blocks, the first ``cols`` columns of
+    each configuration matrix as a strided view (the reference's embedded
+    rectangular route runs torch.geqrf on data[:, :, :cols]); one process,
+    N=1 only.  Algorithmic work 2 m cols^2 - 2 cols^3 / 3 flops per matrix."""
+    import fastqr
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = inputs.CONFIGS[args.config]
+    m, batch = cfg["n"], cfg["batch"]
+    cols = args.cols or (3 * m) // 4
+    if not 0 < cols <= m:
+        raise SystemExit(f"--cols must be in 1..{m}")
+    steps = args.steps
+    full = inputs.baseline_input(args.config, args.seed, dev)
+    a = full[:, :, :cols]
+    h = torch.empty_strided((batch, m, cols), (m * cols, 1, m), device=dev, dtype=torch.float32)
+    tau = torch.empty((batch, cols), device=dev, dtype=torch.float32)
+    ws = torch.empty(max(1, fastqr.workspace_bytes(batch, cols, m)), dtype=torch.uint8, device=dev)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+
+    def step():
+        return fastqr.geqrf(a, out=(h, tau), workspace=ws)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    chk = min(batch, 8)
+    q = torch.linalg.householder_product(h[:chk], tau[:chk]).double()
+    r = torch.triu(h[:chk, :cols, :].double())
+    ad = a[:chk].double()
+    e1 = float(((q @ r - ad).flatten(1).norm(dim=1) / ad.flatten(1).norm(dim=1)).max())
+    e2 = float(((q.transpose(1, 2) @ q - torch.eye(cols, device=dev, dtype=torch.float64)).flatten(1)
+                .norm(dim=1) / cols ** 0.5).max())
+    gate = {"recon_rel_f": e1, "orth_rel_f": e2}
+    ok = e1 <= 1e-4 and e2 <= 1e-4
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    stream = torch.cuda.current_stream(dev)
+    torch.cuda.synchronize(dev)
+    with ClockSampler(0) as clk:
+        for i in range(steps):
+            flush.fill_(float(i))
+            starts[i].record(stream)
+            step()
+            ends[i].record(stream)
+        torch.cuda.synchronize(dev)
+    clocks = clk.summary()
+    ms = sum(s_.elapsed_time(e_) for s_, e_ in zip(starts, ends)) / steps
+    mps = batch / (ms / 1e3)
+    alg = batch * (2.0 * m * cols * cols - 2.0 * cols ** 3 / 3.0)
+    pk = peaks()
+    tf32 = pk["bf16_tflops"] / 2.0
+    ach = alg / (ms / 1e3) / 1e12
+    cpu = None
+    if not args.no_cpu:
+        threads = os.cpu_count() or 1
+        torch.set_num_threads(threads)
+        ac = a[:min(batch, 32)].cpu().contiguous()
+        torch.geqrf(ac)
+        times = []
+        t_start = time.perf_counter()
+        while len(times) < 3 or time.perf_counter() - t_start < 5.0:
+            t0 = time.perf_counter()
+            torch.geqrf(ac)
+            times.append(time.perf_counter() - t0)
+            if time.perf_counter() - t_start > 20.0:
+                break
+        per = statistics.median(times)
+        cpu = {"value": ac.shape[0] / per, "unit": "matrices/s", "cores": threads, "kind": "reference",
+               "sample": f"torch.geqrf (host LAPACK) on {ac.shape[0]} of the {batch} {m}x{cols} blocks, "
+                         f"median of {len(times)} reps"}
+    # blocked path: per half of the batch a copy-in, the panels and all but the last panel's trailing update
+    panels = -(-cols // 32)
+    launches = (2 if batch >= 2 else 1) * (1 + panels + (panels - 1))
+    line = {
+        "metric": f"matrices/s ({args.config} rect {m}x{cols})", "value": mps, "unit": "matrices/s",
+        "n_gpus": 1, "steps": steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded, the reference generator's distributions)",
+        "config": {"workload": f"{args.config} first {cols} columns: {cfg['desc']}", "op": "rect", "m": m,
+                   "n": cols, "batch_per_gpu": batch,
+                   "l2": f"flushed before every step ({L2_FLUSH_BYTES >> 20} MiB write)"},
+        "verified": ok, "gate": gate,
+        "roofline": {"kernel": "geqrf (whole op)", "bound": "tensor", "achieved": ach, "peak": tf32,
+                     "unit": "TFLOP/s", "frac": ach / tf32, "traffic": None,
+                     "peak_source": pk["source"] + "; TF32 dense peak taken as measured bf16 / 2"},
+        "cpu_baseline": cpu, "e2e": None, "gpu_launches": steps * launches, "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+    return 0 if ok else 1
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -518,14 +612,19 @@ def main() -> int:
     ap.add_argument("--impl", default="fastqr", choices=["fastqr", "reference"])
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--op", default="geqrf", choices=["geqrf", "orgqr", "ormqr"],
-                    help="geqrf (the headline); orgqr / ormqr time Q formation / Q^T A from geqrf's factors")
+    ap.add_argument("--cols", type=int, default=None,
+                    help="--op rect: columns of the tall blocks (default 3/4 of n)")
+    ap.add_argument("--op", default="geqrf", choices=["geqrf", "orgqr", "ormqr", "rect"],
+                    help="geqrf (the headline); orgqr / ormqr time Q formation / Q^T A from geqrf's factors; "
+                         "rect times geqrf of the tall blocks A[:, :, :cols]")
     args = ap.parse_args()
     if args.steps is None:
         args.steps = DEFAULT_STEPS[args.config]
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         return run_reference(args)
+    if args.op == "rect":
+        return run_rect_op(args)
     if args.op != "geqrf":
         return run_apply_op(args)
     return run_fastqr(args)
