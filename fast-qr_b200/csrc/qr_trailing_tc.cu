@@ -12,10 +12,10 @@
 //            [V_hi | V_lo] (N=64) and C_lo against V_hi (N=32).  Thread 0
 //            streams the chunks by TMA (tensor maps over H, 128-byte
 //            swizzle: each column's 32 rows are one 128-byte operand row)
-//            through a 3-stage ring; all threads split chunk i into its lo
-//            buffers while the MMAs of chunk i-1 run.  This phase is bound by
-//            shared-memory bandwidth (TMA writes, the split's loads and
-//            stores, the MMAs' operand reads).
+//            through a 4-stage ring; while the MMAs of chunk i-1 run, every
+//            thread loads its column of chunk i from the stage and stores hi
+//            and lo into tensor memory, where the MMAs read their A operand
+//            (only V, the B operand, is read from shared memory).
 //   phase B  Y = T^T W                            per thread (one column c), by
 //            forward substitution with S = V^T V (strict upper) and tau:
 //            T = D (I + S D)^-1, so (I + D S^T) Y = D W
@@ -45,14 +45,18 @@ namespace {
 
 constexpr int kTN = 128;          // trailing columns per CTA
 constexpr int kRC = 32;           // rows per phase-A chunk (MMA K; one 128-byte swizzle row)
-constexpr int kStages = 3;        // phase-A ring of raw chunks
+constexpr int kStages = 4;        // phase-A ring of raw chunks (fills phase C's 96 KB area)
 constexpr int kRCC = 128;         // rows per phase-C chunk (MMA M)
 constexpr int kThreads = 128;
 constexpr uint32_t kTmemCols = 256;
 // phase A accumulates W^T in three parts: kDA holds C_hi^T [V_hi | V_lo]
-// (64 columns: the hi*hi then the hi*lo products), kDA2 holds C_lo^T V_hi
+// (64 columns: the hi*hi then the hi*lo products), kDA2 holds C_lo^T V_hi.
+// Its A operands (C_hi^T and C_lo^T of a 32-row chunk: 128 lanes x 32
+// columns each) sit in tensor memory too, double-buffered by chunk parity.
 constexpr uint32_t kDA = 0;
 constexpr uint32_t kDA2 = 64;
+constexpr uint32_t kAHi = 96;   // + 64 * (chunk & 1)
+constexpr uint32_t kALo = 128;  // + 64 * (chunk & 1)
 constexpr uint32_t kDP0 = 0;      // P of even phase-C chunks (128 columns; W is dead by then)
 constexpr uint32_t kDP1 = 128;    // P of odd phase-C chunks
 constexpr uint64_t kWaitLimit = 1000000000ull;  // 1 s of wall time per wait
@@ -63,15 +67,15 @@ constexpr int kFlagEarlyTrigger = 1;
 // shared memory map (bytes, from a 1024-byte aligned base).  Phase A: a ring
 // of kStages chunks, each C^T (128 c x 32 r, 16 KB), V (32 j x 32 r, 4 KB)
 // as raw fp32 in the 128-byte swizzle layout, then V's lo part (4 KB) right
-// after V, so that [V | V_lo] is one N = 64 operand; and two lo buffers of
-// C^T.  Reading C_hi once per K step for both of its products (instead of
-// twice) matters: phase A is bound by shared-memory bandwidth.
+// after V, so that [V | V_lo] is one N = 64 operand.  C's hi and lo parts go
+// from the stage through registers into tensor memory (the MMAs' A
+// operand), so shared memory carries C once by TMA and once to registers:
+// phase A is bound by shared-memory bandwidth.
 constexpr int kCBytes = kTN * kRC * 4;                   // 16 KB
 constexpr int kVBytes = kPanel * kRC * 4;                // 4 KB
 constexpr int kLoadBytes = kCBytes + kVBytes;            // 20 KB arrive by TMA per chunk
 constexpr int kStageBytes = kLoadBytes + kVBytes;        // 24 KB
-constexpr int kOffLo = kStages * kStageBytes;            // 72 KB
-constexpr int kOffT = kOffLo + 2 * kCBytes;              // 104 KB: S, column-major 32 x 32 (4 KB)
+constexpr int kOffT = 96 * 1024;                         // S, column-major 32 x 32 (4 KB), after phase C's area
 constexpr int kOffTau = kOffT + 4096;                    // tau of the panel (128 B)
 constexpr int kOffBar = kOffTau + 128;  // mbarriers: full[3], mma[2], phase C; TMEM address
 constexpr int kSmemUsed = kOffBar + 128;
@@ -89,22 +93,46 @@ constexpr int kOffCQ = 65536;
 constexpr int kCQCols = 32;
 constexpr int kCQBytes = kRCC * kCQCols * 4;  // 16 KB
 static_assert(kOffCQ + 2 * kCQBytes <= kOffT, "phase-C buffers overlap S");
+static_assert(kStages * kStageBytes <= kOffT, "phase-A ring overlaps S");
 static_assert(kStageBytes % 1024 == 0 && kCBytes % 1024 == 0, "swizzle atoms need 1024-byte alignment");
 
 constexpr uint32_t kIdescA = tc::idesc_tf32(128, 64, 0, 0);   // A = C^T (M = c), B = [V | V_lo] (N = 2 x j)
 constexpr uint32_t kIdescA2 = tc::idesc_tf32(128, 32, 0, 0);  // A = C_lo^T, B = V
 constexpr uint32_t kIdescC = tc::idesc_tf32(128, 128, 0, 0);  // A = V (M = r), B = Y (N = c)
 
-// lo = x - trunc_tf32(x) over one stage, elementwise (the layout does not
-// matter): C's into the lo buffer, V's into the slot after V.  For the first
-// chunk the V part is also made unit lower triangular in place (panel rows
-// r < j hold R, row j holds beta).
-__device__ __forceinline__ void split_stage(unsigned char *raw, unsigned char *lo, bool first, int tid)
+// The split of one stage (lo = x - trunc_tf32(x)).  C: thread tid owns
+// trailing column c = tid of the tile, i.e. A row tid, whose 32 rows are one
+// 128-byte swizzled row of the stage (16-byte piece q at (q ^ (c & 7)) * 16);
+// it loads them once and stores hi and lo into its TMEM lane (a_hi / a_lo are
+// the warp's lane-quarter addresses).  V: elementwise into the slot after V;
+// for the first chunk V is also made unit lower triangular in place (panel
+// rows r < j hold R, row j holds beta).  Every thread of a warp runs the
+// tensor-memory stores (they are warp-collective).
+__device__ __forceinline__ void split_stage(unsigned char *raw, uint32_t a_hi, uint32_t a_lo, bool first,
+                                            int tid)
 {
-#pragma unroll 2
-    for (int off = tid * 16; off < kLoadBytes; off += kThreads * 16) {
+    {
+        float hv[32], lv[32];
+        const unsigned char *row = raw + tid * 128;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const float4 v = *reinterpret_cast<const float4 *>(row + ((q ^ (tid & 7)) << 4));
+            hv[4 * q] = v.x;
+            hv[4 * q + 1] = v.y;
+            hv[4 * q + 2] = v.z;
+            hv[4 * q + 3] = v.w;
+            lv[4 * q] = tc::tf32_lo(v.x);
+            lv[4 * q + 1] = tc::tf32_lo(v.y);
+            lv[4 * q + 2] = tc::tf32_lo(v.z);
+            lv[4 * q + 3] = tc::tf32_lo(v.w);
+        }
+        tc::tmem_st_32x32(a_hi, hv);
+        tc::tmem_st_32x32(a_lo, lv);
+    }
+#pragma unroll
+    for (int off = kCBytes + tid * 16; off < kLoadBytes; off += kThreads * 16) {
         float4 v = *reinterpret_cast<const float4 *>(raw + off);
-        if (first && off >= kCBytes) {
+        if (first) {
             // V row j (= operand row) at (off - kCBytes) / 128; its 16-byte
             // chunk holds panel rows 4 * ((chunk ^ j) & 7) .. + 3
             const int vo = off - kCBytes;
@@ -117,8 +145,7 @@ __device__ __forceinline__ void split_stage(unsigned char *raw, unsigned char *l
             v = make_float4(e[0], e[1], e[2], e[3]);
             *reinterpret_cast<float4 *>(raw + off) = v;
         }
-        unsigned char *dst = off < kCBytes ? lo + off : raw + kVBytes + off;
-        *reinterpret_cast<float4 *>(dst) =
+        *reinterpret_cast<float4 *>(raw + kVBytes + off) =
             make_float4(tc::tf32_lo(v.x), tc::tf32_lo(v.y), tc::tf32_lo(v.z), tc::tf32_lo(v.w));
     }
 }
@@ -234,28 +261,34 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
         const int sidx = i % kStages, b = i & 1;
         unsigned char *st = smem + sidx * kStageBytes;
         const bool landed = tc::mbar_wait(&full[sidx], (uint32_t)(i / kStages) & 1u, kWaitLimit);
-        if (landed && !bad) split_stage(st, smem + kOffLo + b * kCBytes, i == 0, tid);
+        // run by every thread (the TMEM stores are warp-collective); after a
+        // wait that gave up it moves garbage that no MMA reads: the loop
+        // ends at the barrier below
+        const uint32_t lane_q = tmem + ((uint32_t)(32 * warp) << 16);
+        tc::fence_after_sync();  // after the wait for chunk i-2's MMAs, which read this A buffer
+        split_stage(st, lane_q + kAHi + 64u * b, lane_q + kALo + 64u * b, i == 0, tid);
+        tc::tmem_st_wait();
         tc::fence_proxy_async_smem();
+        tc::fence_before_sync();
         ok = !__syncthreads_or(!landed || bad);
         if (!ok) break;
         if (tid == 0) {
             tc::fence_after_sync();
-            const uint32_t sC = sbase + sidx * kStageBytes, sV = sC + kCBytes;
-            const uint32_t lC = sbase + kOffLo + b * kCBytes;
+            const uint32_t sV = sbase + sidx * kStageBytes + kCBytes;
 #pragma unroll
             for (int s = 0; s < kRC / 8; ++s) {
                 const uint32_t ko = (uint32_t)s * 32;  // 8 K elements inside the swizzle atom
-                const uint64_t ah = tc::smem_desc_sw128(sC + ko), al = tc::smem_desc_sw128(lC + ko);
                 const uint64_t bv = tc::smem_desc_sw128(sV + ko);  // V rows, then V_lo rows
                 const uint32_t acc = (i > 0 || s > 0) ? 1u : 0u;
-                tc::mma_tf32(tmem + kDA, ah, bv, kIdescA, acc);
-                tc::mma_tf32(tmem + kDA2, al, bv, kIdescA2, acc);
+                // A from tensor memory: K elements 8s .. 8s+7 are columns 8s ..
+                tc::mma_tf32_ts(tmem + kDA, tmem + kAHi + 64u * b + 8u * s, bv, kIdescA, acc);
+                tc::mma_tf32_ts(tmem + kDA2, tmem + kALo + 64u * b + 8u * s, bv, kIdescA2, acc);
             }
             tc::mma_commit(&mmab[b]);
         }
         ++mma_issued[b];
         if (i >= 1) {
-            // chunk i-1's MMAs: afterwards its ring stage and lo buffer are free
+            // chunk i-1's MMAs: afterwards its ring stage and TMEM A buffer are free
             const int pb = b ^ 1;
             const bool done = tc::mbar_wait(&mmab[pb], mma_waited[pb] & 1u, kWaitLimit);
             if (done) ++mma_waited[pb];
