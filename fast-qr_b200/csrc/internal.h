@@ -17,9 +17,10 @@ cudaError_t launch_small(const float *A, int64_t batch, int n, int64_t bs, int64
 
 // Blocked path pieces (n > 64, or any m x n with m >= n).  H holds m x n
 // column-major per matrix (column length m), tau n values per matrix.
-// Also clears status[0 .. clear-1] (the bounded-wait status words).
+// Also clears status[i] for every bit i set in clear_mask (the bounded-wait
+// status words).
 cudaError_t launch_copy_in(const float *A, int64_t batch, int m, int n, int64_t bs, int64_t rs, int64_t cs,
-                           float *H, int *status, int clear, cudaStream_t st);
+                           float *H, int *status, unsigned clear_mask, cudaStream_t st);
 cudaError_t launch_panel(float *H, float *tau, float *Tws, int64_t batch, int m, int n, int k,
                          cudaStream_t st);
 cudaError_t launch_trailing(float *H, const float *Sws, const float *tau, int64_t batch, int m, int n, int k,

@@ -34,11 +34,12 @@ namespace fqr {
 // memory so both the reads (rows) and the writes (columns) are coalesced.
 __global__ void __launch_bounds__(256)
 copy_in_rowmajor_kernel(const float *__restrict__ A, int64_t batch, int m, int n, int64_t bs, int64_t rs,
-                        float *__restrict__ H, int *__restrict__ status, int clear)
+                        float *__restrict__ H, int *__restrict__ status, unsigned clear_mask)
 {
     __shared__ float tile[32][33];
     pdl_trigger();  // the first panel may be scheduled; it waits for this grid
-    if (status && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && threadIdx.x < clear)
+    if (status && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && threadIdx.x < 32 &&
+        ((clear_mask >> threadIdx.x) & 1u))
         status[threadIdx.x] = 0;
     const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
     const int j0 = blockIdx.x * 32, i0 = blockIdx.y * 32;
@@ -64,10 +65,11 @@ copy_in_rowmajor_kernel(const float *__restrict__ A, int64_t batch, int m, int n
 // writes coalesced along columns of H.
 __global__ void __launch_bounds__(256)
 copy_in_strided_kernel(const float *__restrict__ A, int64_t batch, int m, int n, int64_t bs, int64_t rs,
-                       int64_t cs, float *__restrict__ H, int *__restrict__ status, int clear)
+                       int64_t cs, float *__restrict__ H, int *__restrict__ status, unsigned clear_mask)
 {
     pdl_trigger();
-    if (status && blockIdx.x == 0 && threadIdx.x < clear) status[threadIdx.x] = 0;
+    if (status && blockIdx.x == 0 && threadIdx.x < 32 && ((clear_mask >> threadIdx.x) & 1u))
+        status[threadIdx.x] = 0;
     const int64_t mn = (int64_t)m * n;
     const int64_t total = batch * mn;
     for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
@@ -80,16 +82,16 @@ copy_in_strided_kernel(const float *__restrict__ A, int64_t batch, int m, int n,
 }
 
 cudaError_t launch_copy_in(const float *A, int64_t batch, int m, int n, int64_t bs, int64_t rs, int64_t cs,
-                           float *H, int *status, int clear, cudaStream_t st)
+                           float *H, int *status, unsigned clear_mask, cudaStream_t st)
 {
     if (cs == 1) {
         dim3 grid((unsigned)((n + 31) / 32), (unsigned)((m + 31) / 32), (unsigned)(batch < 65535 ? batch : 65535));
-        copy_in_rowmajor_kernel<<<grid, 256, 0, st>>>(A, batch, m, n, bs, rs, H, status, clear);
+        copy_in_rowmajor_kernel<<<grid, 256, 0, st>>>(A, batch, m, n, bs, rs, H, status, clear_mask);
     } else {
         const int64_t total = batch * (int64_t)m * n;
         int64_t blocks = (total + 255) / 256;
         if (blocks > 148 * 64) blocks = 148 * 64;
-        copy_in_strided_kernel<<<(unsigned)blocks, 256, 0, st>>>(A, batch, m, n, bs, rs, cs, H, status, clear);
+        copy_in_strided_kernel<<<(unsigned)blocks, 256, 0, st>>>(A, batch, m, n, bs, rs, cs, H, status, clear_mask);
     }
     return cudaGetLastError();
 }

@@ -7,10 +7,11 @@
  * validate arguments on the host, enqueue kernels and return.  The library
  * allocates no device memory on this path; scratch space is caller-owned
  * (see fqr_workspace_bytes).  Calls are reentrant: the only global state is
- * per device -- a second stream and two events, created on first use, on
- * which the blocked path runs half of a batch of two or more matrices (always
- * ordered with the caller's stream: it waits for the caller's prior work and
- * the caller's stream waits for it).
+ * per device -- up to three internal streams and their events, created on
+ * first use, on which the blocked path runs parts of a batch of two or more
+ * matrices (two parts, four for n >= 2048; always ordered with the caller's
+ * stream: they wait for the caller's prior work and the caller's stream waits
+ * for them).
  *
  * Output layout (the contract of torch.geqrf, and of the reference's
  * `custom_kernel(data) -> (H, tau)`):
@@ -89,7 +90,7 @@ const char *fqr_status_string(int status);
 int fqr_plan_describe(int64_t batch, int64_t n, char *buf, size_t len);
 
 /* Number of kernel launches fqr_geqrf_f32 enqueues for (batch, n), counting
- * both halves of a batch of two or more on the blocked path (n > 64). */
+ * every part of a batch of two or more on the blocked path (n > 64). */
 int fqr_launch_count(int64_t batch, int64_t n);
 
 /* Largest batch fqr_geqrf_f32_noalloc accepts when n > 64 (its static

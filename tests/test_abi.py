@@ -66,9 +66,12 @@ def test_workspace_and_plan_depend_on_shape_only():
     with pytest.raises(fastqr.FastQRError):
         fastqr.plan(1, 10000)
     assert fastqr.launch_count(1024, 32) == 1
-    # two halves of a batch on two streams, each copy-in + 8 panels + 7 trailing
+    # two parts of a batch on two streams, each copy-in + 8 panels + 7 trailing
     assert fastqr.launch_count(256, 256) == 2 * (1 + 8 + 7)
     assert fastqr.launch_count(1, 256) == 1 + 8 + 7
+    # four parts for n >= 2048 (64 panels: copy-in + 64 panels + 63 trailing each)
+    assert fastqr.launch_count(16, 2048) == 4 * (1 + 64 + 63)
+    assert fastqr.launch_count(3, 2048) == 3 * (1 + 64 + 63)
 
 
 def test_python_api_rejects_cpu_tensors():
