@@ -1,10 +1,10 @@
 // fqr_geqrf_f32_host: batched QR of matrices held in HOST memory.
 //
-// The batch is cut into chunks.  Each chunk is copied host->device, factored
-// and copied back device->host on one of up to kMaxSlots internal streams,
-// each stream with its own device staging slot, so that the upload of chunk
-// c+1, the factorisation of chunk c and the download of chunk c-1 run at the
-// same time (the two copy directions use separate copy engines).  A call made
+// The batch is cut into up to 16 chunks.  Each chunk is copied host->device,
+// factored and copied back device->host on its own internal stream with its
+// own device staging slot, so that the uploads run back to back while earlier
+// chunks are factored and downloaded (the two copy directions use separate
+// copy engines).  A call made
 // through the device-pointer entry point pays the two transfers one after the
 // other and after the kernels; here the whole call costs about one transfer
 // plus the factorisation and download of a single chunk.
@@ -16,6 +16,13 @@
 // unmodified until `stream` has passed the call.  Copies overlap only when the
 // host buffers are page-locked (cudaHostAlloc / cudaHostRegister); pageable
 // buffers still give correct results, with the copies staged by the driver.
+//
+// The work of a call (copies, kernels, events) is captured once into a CUDA
+// graph per distinct argument set and replayed by a single graph launch on
+// `stream` afterwards (up to eight graphs per device, least recently used
+// replaced); arguments that do not capture, such as pageable host buffers, are
+// enqueued directly every time.  A caller that is capturing `stream` itself
+// gets the work recorded into its own graph.
 //
 // The internal streams and events are created once per device, on the first
 // call made with that device current, and live until the process exits.
@@ -33,8 +40,12 @@ namespace {
 
 using fqr::kWsAlign;
 
-constexpr int kMaxSlots = 4;
-constexpr int kMaxChunks = 8;
+// Every chunk gets its own staging slot and stream: a slot reused by a later
+// chunk would hold that chunk's upload until the earlier chunk's
+// factorisation (a per-matrix latency chain of ~0.35 ms at n = 256, whatever
+// the chunk's size) and download are done.
+constexpr int kMaxSlots = 16;
+constexpr int kMaxChunks = 16;
 constexpr size_t kMinChunkBytes = size_t(1) << 20;  // 1 MiB of input per chunk at least
 constexpr int kMaxDevices = 64;
 
@@ -76,11 +87,42 @@ bool host_plan(int64_t batch, int64_t n, HostPlan *p)
     return true;
 }
 
+// One call's arguments: the key of its cached graph.
+struct HostCall {
+    const float *A;
+    int64_t batch, n, a_bstride, a_rstride, a_cstride;
+    float *H, *tau;
+    void *workspace;
+    size_t workspace_bytes;
+    bool operator==(const HostCall &o) const
+    {
+        return A == o.A && batch == o.batch && n == o.n && a_bstride == o.a_bstride &&
+               a_rstride == o.a_rstride && a_cstride == o.a_cstride && H == o.H && tau == o.tau &&
+               workspace == o.workspace && workspace_bytes == o.workspace_bytes;
+    }
+};
+
+// The work of a call is a fixed DAG of copies and kernels for fixed
+// arguments; enqueueing it costs ~4.5 us of host time per launch (about 1 ms
+// at C2, 4 ms at n = 1024), which the GPU would wait for.  So the DAG is
+// captured once into a CUDA graph, cached per device by the call's arguments,
+// and replayed with one launch.
+constexpr int kGraphCache = 8;
+struct CachedGraph {
+    bool used = false;
+    HostCall key{};
+    cudaGraphExec_t exec = nullptr;  // null: these arguments do not capture (enqueue directly)
+    uint64_t last = 0;
+};
+
 struct DeviceStreams {
     bool ready = false;
+    cudaStream_t origin = nullptr;  // root of a captured call
     cudaStream_t st[kMaxSlots] = {};
     cudaEvent_t fork = nullptr;
     cudaEvent_t done[kMaxSlots] = {};
+    CachedGraph graphs[kGraphCache];
+    uint64_t tick = 0;
     std::mutex mu;
 };
 DeviceStreams g_dev[kMaxDevices];
@@ -93,7 +135,9 @@ int device_streams(DeviceStreams **out)
     DeviceStreams &d = g_dev[dev];
     *out = &d;
     if (d.ready) return FQR_OK;
-    if (cudaEventCreateWithFlags(&d.fork, cudaEventDisableTiming) != cudaSuccess) return FQR_ECUDA;
+    if (cudaEventCreateWithFlags(&d.fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&d.origin, cudaStreamNonBlocking) != cudaSuccess)
+        return FQR_ECUDA;
     for (int s = 0; s < kMaxSlots; ++s) {
         if (cudaStreamCreateWithFlags(&d.st[s], cudaStreamNonBlocking) != cudaSuccess ||
             cudaEventCreateWithFlags(&d.done[s], cudaEventDisableTiming) != cudaSuccess)
@@ -103,43 +147,16 @@ int device_streams(DeviceStreams **out)
     return FQR_OK;
 }
 
-}  // namespace
-
-extern "C" {
-
-size_t fqr_host_workspace_bytes(int64_t batch, int64_t n)
+// Enqueue one host-buffer call on the internal streams, forked from and
+// joined back into `caller`.
+int enqueue_host(const HostCall &c, const HostPlan &p, DeviceStreams *d, cudaStream_t caller)
 {
-    HostPlan p;
-    return host_plan(batch, n, &p) ? p.total : 0;
-}
-
-int fqr_geqrf_f32_host(const float *A, int64_t batch, int64_t n, int64_t a_bstride,
-                       int64_t a_rstride, int64_t a_cstride, float *H, float *tau,
-                       void *workspace, size_t workspace_bytes, void *stream)
-{
-    if (batch < 0 || n < 0) return FQR_EINVAL;
-    if (batch == 0 || n == 0) return FQR_OK;
-    if (n > FQR_MAX_N) return FQR_EUNSUPPORTED;
-    if (!A || !H || !tau) return FQR_EINVAL;
-    // each host matrix must be one dense n x n block (row- or column-major)
-    const bool rowmajor = a_rstride == n && a_cstride == 1;
-    const bool colmajor = a_rstride == 1 && a_cstride == n;
-    if (n > 1 && !rowmajor && !colmajor) return FQR_EINVAL;
-    if (batch > 1 && a_bstride < n * n) return FQR_EINVAL;
-    HostPlan p;
-    if (!host_plan(batch, n, &p)) return FQR_EUNSUPPORTED;
-    if (!workspace || workspace_bytes < p.total) return FQR_EWORKSPACE;
-    if (((uintptr_t)workspace) % kWsAlign) return FQR_EINVAL;
-
-    DeviceStreams *d = nullptr;
-    int dev = -1;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return FQR_ECUDA;
-    std::lock_guard<std::mutex> lock(g_dev[dev].mu);
-    int rc = device_streams(&d);
-    if (rc != FQR_OK) return rc;
-
-    cudaStream_t caller = (cudaStream_t)stream;
-    unsigned char *ws = (unsigned char *)workspace;
+    const float *A = c.A;
+    const int64_t batch = c.batch, n = c.n, a_bstride = c.a_bstride;
+    float *H = c.H, *tau = c.tau;
+    const bool colmajor = c.a_rstride == 1 && c.a_cstride == n && n > 1;
+    int rc = FQR_OK;
+    unsigned char *ws = (unsigned char *)c.workspace;
     int *status = (int *)ws;
     const size_t mat_elems = (size_t)n * (size_t)n;
     const size_t mat_bytes = mat_elems * sizeof(float);
@@ -194,6 +211,83 @@ int fqr_geqrf_f32_host(const float *A, int64_t batch, int64_t n, int64_t a_bstri
             return FQR_ECUDA;
     }
     return FQR_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t fqr_host_workspace_bytes(int64_t batch, int64_t n)
+{
+    HostPlan p;
+    return host_plan(batch, n, &p) ? p.total : 0;
+}
+
+int fqr_geqrf_f32_host(const float *A, int64_t batch, int64_t n, int64_t a_bstride,
+                       int64_t a_rstride, int64_t a_cstride, float *H, float *tau,
+                       void *workspace, size_t workspace_bytes, void *stream)
+{
+    if (batch < 0 || n < 0) return FQR_EINVAL;
+    if (batch == 0 || n == 0) return FQR_OK;
+    if (n > FQR_MAX_N) return FQR_EUNSUPPORTED;
+    if (!A || !H || !tau) return FQR_EINVAL;
+    // each host matrix must be one dense n x n block (row- or column-major)
+    const bool rowmajor = a_rstride == n && a_cstride == 1;
+    const bool colmajor = a_rstride == 1 && a_cstride == n;
+    if (n > 1 && !rowmajor && !colmajor) return FQR_EINVAL;
+    if (batch > 1 && a_bstride < n * n) return FQR_EINVAL;
+    HostPlan p;
+    if (!host_plan(batch, n, &p)) return FQR_EUNSUPPORTED;
+    if (!workspace || workspace_bytes < p.total) return FQR_EWORKSPACE;
+    if (((uintptr_t)workspace) % kWsAlign) return FQR_EINVAL;
+
+    DeviceStreams *d = nullptr;
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return FQR_ECUDA;
+    std::lock_guard<std::mutex> lock(g_dev[dev].mu);
+    int rc = device_streams(&d);
+    if (rc != FQR_OK) return rc;
+
+    const HostCall call{A, batch, n, a_bstride, a_rstride, a_cstride, H, tau, workspace, workspace_bytes};
+    cudaStream_t caller = (cudaStream_t)stream;
+    // the caller is capturing a graph itself: record the work into it directly
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(caller, &cs) != cudaSuccess) return FQR_ECUDA;
+    if (cs != cudaStreamCaptureStatusNone) return enqueue_host(call, p, d, caller);
+
+    const uint64_t now = ++d->tick;
+    for (CachedGraph &g : d->graphs)
+        if (g.used && g.key == call) {
+            g.last = now;
+            if (!g.exec) return enqueue_host(call, p, d, caller);
+            return cudaGraphLaunch(g.exec, caller) == cudaSuccess ? FQR_OK : FQR_ECUDA;
+        }
+    // capture on the internal origin stream (the caller's may be the legacy
+    // default stream, which cannot capture); the graph launch then orders the
+    // whole DAG after the caller's prior work and before its later work
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    if (cudaStreamBeginCapture(d->origin, cudaStreamCaptureModeRelaxed) == cudaSuccess) {
+        const int crc = enqueue_host(call, p, d, d->origin);
+        const cudaError_t ec = cudaStreamEndCapture(d->origin, &graph);
+        if (crc == FQR_OK && ec == cudaSuccess && graph &&
+            cudaGraphInstantiate(&exec, graph, 0) != cudaSuccess)
+            exec = nullptr;
+        if (graph) cudaGraphDestroy(graph);
+    }
+    if (!exec) cudaGetLastError();  // not capturable (pageable host memory, say)
+    CachedGraph *slot = &d->graphs[0];
+    for (CachedGraph &g : d->graphs) {
+        if (!g.used) { slot = &g; break; }
+        if (g.last < slot->last) slot = &g;
+    }
+    if (slot->used && slot->exec) cudaGraphExecDestroy(slot->exec);
+    slot->used = true;
+    slot->key = call;
+    slot->exec = exec;
+    slot->last = now;
+    if (!exec) return enqueue_host(call, p, d, caller);
+    return cudaGraphLaunch(exec, caller) == cudaSuccess ? FQR_OK : FQR_ECUDA;
 }
 
 int fqr_host_check_status(const void *workspace, size_t workspace_bytes, int64_t batch, int64_t n,

@@ -94,3 +94,24 @@ def test_host_matches_oracle_small(dev):
     h64, t64 = oracle.geqrf_f64(a.numpy())
     ok, msg = checker.check_columns(h.numpy(), t.numpy(), h64, t64, 1e-3)
     assert ok, msg
+
+
+def test_host_replayed_call_sees_new_data(dev):
+    """Repeated calls with the same buffers replay one captured graph: each
+    call must read the host input as it is at that call (bitwise equal to the
+    device entry on that data), with page-locked and with pageable buffers
+    (which do not capture and are enqueued directly)."""
+    batch, n = 24, 256
+    for pinned in (True, False):
+        a = torch.empty(batch, n, n)
+        h = torch.empty_strided((batch, n, n), (n * n, 1, n))
+        t = torch.empty(batch, n)
+        if pinned:
+            a, h, t = a.pin_memory(), h.pin_memory(), t.pin_memory()
+        ws = torch.empty(fastqr.host_workspace_bytes(batch, n), dtype=torch.uint8, device=dev)
+        for seed in (1, 2, 3):
+            a.copy_(inputs.generate_input(batch, n, 1, seed, device="cpu"))
+            fastqr.geqrf_host(a, out=(h, t), workspace=ws, device=dev)
+            hd, td = device_result(a, dev)
+            assert torch.equal(h, hd) and torch.equal(t, td), (pinned, seed)
+            fastqr.host_check_status(ws, batch, n)  # raises if a bounded wait gave up
