@@ -39,7 +39,9 @@ constexpr int kStagePitch = 36;  // floats per row of a warp's 32 x 32 staging b
 //     memory and one cluster barrier replaces the CTA barrier's role;
 //   * every thread applies the rank-1 update to its tile.
 // Only the warp holding panel rows 0..31 needs row masks (rows <= c are R
-// rows); it runs a masked copy of the per-column code, all others do not.
+// rows), but every warp runs the same masked code (the masks are all-true
+// elsewhere): one copy of the unrolled column body instead of two keeps it in
+// the instruction cache (measured: panel time -14% at m = 256).
 // The compact-WY factor is stored as S(l, c) = v_l^T v_c (= w_l for l < c,
 // a by-product of column c's reduction) plus tau; the trailing update uses
 // them through Y = T^T W = (I + D S^T)^-1 D W, D = diag(tau).
@@ -146,13 +148,8 @@ panel_kernel(float *__restrict__ H, float *__restrict__ tau, float *__restrict__
             float x[NR], xm[NR];
 #pragma unroll
             for (int q = 0; q < NR; ++q) x[q] = __shfl_sync(kFull, p[q][cc], cb + 8 * rg);
-            if (top) {
 #pragma unroll
-                for (int q = 0; q < NR; ++q) xm[q] = (q < 8 && row[q] <= c) ? 0.0f : x[q];
-            } else {
-#pragma unroll
-                for (int q = 0; q < NR; ++q) xm[q] = x[q];
-            }
+            for (int q = 0; q < NR; ++q) xm[q] = (q < 8 && row[q] <= c) ? 0.0f : x[q];
             // (column c's own slot gives sum xm * x = sigma for free)
             float d[4];
 #pragma unroll
@@ -163,14 +160,12 @@ panel_kernel(float *__restrict__ H, float *__restrict__ tau, float *__restrict__
                 d[jj] = a2[0] + a2[1];
             }
             part[par][wid][4 * cgp + rg] = reduce_scatter4(d);
-            if (top) {
 #pragma unroll
-                for (int q = 0; q < 8; ++q)
-                    if (row[q] == c) {
+            for (int q = 0; q < 8; ++q)
+                if (row[q] == c) {
 #pragma unroll
-                        for (int jj = 0; jj < 4; ++jj) rowc_s[par][4 * cgp + jj] = p[q][jj];
-                    }
-            }
+                    for (int jj = 0; jj < 4; ++jj) rowc_s[par][4 * cgp + jj] = p[q][jj];
+                }
             __syncthreads();
 
             // (2) every warp: CTA (and cluster) totals, reflector, tau * w_j
@@ -234,8 +229,8 @@ panel_kernel(float *__restrict__ H, float *__restrict__ tau, float *__restrict__
                     float acc = 0.0f;
 #pragma unroll
                     for (int q = 0; q < NR; ++q) {
-                        const bool below = !top || q >= 8 || row[q] > c;
-                        const bool diag = top && q < 8 && row[q] == c;
+                        const bool below = q >= 8 || row[q] > c;
+                        const bool diag = q < 8 && row[q] == c;
                         const float v = below ? reflector_apply(r, x[q]) : (diag ? 1.0f : 0.0f);
                         acc = fmaf(v, p[q][jj], acc);
                     }
@@ -279,12 +274,12 @@ panel_kernel(float *__restrict__ H, float *__restrict__ tau, float *__restrict__
 #pragma unroll
             for (int q = 0; q < NR; ++q) {
                 float v;
-                if (top && q < 8) v = row[q] > c ? vv[q] : (row[q] == c ? 1.0f : 0.0f);
+                if (q < 8) v = row[q] > c ? vv[q] : (row[q] == c ? 1.0f : 0.0f);
                 else v = vv[q];
 #pragma unroll
                 for (int jj = 0; jj < 4; ++jj) p[q][jj] = fmaf(-twv[jj], v, p[q][jj]);
                 if (owner) {
-                    if (top && q < 8) {
+                    if (q < 8) {
                         if (row[q] > c) p[q][cc] = v;
                         else if (row[q] == c) p[q][cc] = r.beta;
                     } else {
