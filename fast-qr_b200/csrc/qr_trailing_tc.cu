@@ -82,8 +82,8 @@ constexpr int kSmem = kSmemUsed + 1024;                  // + alignment slack: ~
 static_assert(2 * (kSmem + 1024) <= 228 * 1024, "two CTAs per SM");
 // Phase C (reuses the phase-A area): V chunk as the K-major A operand
 // (128 r x 32 j) and Y as the K-major B operand (128 c x 32 j), raw + lo, and
-// two -P quarters (128 rows x 32 columns as they sit in H, [c][r]) that TMA
-// reduce-adds into C.
+// two -P quarters (128 rows x 32 columns; each warp's 32 rows a 4 KB slice,
+// [c][r] as they sit in H) that TMA reduce-adds into C, warp by warp.
 constexpr int kOffVCraw = 0;
 constexpr int kOffVClo = 16384;
 constexpr int kOffYraw = 32768;
@@ -434,30 +434,33 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
         // shared quarter (32 columns) that TMA adds into C at the L2: no load
         // of C, half the shared-memory traffic of load/subtract/store, and
         // C - P and C + (-P) round identically.  Rows and columns past the
-        // end of C are outside the tensor map and are not written.
+        // end of C are outside the tensor map and are not written.  Each
+        // warp stages and reduce-adds its own 32 rows (a 4 KB slice of the
+        // two quarter buffers), so the epilogue needs no CTA barrier: lane 0
+        // of the warp owns the warp's bulk groups.
         for (int q = 0; q < nqc; ++q) {
             const int u = j * nqc + q;
             float pv[32];
             tc::tmem_ld_32x32(pc + kCQCols * q, pv);
             tc::tmem_ld_wait();
-            float *cs = reinterpret_cast<float *>(smem + kOffCQ + (u & 1) * kCQBytes);
+            float *cs = reinterpret_cast<float *>(smem + kOffCQ + (u & 1) * kCQBytes) + warp * (32 * kCQCols);
+            // the warp's reduce of quarter u-2 (same slice) has read it; the
+            // one of quarter u-1 may still be in flight
+            if (lane == 0) tc::bulk_wait_group_read<1>();
+            __syncwarp();
 #pragma unroll
-            for (int c = 0; c < kCQCols; ++c) cs[c * kRCC + tid] = -pv[c];
+            for (int c = 0; c < kCQCols; ++c) cs[c * 32 + lane] = -pv[c];
             tc::fence_proxy_async_smem();
-            // the reduce of quarter u-1 (the only one outstanding) has read
-            // its buffer before anyone passes this barrier: quarter u+1
-            // writes that buffer
-            if (tid == 0) tc::bulk_wait_group_read<0>();
-            __syncthreads();
-            if (tid == 0) {
-                tc::tma_reduce_add_3d(&tmCQ, k + kRCC * j, c0 + kCQCols * q, (int)mat, cs);
+            __syncwarp();
+            if (lane == 0) {
+                tc::tma_reduce_add_3d(&tmCQ, k + kRCC * j + 32 * warp, c0 + kCQCols * q, (int)mat, cs);
                 tc::bulk_commit_group();
             }
         }
         tc::fence_before_sync();
     }
     if (!early_trigger) pdl_trigger();
-    if (tid == 0) tc::bulk_wait_group<0>();  // reduces complete before shared memory goes away
+    if (lane == 0) tc::bulk_wait_group<0>();  // each warp's reduces complete before shared memory goes away
 
     if (!ok && tid == 0) {
         atomicOr(status, 1);
@@ -518,7 +521,7 @@ cudaError_t prepare_apply_maps(const float *H, int ld, int hcols, float *C, int6
     const cuuint64_t cdims[3] = {(cuuint64_t)ld, (cuuint64_t)c_cols, (cuuint64_t)batch};
     const cuuint64_t cstrides[2] = {(cuuint64_t)ld * 4, (cuuint64_t)ld * (cuuint64_t)c_cols * 4};
     const cuuint32_t box_c[3] = {kRC, kTN, 1}, box_v[3] = {kRC, kPanel, 1}, unit[3] = {1, 1, 1};
-    const cuuint32_t box_cq[3] = {kRCC, kCQCols, 1};
+    const cuuint32_t box_cq[3] = {32, kCQCols, 1};  // one warp's 32 rows of a quarter
     if (enc(&maps->c, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, C, cdims, cstrides, box_c, unit,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS ||
