@@ -232,6 +232,17 @@ def test_large_n_properties(n, batch, dev):
     assert g["ok"], g
 
 
+def test_largest_n(dev):
+    """n = FQR_MAX_N: panels taller than 4096 rows run as clusters of 16-warp
+    CTAs (8 at the first panel); the QR gates on one matrix."""
+    n = 8192
+    assert "cluster 8" in fastqr.plan(1, n)
+    a = inputs.generate_input(1, n, 0, 8192, device=dev)
+    h, t = fastqr.geqrf(a)
+    g = gates(a, h, t, chunk=1)
+    assert g["ok"], g
+
+
 @pytest.mark.parametrize("n", [1100, 2100])
 def test_cluster_panel_columns(n, dev):
     """Panels taller than 1024 rows run as thread-block clusters of 512-row
