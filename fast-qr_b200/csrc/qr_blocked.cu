@@ -61,6 +61,48 @@ copy_in_rowmajor_kernel(const float *__restrict__ A, int64_t batch, int m, int n
     }
 }
 
+// Row-major rows with 16-byte alignment (a_cstride == 1; m, n, the row and
+// batch strides multiples of 4; A and H 16-byte aligned): 64 x 64 tiles,
+// every global access 16 bytes wide -- rows of A read as float4, columns of H
+// written as float4 by 16 consecutive threads (256 contiguous bytes).
+__global__ void __launch_bounds__(256)
+copy_in_rowmajor_v4_kernel(const float *__restrict__ A, int64_t batch, int m, int n, int64_t bs, int64_t rs,
+                           float *__restrict__ H, int *__restrict__ status, unsigned clear_mask)
+{
+    __shared__ float tile[64][65];
+    pdl_trigger();  // the first panel may be scheduled; it waits for this grid
+    if (status && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && threadIdx.x < 32 &&
+        ((clear_mask >> threadIdx.x) & 1u))
+        status[threadIdx.x] = 0;
+    const int t = threadIdx.x;
+    const int j0 = blockIdx.x * 64, i0 = blockIdx.y * 64;
+    for (int64_t b = blockIdx.z; b < batch; b += gridDim.z) {
+        const float *Am = A + b * bs;
+        float *Hm = H + b * (int64_t)m * n;
+#pragma unroll
+        for (int s4 = 0; s4 < 4; ++s4) {
+            const int f = t + 256 * s4, r = f >> 4, c4 = (f & 15) * 4;  // row, first column
+            const int i = i0 + r, j = j0 + c4;
+            float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (i < m && j < n) v = __ldg(reinterpret_cast<const float4 *>(Am + (int64_t)i * rs + j));
+            tile[r][c4] = v.x;
+            tile[r][c4 + 1] = v.y;
+            tile[r][c4 + 2] = v.z;
+            tile[r][c4 + 3] = v.w;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int s4 = 0; s4 < 4; ++s4) {
+            const int f = t + 256 * s4, c = f >> 4, r4 = (f & 15) * 4;  // column, first row
+            const int j = j0 + c, i = i0 + r4;
+            if (i < m && j < n)
+                *reinterpret_cast<float4 *>(Hm + (int64_t)j * m + i) =
+                    make_float4(tile[r4][c], tile[r4 + 1][c], tile[r4 + 2][c], tile[r4 + 3][c]);
+        }
+        __syncthreads();
+    }
+}
+
 // Any other strides (column-major input included): one thread per element,
 // writes coalesced along columns of H.
 __global__ void __launch_bounds__(256)
@@ -84,7 +126,12 @@ copy_in_strided_kernel(const float *__restrict__ A, int64_t batch, int m, int n,
 cudaError_t launch_copy_in(const float *A, int64_t batch, int m, int n, int64_t bs, int64_t rs, int64_t cs,
                            float *H, int *status, unsigned clear_mask, cudaStream_t st)
 {
-    if (cs == 1) {
+    const bool v4 = cs == 1 && m % 4 == 0 && n % 4 == 0 && rs % 4 == 0 && (batch == 1 || bs % 4 == 0) &&
+                    ((uintptr_t)A % 16) == 0 && ((uintptr_t)H % 16) == 0;
+    if (v4) {
+        dim3 grid((unsigned)((n + 63) / 64), (unsigned)((m + 63) / 64), (unsigned)(batch < 65535 ? batch : 65535));
+        copy_in_rowmajor_v4_kernel<<<grid, 256, 0, st>>>(A, batch, m, n, bs, rs, H, status, clear_mask);
+    } else if (cs == 1) {
         dim3 grid((unsigned)((n + 31) / 32), (unsigned)((m + 31) / 32), (unsigned)(batch < 65535 ? batch : 65535));
         copy_in_rowmajor_kernel<<<grid, 256, 0, st>>>(A, batch, m, n, bs, rs, H, status, clear_mask);
     } else {
