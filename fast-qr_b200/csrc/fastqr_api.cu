@@ -4,7 +4,10 @@
 //   m == n <= 64 : one warp per matrix, registers (qr_small.cu)
 //   otherwise    : blocked compact-WY: copy-in, then per 32-column panel a
 //                  panel kernel and a trailing-update kernel (qr_blocked.cu);
-//                  rectangular m x n (m > n) always takes this path
+//                  for n >= 2048 (and m <= 4096) per 64 columns two panels,
+//                  the in-block update between them, the cross Gram block
+//                  and one rank-64 trailing update; rectangular m x n (m > n)
+//                  always takes this path
 // No path inspects matrix values and there is no CPU fallback: a failed
 // launch is reported as a status code.
 #include <cuda_runtime.h>
@@ -68,8 +71,9 @@ const char *fqr_status_string(int status)
 size_t fqr_workspace_bytes(int64_t batch, int64_t n)
 {
     if (batch <= 0 || n <= 0 || n > FQR_MAX_N || small_path(n)) return 0;
-    // one 32 x 32 T factor per matrix, then a status word
-    return fqr::ws_total_bytes(batch);
+    // a status block, then one S block per matrix (32 x 32, or 64 x 64 for
+    // the rank-64 plan)
+    return fqr::ws_total_bytes(batch, n, n);
 }
 
 int fqr_launch_count(int64_t batch, int64_t n)
@@ -77,11 +81,22 @@ int fqr_launch_count(int64_t batch, int64_t n)
     if (batch <= 0 || n <= 0) return 0;
     if (n > FQR_MAX_N) return -1;
     if (small_path(n)) return 1;
-    const int64_t panels = (n + fqr::kPanel - 1) / fqr::kPanel;
-    // copy-in + per panel (panel + trailing), the last panel has no trailing
-    auto range = [panels](int64_t b) {
+    const bool outer = use_tc(n) && fqr::use_outer64(n, n);
+    // copy-in + per panel (panel + trailing), the last panel has no trailing;
+    // the rank-64 plan has per 64-column block two panels, the in-block
+    // update and (all but the last block) the Gram block and one trailing
+    // update, then rank-32 steps for the columns left
+    const int64_t blocks = outer ? n / fqr::kOuter : 0;
+    const int64_t rest = n - blocks * fqr::kOuter;
+    const int64_t panels = (rest + fqr::kPanel - 1) / fqr::kPanel;
+    auto range = [blocks, rest, panels](int64_t b) {
         const int64_t chunks = (b + 65534) / 65535;
-        return 1 + panels + (panels - 1) * chunks;
+        int64_t t = 1 + panels + (panels > 0 ? panels - 1 : 0) * chunks;
+        if (blocks > 0) {
+            const int64_t full = rest > 0 ? blocks : blocks - 1;  // blocks with a trailing update
+            t += blocks * 3 + full * (1 + chunks);
+        }
+        return t;
     };
     // a batch of two or more runs as split_parts(batch, n) parts on as many
     // streams
@@ -103,11 +118,13 @@ int fqr_plan_describe(int64_t batch, int64_t n, char *buf, size_t len)
                  n <= 32 ? 32 : 64, (long long)batch);
     } else {
         const fqr::PanelShape s = fqr::panel_shape((int)n);
+        const bool outer = use_tc(n) && fqr::use_outer64(n, n);
         snprintf(buf, len,
                  "blocked: panel %d cols (first panel %d warps x %d row blocks, cluster %d), "
-                 "trailing %s, %d launches",
+                 "trailing %s rank %d, %d launches",
                  fqr::kPanel, s.warps, s.rows_per_thread_blocks, s.cluster,
-                 use_tc(n) ? "tcgen05 3xTF32" : "simt fp32", fqr_launch_count(batch, n));
+                 use_tc(n) ? "tcgen05 3xTF32" : "simt fp32", outer ? fqr::kOuter : fqr::kPanel,
+                 fqr_launch_count(batch, n));
     }
     return FQR_OK;
 }
@@ -155,9 +172,12 @@ struct StageTimer {
 };
 
 // The blocked path for one batch range of m x n matrices (m >= n): copy-in,
-// then per 32-column panel a panel kernel and a trailing update, all on `st`.
+// then per 32-column panel a panel kernel and a trailing update, all on `st`;
+// with the rank-64 plan, per 64 columns: panel(k), the update of columns
+// k+32 .. k+63 by panel k's reflectors, panel(k+32), the Gram block
+// V1^T V2 and one trailing update with all 64 reflectors.
 int enqueue_blocked(const float *A, int64_t batch, int m, int n, int64_t a_bstride, int64_t a_rstride,
-                    int64_t a_cstride, float *H, float *tau, float *Tws, int *status_base, int part,
+                    int64_t a_cstride, float *H, float *tau, float *Sws, int *status_base, int part,
                     unsigned clear_mask, bool tc, cudaStream_t st, StageTimer *tm)
 {
     // status_base[part] records a bounded wait that gave up; the copy-in
@@ -165,23 +185,51 @@ int enqueue_blocked(const float *A, int64_t batch, int m, int n, int64_t a_bstri
     int *status = status_base + part;
     fqr::TrailingMaps maps;
     if (tc && fqr::prepare_trailing_tc(H, batch, m, n, &maps) != cudaSuccess) return FQR_ECUDA;
+    const int64_t s_stride = fqr::s_block_floats(m, n);
     cudaError_t e;
-    if (tm) tm->begin(FQR_STAGE_COPY_IN);
-    e = fqr::launch_copy_in(A, batch, m, n, a_bstride, a_rstride, a_cstride, H, status_base, clear_mask, st);
-    if (tm) tm->end();
-    if (e != cudaSuccess) return status_from(e);
-    for (int k = 0; k < n; k += fqr::kPanel) {
-        if (tm) tm->begin(FQR_STAGE_PANEL);
-        e = fqr::launch_panel(H, tau, Tws, batch, m, n, k, st);
+    auto step = [&](int stage, auto &&launch) -> bool {
+        if (tm) tm->begin(stage);
+        e = launch();
         if (tm) tm->end();
-        if (e != cudaSuccess) return status_from(e);
-        if (k + fqr::kPanel < n) {
-            if (tm) tm->begin(FQR_STAGE_TRAILING);
-            e = tc ? fqr::launch_trailing_tc(maps, H, Tws, tau, status, batch, m, n, k, st)
-                   : fqr::launch_trailing(H, Tws, tau, batch, m, n, k, st);
-            if (tm) tm->end();
-            if (e != cudaSuccess) return status_from(e);
+        return e == cudaSuccess;
+    };
+    if (!step(FQR_STAGE_COPY_IN, [&] {
+            return fqr::launch_copy_in(A, batch, m, n, a_bstride, a_rstride, a_cstride, H, status_base, clear_mask,
+                                       st);
+        }))
+        return status_from(e);
+    int k = 0;
+    if (tc && fqr::use_outer64(m, n)) {
+        // S of both panels on the diagonal of one 64 x 64 row-major block per
+        // matrix; the Gram step adds the off-diagonal block
+        const fqr::SBlock s11{Sws, s_stride, fqr::kOuter, 1};
+        const fqr::SBlock s22{Sws + fqr::kPanel * fqr::kOuter + fqr::kPanel, s_stride, fqr::kOuter, 1};
+        for (; n - k >= fqr::kOuter; k += fqr::kOuter) {
+            if (!step(FQR_STAGE_PANEL, [&] { return fqr::launch_panel(H, tau, s11, batch, m, n, k, st); }) ||
+                !step(FQR_STAGE_INBLOCK,
+                      [&] { return fqr::launch_inblock(H, tau, Sws, s_stride, batch, m, n, k, false, st); }) ||
+                !step(FQR_STAGE_PANEL,
+                      [&] { return fqr::launch_panel(H, tau, s22, batch, m, n, k + fqr::kPanel, st); }))
+                return status_from(e);
+            if (n - k > fqr::kOuter &&
+                (!step(FQR_STAGE_INBLOCK,
+                       [&] { return fqr::launch_inblock(H, tau, Sws, s_stride, batch, m, n, k, true, st); }) ||
+                 !step(FQR_STAGE_TRAILING, [&] {
+                     return fqr::launch_trailing64_tc(maps, H, Sws, s_stride, tau, status, batch, m, n, k, st);
+                 })))
+                return status_from(e);
         }
+    }
+    // rank-32 steps (the whole matrix, or the columns the rank-64 blocks left)
+    const fqr::SBlock s32{Sws, s_stride, 1, fqr::kPanel};
+    for (; k < n; k += fqr::kPanel) {
+        if (!step(FQR_STAGE_PANEL, [&] { return fqr::launch_panel(H, tau, s32, batch, m, n, k, st); }))
+            return status_from(e);
+        if (k + fqr::kPanel < n && !step(FQR_STAGE_TRAILING, [&] {
+                return tc ? fqr::launch_trailing_tc(maps, H, Sws, s_stride, tau, status, batch, m, n, k, st)
+                          : fqr::launch_trailing(H, Sws, s_stride, tau, batch, m, n, k, st);
+            }))
+            return status_from(e);
     }
     return FQR_OK;
 }
@@ -204,7 +252,7 @@ constexpr int kMaxDevices = 64;
 SplitStreams g_split[kMaxDevices];
 
 int enqueue_blocked_split(const float *A, int64_t batch, int m, int n, int64_t a_bstride, int64_t a_rstride,
-                          int64_t a_cstride, float *H, float *tau, float *Tws, int *status, bool tc,
+                          int64_t a_cstride, float *H, float *tau, float *Sws, int *status, bool tc,
                           cudaStream_t st)
 {
     int dev = -1;
@@ -232,7 +280,7 @@ int enqueue_blocked_split(const float *A, int64_t batch, int m, int n, int64_t a
     for (int p = 0; p < parts; ++p) {
         const int64_t lo = batch * p / parts, hi = batch * (p + 1) / parts;
         const int r = enqueue_blocked(A + lo * a_bstride, hi - lo, m, n, a_bstride, a_rstride, a_cstride,
-                                      H + lo * mn, tau + lo * n, Tws + lo * (fqr::kPanel * fqr::kPanel),
+                                      H + lo * mn, tau + lo * n, Sws + lo * fqr::s_block_floats(m, n),
                                       status, p, (1u << p) | (p == 0 ? unused : 0u), tc,
                                       p == 0 ? st : sp.side[p - 1], nullptr);
         if (rc == FQR_OK) rc = r;
@@ -271,19 +319,19 @@ int run_geqrf(const float *A, int64_t batch, int64_t m, int64_t n, int64_t a_bst
         return status_from(e);
     }
 
-    const size_t need = fqr::ws_total_bytes(batch);
+    const size_t need = fqr::ws_total_bytes(batch, m, n);
     if (!workspace || workspace_bytes < need) return FQR_EWORKSPACE;
     if (((uintptr_t)workspace) % kWsAlign) return FQR_EINVAL;
-    float *Tws = (float *)workspace;
-    int *status = status_word ? status_word
-                              : (int *)((unsigned char *)workspace + fqr::ws_t_bytes(batch));
+    // the status block first, then the S blocks
+    float *Sws = (float *)((unsigned char *)workspace + kWsAlign);
+    int *status = status_word ? status_word : (int *)workspace;
     const bool tc = use_tc(m) && ((uintptr_t)H % 16) == 0;
     if (split && !tm && batch >= 2)
-        return enqueue_blocked_split(A, batch, mi, ni, a_bstride, a_rstride, a_cstride, H, tau, Tws, status,
+        return enqueue_blocked_split(A, batch, mi, ni, a_bstride, a_rstride, a_cstride, H, tau, Sws, status,
                                      tc, st);
     // an own status word (host entry, one per chunk) or both words of the
     // workspace's status block
-    return enqueue_blocked(A, batch, mi, ni, a_bstride, a_rstride, a_cstride, H, tau, Tws, status, 0,
+    return enqueue_blocked(A, batch, mi, ni, a_bstride, a_rstride, a_cstride, H, tau, Sws, status, 0,
                            status_word ? 1u : (1u << kSplitParts) - 1u, tc, st, tm);
 }
 
@@ -320,7 +368,7 @@ size_t fqr_geqrf_rect_workspace_bytes(int64_t batch, int64_t m, int64_t n)
 {
     if (batch <= 0 || n <= 0 || m < n || m > FQR_MAX_N) return 0;
     if (m == n) return fqr_workspace_bytes(batch, n);
-    return fqr::ws_total_bytes(batch);
+    return fqr::ws_total_bytes(batch, m, n);
 }
 
 int fqr_geqrf_rect_f32(const float *A, int64_t batch, int64_t m, int64_t n, int64_t a_bstride,
@@ -334,14 +382,13 @@ int fqr_geqrf_rect_f32(const float *A, int64_t batch, int64_t m, int64_t n, int6
 int fqr_check_status(const void *workspace, size_t workspace_bytes, int64_t batch, void *stream)
 {
     if (batch <= 0) return FQR_OK;
-    const size_t t = fqr::ws_t_bytes(batch);
-    if (!workspace || workspace_bytes < t + kSplitParts * sizeof(int)) return FQR_EINVAL;
+    // the status block is the workspace's first 256 bytes
+    if (!workspace || workspace_bytes < kSplitParts * sizeof(int)) return FQR_EINVAL;
     // one word per part of a batch split over streams; every call clears all
     // of them (each part its own, part 0 the unused ones)
     int v[kSplitParts] = {};
     cudaStream_t st = (cudaStream_t)stream;
-    if (cudaMemcpyAsync(v, (const unsigned char *)workspace + t, sizeof(v), cudaMemcpyDeviceToHost,
-                        st) != cudaSuccess)
+    if (cudaMemcpyAsync(v, workspace, sizeof(v), cudaMemcpyDeviceToHost, st) != cudaSuccess)
         return FQR_ECUDA;
     if (cudaStreamSynchronize(st) != cudaSuccess) return FQR_ECUDA;
     int any = 0;

@@ -9,14 +9,15 @@
 // latency-critical loops that cannot afford cudaMalloc/cudaFree, which may
 // synchronize the whole device.
 //
-// How: the only scratch the QR needs (one 32 x 32 T factor per matrix on the
-// blocked path, n > 64, plus a status word) lives in a file-scope __device__
-// array of fixed size, kNoAllocScratchBytes (4 MiB + 256 bytes).  Every GPU
+// How: the only scratch the QR needs (one 32 x 32 S block per matrix on the
+// blocked path, n > 64, 64 x 64 for n >= 2048, plus a status block) lives in
+// a file-scope __device__ array of fixed size, kNoAllocScratchBytes (16 MiB +
+// 256 bytes).  Every GPU
 // that loads this library keeps that array until the process exits.  Its
 // device address is looked up once per device with cudaGetSymbolAddress, with
 // that device current, on the first call made while it is current; make that
 // first call before any stream capture begins.  Nothing in the array needs to
-// start at zero: every T factor is written completely before it is read, and
+// start at zero: every S block is written completely before it is read, and
 // the status word is cleared by the first kernel of every call.
 //
 // Limits: on the blocked path (n > 64) at most FQR_NOALLOC_MAX_BATCH matrices
@@ -34,7 +35,9 @@
 
 namespace {
 
-constexpr size_t kNoAllocScratchBytes = fqr::ws_total_bytes(FQR_NOALLOC_MAX_BATCH);
+// the largest workspace of a call with up to FQR_NOALLOC_MAX_BATCH matrices
+// (64 x 64 S blocks: the rank-64 plan)
+constexpr size_t kNoAllocScratchBytes = fqr::ws_total_bytes(FQR_NOALLOC_MAX_BATCH, 4096, 4096);
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 

@@ -21,10 +21,19 @@ cudaError_t launch_small(const float *A, int64_t batch, int n, int64_t bs, int64
 // status words).
 cudaError_t launch_copy_in(const float *A, int64_t batch, int m, int n, int64_t bs, int64_t rs, int64_t cs,
                            float *H, int *status, unsigned clear_mask, cudaStream_t st);
-cudaError_t launch_panel(float *H, float *tau, float *Tws, int64_t batch, int m, int n, int k,
+// Where a panel kernel stores its S = V^T V (strictly upper 32 x 32):
+// S(l, c) at base + mat * stride + l * ls + c * cs.
+struct SBlock {
+    float *base;
+    int64_t stride;
+    int ls, cs;
+};
+cudaError_t launch_panel(float *H, float *tau, const SBlock &sb, int64_t batch, int m, int n, int k,
                          cudaStream_t st);
-cudaError_t launch_trailing(float *H, const float *Sws, const float *tau, int64_t batch, int m, int n, int k,
-                            cudaStream_t st);
+// SIMT fp32 trailing update (any m); S blocks (32 x 32, column-major) at
+// Sws + mat * s_stride.
+cudaError_t launch_trailing(float *H, const float *Sws, int64_t s_stride, const float *tau, int64_t batch, int m,
+                            int n, int k, cudaStream_t st);
 
 // Tensor-core (tcgen05, 3xTF32) trailing update; needs a row count m with
 // m % 4 == 0, m >= 128 and a 16-byte aligned H.  Sets *status to nonzero if a bounded wait gave up.
@@ -34,7 +43,8 @@ bool trailing_tc_supported(int m);
 struct TrailingMaps {
     CUtensorMap c;  // 32 rows x 128 trailing columns, 128-byte swizzle
     CUtensorMap v;   // 32 rows x 32 panel columns, 128-byte swizzle
-    CUtensorMap cq;  // 128 rows x 32 trailing columns, no swizzle (phase C)
+    CUtensorMap cq;  // 32 rows x 32 trailing columns, no swizzle (phase C)
+    CUtensorMap v64;  // 32 rows x 64 panel columns, 128-byte swizzle (rank-64 update)
 };
 cudaError_t prepare_trailing_tc(float *H, int64_t batch, int m, int n, TrailingMaps *maps);
 // Maps for applying the reflectors stored in H (n x n per matrix) to a
@@ -49,18 +59,50 @@ cudaError_t prepare_apply_maps(const float *H, int m, int hcols, float *C, int64
 cudaError_t launch_apply_tc(const TrailingMaps &maps, const float *H, const float *Sws, int64_t s_stride,
                             const float *tau, int *status, int64_t batch, int m, int hcols, int k,
                             int c_begin, int c_end, bool apply_t, cudaStream_t st);
-cudaError_t launch_trailing_tc(const TrailingMaps &maps, float *H, const float *Sws, const float *tau,
-                               int *status, int64_t batch, int m, int n, int k, cudaStream_t st);
+cudaError_t launch_trailing_tc(const TrailingMaps &maps, float *H, const float *Sws, int64_t s_stride,
+                               const float *tau, int *status, int64_t batch, int m, int n, int k, cudaStream_t st);
 
-// Workspace layout: one 32 x 32 float block per matrix holding the panel's
-// S = V^T V (strictly upper; the compact-WY T factor is T = D (I + S D)^-1,
-// D = diag(tau)), then a 256-byte status block (int status word first).
+// Rank-64 blocking (two 32-column panels per trailing update) for m x n
+// matrices with n >= 2048 and m <= 4096 (m % 4 == 0, the tensor-core
+// trailing update's condition): per 64 columns a panel, the in-block update
+// of the next 32 columns, a second panel, the cross Gram block V1^T V2 and
+// one rank-64 trailing update.  A static plan by (m, n).  The rank-64 update
+// moves half the HBM bytes of two rank-32 updates (-42% trailing time at
+// 16 x 4096^2), but the two in-block launches per block lengthen the
+// per-block chain of latency-bound kernels: at n = 512 and 1024 the step
+// was 5 to 7% slower, so smaller n keep rank-32 steps.
+constexpr int kOuter = 64;
+constexpr bool use_outer64(int64_t m, int64_t n) { return n >= 2048 && m <= 4096 && m % 4 == 0; }
+
+// Workspace layout: a 256-byte status block (one int status word per part of
+// a split batch), then one S block per matrix: 32 x 32 floats (column-major)
+// for rank-32 plans, 64 x 64 floats (row-major, S(l, c) at l * 64 + c) for
+// rank-64 plans.  S = V^T V (strictly upper); the compact-WY T factor is
+// T = D (I + S D)^-1, D = diag(tau).
 constexpr size_t kWsAlign = 256;
-constexpr size_t ws_t_bytes(int64_t batch)
+constexpr int64_t s_block_floats(int64_t m, int64_t n)
 {
-    return ((size_t)batch * kPanel * kPanel * sizeof(float) + kWsAlign - 1) / kWsAlign * kWsAlign;
+    return use_outer64(m, n) ? kOuter * kOuter : kPanel * kPanel;
 }
-constexpr size_t ws_total_bytes(int64_t batch) { return ws_t_bytes(batch) + kWsAlign; }
+constexpr size_t ws_t_bytes(int64_t batch, int64_t m, int64_t n)
+{
+    return ((size_t)batch * (size_t)s_block_floats(m, n) * sizeof(float) + kWsAlign - 1) / kWsAlign * kWsAlign;
+}
+constexpr size_t ws_total_bytes(int64_t batch, int64_t m, int64_t n) { return kWsAlign + ws_t_bytes(batch, m, n); }
+
+// In-block steps of a rank-64 block at columns k .. k+63 (S64: the
+// matrices' 64 x 64 row-major S blocks, s_stride floats apart; the two
+// panels store their S11 and S22 on its diagonal):
+// gram == false: C2 := (I - V1 T1^T V1^T) C2 for C2 = H[k:m, k+32:k+64], V1
+//   the reflectors of columns k .. k+31, T1 from S11 and tau;
+// gram == true: the off-diagonal block S12 = V1^T V2 over rows k+32 .. m-1.
+cudaError_t launch_inblock(float *H, const float *tau, float *S64, int64_t s_stride, int64_t batch, int m,
+                           int n, int k, bool gram, cudaStream_t st);
+// Rank-64 tensor-core trailing update of columns k+64 .. n-1 with the 64
+// reflectors of columns k .. k+63 (S64 complete) and tau.
+cudaError_t launch_trailing64_tc(const TrailingMaps &maps, float *H, const float *S64, int64_t s_stride,
+                                 const float *tau, int *status, int64_t batch, int m, int n, int k,
+                                 cudaStream_t st);
 
 // Validates and enqueues one batched geqrf (the body of fqr_geqrf_f32);
 // returns an FQR_* status.

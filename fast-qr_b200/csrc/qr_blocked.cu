@@ -149,7 +149,8 @@ cudaError_t launch_copy_in(const float *A, int64_t batch, int m, int n, int64_t 
 // only through Y = T^T W, solved from S = V^T V (strict upper) and tau.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256)
-trailing_simt_kernel(float *__restrict__ H, const float *__restrict__ Sws, const float *__restrict__ tau,
+trailing_simt_kernel(float *__restrict__ H, const float *__restrict__ Sws, int64_t s_stride,
+                     const float *__restrict__ tau,
                      int ld, int n, int k)
 {
     __shared__ float Vs[32][33];
@@ -191,7 +192,7 @@ trailing_simt_kernel(float *__restrict__ H, const float *__restrict__ Sws, const
     }
 #pragma unroll
     for (int q = 0; q < 4; ++q) Ws[4 * tg + q][lane] = acc[q];
-    const float *Sm = Sws + mat * (kPanel * kPanel);
+    const float *Sm = Sws + mat * s_stride;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const int cc = tg + 8 * i;
@@ -241,8 +242,8 @@ trailing_simt_kernel(float *__restrict__ H, const float *__restrict__ Sws, const
     }
 }
 
-cudaError_t launch_trailing(float *H, const float *Sws, const float *tau, int64_t batch, int m, int n, int k,
-                            cudaStream_t st)
+cudaError_t launch_trailing(float *H, const float *Sws, int64_t s_stride, const float *tau, int64_t batch, int m,
+                            int n, int k, cudaStream_t st)
 {
     const int nc = n - k - kPanel;
     if (nc <= 0) return cudaSuccess;
@@ -251,7 +252,7 @@ cudaError_t launch_trailing(float *H, const float *Sws, const float *tau, int64_
         const int64_t nb = (batch - b0) < 65535 ? (batch - b0) : 65535;
         dim3 grid(tiles, (unsigned)nb);
         cudaError_t e = launch_dependent(trailing_simt_kernel, grid, dim3(256), 0, st, nullptr, 0,
-                                         H + b0 * (int64_t)m * n, Sws + b0 * kPanel * kPanel, tau + b0 * n,
+                                         H + b0 * (int64_t)m * n, Sws + b0 * s_stride, s_stride, tau + b0 * n,
                                          m, n, k);
         if (e != cudaSuccess) return e;
     }

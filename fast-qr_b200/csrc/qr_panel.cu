@@ -48,7 +48,8 @@ constexpr int kStagePitch = 36;  // floats per row of a warp's 32 x 32 staging b
 // ---------------------------------------------------------------------------
 template <int NW, int R, bool CLUSTER>
 __global__ void __launch_bounds__(NW * 32, 1)
-panel_kernel(float *__restrict__ H, float *__restrict__ tau, float *__restrict__ Tws, int ld, int n, int k)
+panel_kernel(float *__restrict__ H, float *__restrict__ tau, float *__restrict__ Sb, int64_t s_stride, int s_ls,
+             int s_cs, int ld, int n, int k)
 {
     constexpr int ROWS = NW * 32 * R;  // panel rows held by one CTA
     constexpr int NR = 8 * R;          // rows per thread
@@ -292,17 +293,6 @@ panel_kernel(float *__restrict__ H, float *__restrict__ tau, float *__restrict__
     __syncthreads();
     pdl_trigger();  // the trailing update may be scheduled (it waits for this grid)
 
-    // The trailing update needs T only through Y = T^T W; since
-    // T = D (I + S D)^-1 with D = diag(tau) and S(l, c) = v_l^T v_c (l < c),
-    // it solves (I + D S^T) Y = D W by forward substitution instead.  So the
-    // panel stores S (strictly upper, column-major) in the T slot and tau.
-    if (top) {
-        float *Sm = Tws + mat * (kPanel * kPanel);
-#pragma unroll 4
-        for (int c = 0; c < 32; ++c) Sm[c * 32 + lane] = (lane < c && c < w) ? Ysm[lane][c] : 0.0f;
-        if (lane < w) tau[mat * n + k + lane] = tau_s[lane];
-    }
-
     // store: the reverse of the load (coalesced 128-byte column segments)
 #pragma unroll
     for (int b = 0; b < R; ++b) {
@@ -324,6 +314,19 @@ panel_kernel(float *__restrict__ H, float *__restrict__ tau, float *__restrict__
             }
         }
         __syncwarp();
+    }
+
+    // The trailing update needs T only through Y = T^T W; since
+    // T = D (I + S D)^-1 with D = diag(tau) and S(l, c) = v_l^T v_c (l < c),
+    // it solves (I + D S^T) Y = D W by forward substitution instead.  So the
+    // panel stores S (strictly upper; S(l, c) at Sb + mat * s_stride + l * s_ls
+    // + c * s_cs) and tau, after its rows (the top warp's stores are on the
+    // kernel's critical path; measured C2 -3%).
+    if (top) {
+        float *Sm = Sb + mat * s_stride;
+#pragma unroll 4
+        for (int c = 0; c < 32; ++c) Sm[lane * s_ls + c * s_cs] = (lane < c && c < w) ? Ysm[lane][c] : 0.0f;
+        if (lane < w) tau[mat * n + k + lane] = tau_s[lane];
     }
     if constexpr (CLUSTER) {
         // keep every CTA's shared memory alive until all remote writes landed
@@ -349,7 +352,7 @@ PanelShape panel_shape(int m)
 }
 
 template <int NW, int R>
-static cudaError_t launch_panel_t(float *H, float *tau, float *Tws, int64_t batch, int ld, int n, int k,
+static cudaError_t launch_panel_t(float *H, float *tau, const SBlock &sb, int64_t batch, int ld, int n, int k,
                                   int cluster, cudaStream_t st)
 {
     // the limit covers static + dynamic shared memory beyond 48 KB, so it is
@@ -360,7 +363,7 @@ static cudaError_t launch_panel_t(float *H, float *tau, float *Tws, int64_t batc
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);
         if (e != cudaSuccess) return e;
         return launch_dependent(panel_kernel<NW, R, false>, dim3((unsigned)batch), dim3(NW * 32), dyn, st,
-                                nullptr, 0, H, tau, Tws, ld, n, k);
+                                nullptr, 0, H, tau, sb.base, sb.stride, sb.ls, sb.cs, ld, n, k);
     }
     cudaError_t e = cudaFuncSetAttribute(panel_kernel<NW, R, true>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);
@@ -371,19 +374,19 @@ static cudaError_t launch_panel_t(float *H, float *tau, float *Tws, int64_t batc
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     return launch_dependent(panel_kernel<NW, R, true>, dim3((unsigned)(batch * cluster)), dim3(NW * 32), dyn,
-                            st, attr, 1, H, tau, Tws, ld, n, k);
+                            st, attr, 1, H, tau, sb.base, sb.stride, sb.ls, sb.cs, ld, n, k);
 }
 
-cudaError_t launch_panel(float *H, float *tau, float *Tws, int64_t batch, int ld, int n, int k,
+cudaError_t launch_panel(float *H, float *tau, const SBlock &sb, int64_t batch, int ld, int n, int k,
                          cudaStream_t st)
 {
     const PanelShape s = panel_shape(ld - k);
     if (s.cluster > 8) return cudaErrorInvalidValue;
     if (s.warps == 4 && s.rows_per_thread_blocks == 1)
-        return launch_panel_t<4, 1>(H, tau, Tws, batch, ld, n, k, 1, st);
-    if (s.warps == 4) return launch_panel_t<4, 2>(H, tau, Tws, batch, ld, n, k, 1, st);
-    if (s.warps == 8) return launch_panel_t<8, 2>(H, tau, Tws, batch, ld, n, k, s.cluster, st);
-    return launch_panel_t<16, 2>(H, tau, Tws, batch, ld, n, k, s.cluster, st);
+        return launch_panel_t<4, 1>(H, tau, sb, batch, ld, n, k, 1, st);
+    if (s.warps == 4) return launch_panel_t<4, 2>(H, tau, sb, batch, ld, n, k, 1, st);
+    if (s.warps == 8) return launch_panel_t<8, 2>(H, tau, sb, batch, ld, n, k, s.cluster, st);
+    return launch_panel_t<16, 2>(H, tau, sb, batch, ld, n, k, s.cluster, st);
 }
 
 }  // namespace fqr

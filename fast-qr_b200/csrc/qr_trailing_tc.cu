@@ -521,6 +521,7 @@ cudaError_t prepare_apply_maps(const float *H, int ld, int hcols, float *C, int6
     const cuuint64_t cdims[3] = {(cuuint64_t)ld, (cuuint64_t)c_cols, (cuuint64_t)batch};
     const cuuint64_t cstrides[2] = {(cuuint64_t)ld * 4, (cuuint64_t)ld * (cuuint64_t)c_cols * 4};
     const cuuint32_t box_c[3] = {kRC, kTN, 1}, box_v[3] = {kRC, kPanel, 1}, unit[3] = {1, 1, 1};
+    const cuuint32_t box_v64[3] = {kRC, 2 * kPanel, 1};
     const cuuint32_t box_cq[3] = {32, kCQCols, 1};  // one warp's 32 rows of a quarter
     if (enc(&maps->c, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, C, cdims, cstrides, box_c, unit,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -530,6 +531,9 @@ cudaError_t prepare_apply_maps(const float *H, int ld, int hcols, float *C, int6
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS ||
         enc(&maps->cq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, C, cdims, cstrides, box_cq, unit,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS ||
+        enc(&maps->v64, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(H), hdims, hstrides, box_v64,
+            unit, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return cudaErrorInvalidValue;
     return cudaSuccess;
@@ -563,11 +567,11 @@ cudaError_t launch_apply_tc(const TrailingMaps &maps, const float *H, const floa
     return cudaSuccess;
 }
 
-cudaError_t launch_trailing_tc(const TrailingMaps &maps, float *H, const float *Sws, const float *tau,
-                               int *status, int64_t batch, int m, int n, int k, cudaStream_t st)
+cudaError_t launch_trailing_tc(const TrailingMaps &maps, float *H, const float *Sws, int64_t s_stride,
+                               const float *tau, int *status, int64_t batch, int m, int n, int k, cudaStream_t st)
 {
     if (n - k - kPanel <= 0) return cudaSuccess;
-    return launch_apply_tc(maps, H, Sws, kPanel * kPanel, tau, status, batch, m, n, k, k + kPanel, n, true, st);
+    return launch_apply_tc(maps, H, Sws, s_stride, tau, status, batch, m, n, k, k + kPanel, n, true, st);
 }
 
 }  // namespace fqr

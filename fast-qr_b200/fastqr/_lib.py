@@ -37,7 +37,7 @@ SIGNATURES = {
     "fqr_version": (ctypes.c_int, []),
 }
 
-STAGES = ("small", "copy_in", "panel", "trailing")
+STAGES = ("small", "copy_in", "panel", "trailing", "inblock")
 
 STATUS = {
     0: "FQR_OK",

@@ -94,13 +94,13 @@ int fqr_plan_describe(int64_t batch, int64_t n, char *buf, size_t len);
 int fqr_launch_count(int64_t batch, int64_t n);
 
 /* Largest batch fqr_geqrf_f32_noalloc accepts when n > 64 (its static
- * scratch holds this many 32 x 32 float T factors: 4 MiB per device). */
+ * scratch holds this many 64 x 64 float S blocks: 16 MiB per device). */
 #define FQR_NOALLOC_MAX_BATCH 1024
 
 /*
  * Same computation and output as fqr_geqrf_f32, for callers that cannot
  * allocate device memory: no workspace argument, and the library allocates
- * nothing.  Scratch comes from a fixed 4 MiB __device__ array inside the
+ * nothing.  Scratch comes from a fixed 16 MiB __device__ array inside the
  * library, present on every GPU that loads it until the process exits.
  * Its address is looked up on the first call made on each device (that device
  * current); make that first call before any stream capture.
@@ -203,7 +203,8 @@ enum {
     FQR_STAGE_COPY_IN = 1,   /* row-major A -> column-major H */
     FQR_STAGE_PANEL = 2,     /* panel factorisation + T factor */
     FQR_STAGE_TRAILING = 3,  /* trailing update C -= V T^T V^T C */
-    FQR_NUM_STAGES = 4
+    FQR_STAGE_INBLOCK = 4,   /* rank-64 blocks: next-panel update and cross Gram block */
+    FQR_NUM_STAGES = 5
 };
 
 /*

@@ -69,9 +69,22 @@ def test_workspace_and_plan_depend_on_shape_only():
     # two parts of a batch on two streams, each copy-in + 8 panels + 7 trailing
     assert fastqr.launch_count(256, 256) == 2 * (1 + 8 + 7)
     assert fastqr.launch_count(1, 256) == 1 + 8 + 7
-    # four parts for n >= 2048 (64 panels: copy-in + 64 panels + 63 trailing each)
-    assert fastqr.launch_count(16, 2048) == 4 * (1 + 64 + 63)
-    assert fastqr.launch_count(3, 2048) == 3 * (1 + 64 + 63)
+    # n >= 2048: rank-64 blocks (panel, in-block update, panel, then Gram
+    # block + trailing update for all but the last block); four parts for
+    # n >= 2048: 32 blocks each
+    assert "rank 64" in fastqr.plan(16, 4096) and "rank 32" in fastqr.plan(64, 1024)
+    assert fastqr.launch_count(16, 2048) == 4 * (1 + 32 * 3 + 31 * 2)
+    assert fastqr.launch_count(3, 2048) == 3 * (1 + 32 * 3 + 31 * 2)
+    assert fastqr.launch_count(64, 1024) == 2 * (1 + 32 + 31)
+    # 2100 = 32 blocks of 64 + a 32- and a 20-column panel (every block has a
+    # trailing update, the first rank-32 panel too)
+    assert fastqr.launch_count(1, 2100) == 1 + 32 * 3 + 32 * 2 + 2 + 1
+    # rows above 4096: rank-32 steps only
+    assert fastqr.launch_count(1, 8192) == 1 + 256 + 255
+    # a status block, then one S block per matrix (64 x 64 for rank-64 plans)
+    assert fastqr.workspace_bytes(16, 4096) == 256 + 16 * 64 * 64 * 4
+    assert fastqr.workspace_bytes(64, 1024) == 256 + 64 * 32 * 32 * 4
+    assert fastqr.workspace_bytes(2, 8192) == 256 + 2 * 32 * 32 * 4
 
 
 def test_python_api_rejects_cpu_tensors():

@@ -243,6 +243,21 @@ def test_largest_n(dev):
     assert g["ok"], g
 
 
+@pytest.mark.parametrize("n", [2048, 2112])
+def test_rank64_plan_columns(n, dev):
+    """n >= 2048: per 64 columns two panels, the in-block update between
+    them, the Gram block and one rank-64 tensor-core trailing update (2112 =
+    33 blocks, the last without a trailing update); H and tau per column
+    against float64 geqrf."""
+    assert "rank 64" in fastqr.plan(1, n)
+    a = inputs.generate_input(1, n, 1, 700 + n, device=dev)
+    h, t = fastqr.geqrf(a)
+    assert gates(a, h, t, chunk=1)["ok"]
+    h64, t64 = torch.geqrf(a.double())
+    he, te = column_errors(h, t, h64, t64)
+    assert float(he.max()) <= COL_TOL and float(te.max()) <= COL_TOL, (float(he.max()), float(te.max()))
+
+
 @pytest.mark.parametrize("n", [1100, 2100])
 def test_cluster_panel_columns(n, dev):
     """Panels taller than 1024 rows run as thread-block clusters of 512-row

@@ -54,12 +54,19 @@ def test_rect_matches_oracle(m, n, dev):
     assert g["ok"], g
 
 
-@pytest.mark.parametrize("m,n", [(1024, 512), (4096, 256)])
+@pytest.mark.parametrize("m,n", [(1024, 512), (4096, 256), (2304, 2080)])
 def test_rect_large_gates(m, n, dev):
+    """Large tall blocks; 2304 x 2080 takes the rank-64 plan (32 blocks of 64
+    columns, then one 32-column panel), checked per column against float64
+    geqrf too."""
     a = tall(2, m, n, 77 + n).to(dev)
     h, t = fastqr.geqrf(a)
     g = gates(a, h, t, chunk=1)
     assert g["ok"], g
+    if n >= 2048:
+        h64, t64 = torch.geqrf(a.double())
+        he, te = column_errors(h, t, h64, t64)
+        assert float(he.max()) <= COL_TOL and float(te.max()) <= COL_TOL, (float(he.max()), float(te.max()))
 
 
 def test_rect_batch_split_and_strides(dev):
