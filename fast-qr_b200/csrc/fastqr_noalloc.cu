@@ -73,6 +73,9 @@ extern "C" int fqr_geqrf_f32_noalloc(const float *A, int64_t batch, int64_t n, i
     if (batch == 0 || n == 0) return FQR_OK;
     if (n > FQR_MAX_N) return FQR_EUNSUPPORTED;
     const size_t need = fqr_workspace_bytes(batch, n);
+    // the documented limit (n > 64: at most FQR_NOALLOC_MAX_BATCH matrices),
+    // whatever the plan's S block size
+    if (need > 0 && batch > FQR_NOALLOC_MAX_BATCH) return FQR_ENOALLOC_LIMIT;
     if (need > kNoAllocScratchBytes) return FQR_ENOALLOC_LIMIT;
     void *scratch = nullptr;
     if (need > 0) {
