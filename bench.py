@@ -65,15 +65,50 @@ def panel_bytes(n: int, b: int = 32) -> float:
     return sum(8.0 * b * (n - k) + 4.0 * b + 4.0 * b * b for k in range(0, n, b))
 
 
-def trailing_flops(n: int, b: int = 32) -> float:
-    """Algorithmic flops of all trailing updates of one matrix:
-    per panel k: 4 (n-k) b (n-k-b) + b^2 (n-k-b)."""
+def plan_blocks(n: int) -> tuple:
+    """(rank-64 blocks, columns left for rank-32 steps) of the library's static
+    plan for square n x n (rank-64 blocks for 2048 <= n <= 4096, n % 4 == 0)."""
+    outer = 2048 <= n <= 4096 and n % 4 == 0
+    blocks = n // 64 if outer else 0
+    return blocks, n - 64 * blocks
+
+
+def trailing_flops(n: int) -> float:
+    """Algorithmic flops of all trailing updates of one matrix: per update at
+    column k with b reflectors, 4 (n-k) b (n-k-b) + b^2 (n-k-b); b = 64 for
+    the rank-64 blocks, 32 for the rank-32 steps."""
+    blocks, _ = plan_blocks(n)
+    steps = [(64 * i, 64) for i in range(blocks)] + [(k, 32) for k in range(64 * blocks, n, 32)]
     tot = 0.0
-    for k in range(0, n, b):
+    for k, b in steps:
         m, nc = n - k, n - k - b
         if nc > 0:
             tot += 4.0 * m * b * nc + b * b * nc
     return tot
+
+
+def inblock_bytes(n: int) -> float:
+    """Algorithmic HBM bytes of the in-block steps of one matrix: per rank-64
+    block at k the update reads V1 and C2 ((n-k) x 32 each) and writes C2; the
+    Gram step (all but a last block with no columns right of it) reads V1 and
+    V2 below row k+32."""
+    blocks, rest = plan_blocks(n)
+    tot = 0.0
+    for i in range(blocks):
+        m = n - 64 * i
+        tot += 12.0 * 32 * m
+        if rest > 0 or i + 1 < blocks:
+            tot += 8.0 * 32 * (m - 32)
+    return tot
+
+
+def stage_launches(n: int) -> dict:
+    """Launches per kernel class of one blocked factorisation (one stream)."""
+    blocks, rest = plan_blocks(n)
+    rp = -(-rest // 32)
+    full = blocks if rest > 0 else max(blocks - 1, 0)
+    return {"small": 1, "copy_in": 1, "panel": 2 * blocks + rp, "inblock": blocks + full,
+            "trailing": full + max(rp - 1, 0)}
 
 
 class ClockSampler:
@@ -344,15 +379,14 @@ def kernel_roofline(cfg_name, a, h, tau, ws, flush, steps, dev) -> dict:
     traffic = _traffic_from_profiles(cfg_name, dom)
     share = {kname: round(v / max(sum(per_step_ms.values()), 1e-12), 4) for kname, v in per_step_ms.items()}
     # launches of the dominant kernel class per profiled step (one stream)
-    panels = -(-n // 32)
-    per_step = {"small": 1, "copy_in": 1, "panel": panels, "trailing": panels - 1}[dom]
+    per_step = stage_launches(n)[dom]
     base = {"kernel": dom, "stage_ms_per_step": per_step_ms, "stage_share": share,
             "traffic": traffic, "launches_per_step": per_step, "peak_source": pk["source"]}
-    if dom in ("small", "copy_in", "panel"):
+    if dom in ("small", "copy_in", "panel", "inblock"):
         # the panel does O(m b^2) flops on O(m b) data: it is framed by HBM
         # bytes, and its limiter is the column-by-column dependency chain
         alg = batch * {"small": bytes_per_matrix(n), "copy_in": 8.0 * n * n,
-                       "panel": panel_bytes(n)}[dom]
+                       "panel": panel_bytes(n), "inblock": inblock_bytes(n)}[dom]
         ach = alg / t / 1e9
         base.update({"bound": "hbm", "achieved": ach, "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": ach / pk["hbm_gbs"], "alg_bytes_per_step": alg,
