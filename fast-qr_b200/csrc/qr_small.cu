@@ -33,15 +33,18 @@ constexpr int kSmallWarps = 4;
 // slot holding column k; lanes with a column j <= k are left unchanged).
 // The owner lane keeps its column unscaled (x, not v = scale * x) so the
 // update needs no per-element select; its scale is recorded and applied when
-// the factor is written out.
-template <int NP, int NC, int S>
+// the factor is written out.  Only the first W window rows are touched: the
+// caller guarantees rows W .. NP-1 are zero (after k steps the window holds
+// rows k .. k+NP-1 of the matrix, and rows n .. are zero), so skipping them
+// changes no bit of the result.
+template <int NP, int NC, int S, int W>
 __device__ __forceinline__ void small_step(float (&a)[NC][NP], int k, int lane, float *stage_row,
                                            float *tau_stage, float *scale_stage,
                                            double *scaled_stage)
 {
     const int kl = k & 31;
     const bool owner = lane == kl;
-    float x[NP];
+    float x[W];
     float s0 = 0.0f, s1 = 0.0f;
     float d0[NC], d1[NC];
     bool anynz = false;
@@ -49,7 +52,7 @@ __device__ __forceinline__ void small_step(float (&a)[NC][NP], int k, int lane, 
     for (int c = 0; c < NC; ++c) d0[c] = d1[c] = 0.0f;
     const float alpha = __shfl_sync(kFull, a[S][0], kl);
 #pragma unroll
-    for (int i = 1; i < NP; ++i) {
+    for (int i = 1; i < W; ++i) {
         x[i] = __shfl_sync(kFull, a[S][i], kl);
         anynz |= (x[i] != 0.0f);
         if (i & 1) {
@@ -89,7 +92,7 @@ __device__ __forceinline__ void small_step(float (&a)[NC][NP], int k, int lane, 
 #pragma unroll
         for (int c = 0; c < NC; ++c) rowk[c] = (owner && c == S) ? r.beta : a[c][0] - tw[c];
 #pragma unroll
-        for (int i = 1; i < NP; ++i) {
+        for (int i = 1; i < W; ++i) {
 #pragma unroll
             for (int c = 0; c < NC; ++c) a[c][i - 1] = fmaf(-tws[c], x[i], a[c][i]);
         }
@@ -97,13 +100,13 @@ __device__ __forceinline__ void small_step(float (&a)[NC][NP], int k, int lane, 
         // LAPACK order: sigma in double, then v, then w_j = v^T a_j
         double sd = 0.0;
 #pragma unroll
-        for (int i = 1; i < NP; ++i) sd = fma((double)x[i], (double)x[i], sd);
+        for (int i = 1; i < W; ++i) sd = fma((double)x[i], (double)x[i], sd);
         r = reflector_from_double(alpha, sd);
         float wv[NC];
 #pragma unroll
         for (int c = 0; c < NC; ++c) wv[c] = a[c][0];
 #pragma unroll
-        for (int i = 1; i < NP; ++i) {
+        for (int i = 1; i < W; ++i) {
             const float v = reflector_apply(r, x[i]);
 #pragma unroll
             for (int c = 0; c < NC; ++c) wv[c] = fmaf(v, a[c][i], wv[c]);
@@ -115,7 +118,7 @@ __device__ __forceinline__ void small_step(float (&a)[NC][NP], int k, int lane, 
             rowk[c] = (owner && c == S) ? r.beta : a[c][0] - tw[c];
         }
 #pragma unroll
-        for (int i = 1; i < NP; ++i) {
+        for (int i = 1; i < W; ++i) {
             const float v = reflector_apply(r, x[i]);
 #pragma unroll
             for (int c = 0; c < NC; ++c) a[c][i - 1] = fmaf(-tw[c], v, a[c][i]);
@@ -130,7 +133,28 @@ __device__ __forceinline__ void small_step(float (&a)[NC][NP], int k, int lane, 
         scaled_stage[k] = r.scale_d;
     }
 #pragma unroll
-    for (int c = 0; c < NC; ++c) a[c][NP - 1] = 0.0f;
+    for (int c = 0; c < NC; ++c) a[c][W - 1] = 0.0f;
+}
+
+// Steps [8P, min(8P + 8, kend)) with the window W = NP - 8P (rows past it are
+// zero: 8P steps have shifted NP >= n rows up by 8P), then the next phase.
+// Eight steps per phase keep one compact runtime loop per phase (NP / 8
+// copies of the step body in all) while the per-step work shrinks with the
+// tail: sum over steps of W is ~(NP^2 / 2) instead of NP^2.
+template <int NP, int NC, int P>
+__device__ __forceinline__ void small_phases(float (&a)[NC][NP], int kend, int lane, float *stage, int ld,
+                                             float *tau_stage, float *scale_stage, double *scaled_stage)
+{
+    constexpr int W = NP - 8 * P;
+    constexpr int S = (8 * P) / 32;  // register slot of columns 8P .. 8P+7
+    const int kb = 8 * P, ke = kend < kb + 8 ? kend : kb + 8;
+#pragma unroll 1
+    for (int k = kb; k < ke; ++k)
+        small_step<NP, NC, S, W>(a, k, lane, stage + k * ld + lane, tau_stage, scale_stage, scaled_stage);
+    if constexpr (P + 1 < NP / 8) {
+        if (kend > kb + 8)
+            small_phases<NP, NC, P + 1>(a, kend, lane, stage, ld, tau_stage, scale_stage, scaled_stage);
+    }
 }
 
 // The final row (k = n-1) has an empty tail: tau = 0, the row is unchanged.
@@ -170,16 +194,8 @@ geqrf_small_kernel(const float *__restrict__ A, int64_t batch, int n, int64_t bs
             a[c][i] = (jin && i < n) ? __ldg(Am + (int64_t)i * rs + (int64_t)j * cs) : 0.0f;
     }
 
-    const int k1 = (n - 1) < 32 ? (n - 1) : 32;  // steps whose column sits in slot 0
-#pragma unroll 1
-    for (int k = 0; k < k1; ++k)
-        small_step<NP, NC, 0>(a, k, lane, stage + k * LD + lane, tau_stage, scale_stage, scaled_stage);
-    if constexpr (NC == 2) {
-#pragma unroll 1
-        for (int k = 32; k < n - 1; ++k)
-            small_step<NP, NC, 1>(a, k, lane, stage + k * LD + lane, tau_stage, scale_stage,
-                                  scaled_stage);
-    }
+    // steps 0 .. n-2 (the last row has an empty tail)
+    small_phases<NP, NC, 0>(a, n - 1, lane, stage, LD, tau_stage, scale_stage, scaled_stage);
     small_last_row<NP, NC>(a, stage + (n - 1) * LD + lane);
     if (lane == 0) tau_stage[n - 1] = 0.0f;
     __syncwarp();
