@@ -258,6 +258,24 @@ def test_rank64_plan_columns(n, dev):
     assert float(he.max()) <= COL_TOL and float(te.max()) <= COL_TOL, (float(he.max()), float(te.max()))
 
 
+def test_rank64_plan_special_structure(dev):
+    """The rank-64 plan (n = 2048) on inputs that reach the panels' robust
+    path and zero reflectors inside the in-block and Gram steps: a block of
+    exactly zero columns straddling two 64-column blocks, exactly repeated
+    columns, and a 1e-30 scaling whose squares underflow in float32; the QR
+    gates on each."""
+    n = 2048
+    g = torch.Generator().manual_seed(5)
+    a = torch.randn(3, n, n, generator=g)
+    a[0, :, 100:164] = 0.0
+    a[1, :, 1024:1100] = a[1, :, 0:76]
+    a[2] *= 1e-30
+    a = a.to(dev)
+    h, t = fastqr.geqrf(a)
+    g = gates(a, h, t, chunk=1)
+    assert g["ok"], g
+
+
 @pytest.mark.parametrize("n", [1100, 2100])
 def test_cluster_panel_columns(n, dev):
     """Panels taller than 1024 rows run as thread-block clusters of 512-row
