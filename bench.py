@@ -8,6 +8,8 @@ configuration is C2 (256 x 256^2, graded columns): BASELINE.json's configs[1].
 Multi-GPU (torchrun, one process per GPU): weak scaling, each rank factors a
 full configuration batch of its own (contiguous shard of a global batch of
 batch x N), no collective on the data path; time = max over ranks.
+``--strong`` splits the configuration's own batch over the ranks instead
+(C5 on 8 GPUs: 2 matrices per GPU).
 
 Prints ONE JSON line on rank 0.  ``--impl reference`` times the reference's
 own CPU implementation of the path -- torch.geqrf on the host (its
@@ -251,8 +253,11 @@ def run_reference(args) -> int:
 
 def _config_block(args, world) -> dict:
     cfg = inputs.CONFIGS[args.config]
-    return {"workload": f"{args.config}: {cfg['desc']}", "batch_per_gpu": cfg["batch"], "n": cfg["n"],
-            "global_batch": cfg["batch"] * world, "l2": "flushed before every step (256 MiB write)",
+    strong = getattr(args, "strong", False)
+    per = -(-cfg["batch"] // world) if strong else cfg["batch"]
+    return {"workload": f"{args.config}: {cfg['desc']}", "batch_per_gpu": per, "n": cfg["n"],
+            "global_batch": cfg["batch"] if strong else cfg["batch"] * world,
+            "l2": "flushed before every step (256 MiB write)",
             "parallelism": f"batch-sharded x{world}, no collective"}
 
 
@@ -269,10 +274,17 @@ def run_fastqr(args) -> int:
     dev = torch.device("cuda", local if world > 1 else 0)
     torch.cuda.set_device(dev)
     cfg = inputs.CONFIGS[args.config]
-    n, batch = cfg["n"], cfg["batch"]
+    n = cfg["n"]
     steps = args.steps
 
-    a, first = rank_inputs(args.config, args.seed, world, rank, dev, weak=True)
+    # weak scaling: every rank a full configuration batch; strong (--strong):
+    # the configuration's batch split into contiguous shards (C5 on 8 GPUs:
+    # 2 matrices per GPU)
+    a, first = rank_inputs(args.config, args.seed, world, rank, dev, weak=not args.strong)
+    batch = a.shape[0]
+    if batch < 1:
+        raise SystemExit(f"--strong: {args.config}'s batch of {cfg['batch']} leaves rank {rank} no matrix")
+    global_batch = cfg["batch"] if args.strong else world * batch
     h, tau = fastqr.empty_outputs(batch, n, dev)
     ws = torch.empty(max(1, fastqr.workspace_bytes(batch, n)), dtype=torch.uint8, device=dev)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
@@ -311,7 +323,7 @@ def run_fastqr(args) -> int:
     total_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
     total_ms = max_over_ranks(total_ms, dev)
     ms = total_ms / steps
-    value = world * batch / (ms / 1e3)
+    value = global_batch / (ms / 1e3)
 
     # per-kernel times for the roofline: same steps again, kernels timed alone
     roof = kernel_roofline(args.config, a, h, tau, ws, flush, steps, dev)
@@ -319,7 +331,7 @@ def run_fastqr(args) -> int:
     # end to end through the public API with host buffers
     e2e = end_to_end(a, n, batch, dev, max(3, min(steps, 50)))
     e2e_value = max_over_ranks(e2e["ms"], dev)
-    e2e_mps = world * batch / (e2e_value / 1e3)
+    e2e_mps = global_batch / (e2e_value / 1e3)
 
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu:
@@ -332,8 +344,8 @@ def run_fastqr(args) -> int:
         line = {
             "metric": f"matrices/s ({args.config} geqrf)", "value": value, "unit": "matrices/s",
             "n_gpus": world, "steps": steps, "warmup": args.warmup, "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded, the reference generator's distributions)",
+            "higher_is_better": True, "scaling": "strong" if args.strong else "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic (seeded, the reference generator's distributions)",
             "config": _config_block(args, world),
             "tflops": value * flops_per_matrix(n) / 1e12,
             "hbm_gbs_alg": value * bytes_per_matrix(n) / 1e9,
@@ -646,6 +658,9 @@ def main() -> int:
     ap.add_argument("--impl", default="fastqr", choices=["fastqr", "reference"])
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--strong", action="store_true",
+                    help="strong scaling: split the configuration's batch over the ranks "
+                         "(default: weak, every rank factors a full batch)")
     ap.add_argument("--cols", type=int, default=None,
                     help="--op rect: columns of the tall blocks (default 3/4 of n)")
     ap.add_argument("--op", default="geqrf", choices=["geqrf", "orgqr", "ormqr", "rect"],
