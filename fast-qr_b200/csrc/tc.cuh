@@ -87,18 +87,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *mbar, uint32_t parity, uint6
 }
 
 // --- MMA --------------------------------------------------------------------
-// Shared-memory matrix descriptor, no swizzle ("interleaved" core matrices of
-// 8 rows x 16 bytes).  lbo/sbo in bytes (multiples of 16), version 1.
-__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo)
-{
-    uint64_t d = 0;
-    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
-    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
-    d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
-    d |= (uint64_t)1 << 46;
-    return d;
-}
-
 // Descriptor of a K-major operand in the 128-byte swizzle layout: each M/N
 // row holds 32 consecutive 32-bit K elements (128 bytes) with its 16-byte
 // chunks permuted by XOR with (row % 8); 8-row atoms of 1024 bytes, which
@@ -117,13 +105,6 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr)
     d |= (uint64_t)2 << 61;            // 128-byte swizzle
     return d;
 }
-// Byte offset of 32-bit element (row, e) (e < 32) in a 128-byte-swizzled
-// tile whose rows are 128 bytes apart.
-__host__ __device__ constexpr uint32_t sw128_offset(int row, int e)
-{
-    return (uint32_t)(row * 128 + ((((e >> 2) ^ row) & 7) << 4) + (e & 3) * 4);
-}
-
 // Instruction descriptor: kind::tf32, D = f32, A = B = tf32, dense.
 // a_mn / b_mn select MN-major operands (0 = K-major).
 __host__ __device__ constexpr uint32_t idesc_tf32(int M, int N, int a_mn, int b_mn)
@@ -187,21 +168,6 @@ __device__ __forceinline__ void tmem_ld_32x32(uint32_t taddr, float (&v)[32])
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
-// 32 lanes x 16 consecutive 32-bit columns
-__device__ __forceinline__ void tmem_ld_32x16(uint32_t taddr, float (&v)[16])
-{
-    uint32_t r[16];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-          "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr)
-        : "memory");
-#pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
 __device__ __forceinline__ void tmem_ld_wait()
 {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
@@ -261,15 +227,8 @@ __device__ __forceinline__ void bulk_load(void *dst_smem, const void *src, uint3
         :: "r"(smem_addr(dst_smem)), "l"(src), "r"(bytes), "r"(smem_addr(mbar))
         : "memory");
 }
-// 3-D tiled tensor store of a box from this CTA's shared memory; elements
+// 3-D tiled global tile += shared tile (fp32 add at the L2); elements
 // outside the tensor are not written.  Completion is tracked by bulk groups.
-__device__ __forceinline__ void tma_store_3d(const void *tmap, int x, int y, int z, const void *src_smem)
-{
-    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];"
-                 :: "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(smem_addr(src_smem))
-                 : "memory");
-}
-// global tile += shared tile (fp32 add at the L2), bulk-group completion
 __device__ __forceinline__ void tma_reduce_add_3d(const void *tmap, int x, int y, int z, const void *src_smem)
 {
     asm volatile("cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group [%0, {%1, %2, %3}], [%4];"
@@ -312,12 +271,6 @@ __device__ __forceinline__ void cp_async_wait_all()
 {
     asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
-// wait until at most N committed groups are still pending
-template <int N>
-__device__ __forceinline__ void cp_async_wait_pending()
-{
-    asm volatile("cp.async.wait_group %0;" :: "n"(N) : "memory");
-}
 
 // --- 3xTF32 split: x = hi + lo with hi exactly representable in TF32 -------
 // kind::tf32 reads a 32-bit operand by dropping its 13 low mantissa bits
@@ -327,11 +280,6 @@ __device__ __forceinline__ void cp_async_wait_pending()
 __device__ __forceinline__ float tf32_lo(float x)
 {
     return x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
-}
-__device__ __forceinline__ void split_tf32(float x, float &hi, float &lo)
-{
-    hi = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
-    lo = x - hi;
 }
 
 }  // namespace tc
