@@ -176,9 +176,9 @@ struct StageTimer {
 // with the rank-64 plan, per 64 columns: panel(k), the update of columns
 // k+32 .. k+63 by panel k's reflectors, panel(k+32), the Gram block
 // V1^T V2 and one trailing update with all 64 reflectors.
-int enqueue_blocked(const float *A, int64_t batch, int m, int n, int64_t a_bstride, int64_t a_rstride,
-                    int64_t a_cstride, float *H, float *tau, float *Sws, int *status_base, int part,
-                    unsigned clear_mask, bool tc, cudaStream_t st, StageTimer *tm)
+int enqueue_blocked(const float *A, int64_t batch, int64_t batch_all, int m, int n, int64_t a_bstride,
+                    int64_t a_rstride, int64_t a_cstride, float *H, float *tau, float *Sws, int *status_base,
+                    int part, unsigned clear_mask, bool tc, cudaStream_t st, StageTimer *tm)
 {
     // status_base[part] records a bounded wait that gave up; the copy-in
     // clears the words of clear_mask
@@ -215,7 +215,8 @@ int enqueue_blocked(const float *A, int64_t batch, int m, int n, int64_t a_bstri
                 (!step(FQR_STAGE_INBLOCK,
                        [&] { return fqr::launch_inblock(H, tau, Sws, s_stride, batch, m, n, k, true, st); }) ||
                  !step(FQR_STAGE_TRAILING, [&] {
-                     return fqr::launch_trailing64_tc(maps, H, Sws, s_stride, tau, status, batch, m, n, k, st);
+                     return fqr::launch_trailing64_tc(maps, H, Sws, s_stride, tau, status, batch, batch_all, m, n,
+                                                      k, st);
                  })))
                 return status_from(e);
         }
@@ -279,7 +280,7 @@ int enqueue_blocked_split(const float *A, int64_t batch, int m, int n, int64_t a
     const unsigned unused = (((1u << kSplitParts) - 1u) & ~((1u << parts) - 1u));
     for (int p = 0; p < parts; ++p) {
         const int64_t lo = batch * p / parts, hi = batch * (p + 1) / parts;
-        const int r = enqueue_blocked(A + lo * a_bstride, hi - lo, m, n, a_bstride, a_rstride, a_cstride,
+        const int r = enqueue_blocked(A + lo * a_bstride, hi - lo, batch, m, n, a_bstride, a_rstride, a_cstride,
                                       H + lo * mn, tau + lo * n, Sws + lo * fqr::s_block_floats(m, n),
                                       status, p, (1u << p) | (p == 0 ? unused : 0u), tc,
                                       p == 0 ? st : sp.side[p - 1], nullptr);
@@ -331,7 +332,7 @@ int run_geqrf(const float *A, int64_t batch, int64_t m, int64_t n, int64_t a_bst
                                      tc, st);
     // an own status word (host entry, one per chunk) or both words of the
     // workspace's status block
-    return enqueue_blocked(A, batch, mi, ni, a_bstride, a_rstride, a_cstride, H, tau, Sws, status, 0,
+    return enqueue_blocked(A, batch, batch, mi, ni, a_bstride, a_rstride, a_cstride, H, tau, Sws, status, 0,
                            status_word ? 1u : (1u << kSplitParts) - 1u, tc, st, tm);
 }
 

@@ -99,10 +99,12 @@ constexpr size_t ws_total_bytes(int64_t batch, int64_t m, int64_t n) { return kW
 cudaError_t launch_inblock(float *H, const float *tau, float *S64, int64_t s_stride, int64_t batch, int m,
                            int n, int k, bool gram, cudaStream_t st);
 // Rank-64 tensor-core trailing update of columns k+64 .. n-1 with the 64
-// reflectors of columns k .. k+63 (S64 complete) and tau.
+// reflectors of columns k .. k+63 (S64 complete) and tau.  batch_all: the
+// whole call's batch (the launch covers `batch` of them), which the static
+// plan uses to decide whether two CTAs share each tile's rows.
 cudaError_t launch_trailing64_tc(const TrailingMaps &maps, float *H, const float *S64, int64_t s_stride,
-                                 const float *tau, int *status, int64_t batch, int m, int n, int k,
-                                 cudaStream_t st);
+                                 const float *tau, int *status, int64_t batch, int64_t batch_all, int m, int n,
+                                 int k, cudaStream_t st);
 
 // Validates and enqueues one batched geqrf (the body of fqr_geqrf_f32);
 // returns an FQR_* status.

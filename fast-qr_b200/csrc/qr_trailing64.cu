@@ -20,11 +20,14 @@
 //            in 32 x 32 pieces, warp by warp
 // The reference has no tensor-core path; this is the same compact-WY update
 // as oracle/geqr2.c's blocked restatement with two panels per block.
+#include <cooperative_groups.h>
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
 #include "internal.h"
 #include "tc.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace fqr {
 
@@ -71,6 +74,8 @@ constexpr int kCQCols = 32;
 constexpr int kCQBytes = kRCC * kCQCols * 4;  // 16 KB: 4 warps x 4 KB
 static_assert(kOffCQ + 2 * kCQBytes <= kOffTau, "phase-C buffers overlap tau");
 static_assert(kR * kR * 4 <= 2 * kCQBytes, "S does not fit the -P area");
+constexpr int kMaxSplit = 2;  // W exchange slots (32 KB each) below the S area
+static_assert(kMaxSplit * kR * kThreads * 4 <= kOffCQ, "W exchange slots overlap S");
 static_assert(kStageBytes % 1024 == 0 && kCBytes % 1024 == 0 && kVBytes % 1024 == 0, "1024-byte atoms");
 
 constexpr uint32_t kIdescA = tc::idesc_tf32(128, 128, 0, 0);  // A = C_hi^T (smem), B = [V | V_lo]
@@ -148,11 +153,13 @@ __device__ __forceinline__ void store_v64(const float (&e)[kR], uint32_t lane_q)
 
 }  // namespace
 
+template <bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 2)
 trailing64_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmV,
                   const __grid_constant__ CUtensorMap tmCQ, const float *__restrict__ H,
                   const float *__restrict__ S64, int64_t s_stride, const float *__restrict__ tau,
-                  int *__restrict__ status, int ld, int n, int k, int64_t b0, int flags)
+                  int *__restrict__ status, int ld, int n, int k, int64_t b0, int flags, int nsplit,
+                  int rows_per)
 {
     const bool early_trigger = flags & kFlagEarlyTrigger;
     extern __shared__ unsigned char smem_raw[];
@@ -161,9 +168,17 @@ trailing64_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constant
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int64_t mat = b0 + blockIdx.y;
     const int c_begin = k + kR;
-    const int c0 = c_begin + blockIdx.x * kTN;  // first column of the tile
+    // nsplit > 1: a cluster of nsplit CTAs (consecutive in x) shares one tile,
+    // CTA `half` taking block rows [half * rows_per, (half + 1) * rows_per)
+    // (rows_per a multiple of 128); their W parts are summed through
+    // distributed shared memory before phase B
+    const int half = SPLIT ? (int)(blockIdx.x % nsplit) : 0;
+    const int c0 = c_begin + (int)(SPLIT ? blockIdx.x / nsplit : blockIdx.x) * kTN;  // first column of the tile
     const int nct = min(kTN, n - c0);
     const int m = ld - k;  // rows k .. ld-1
+    const int r_begin = half * rows_per;  // this CTA's first block row
+    const int mloc = SPLIT ? max(0, min(m, r_begin + rows_per) - r_begin) : m;
+    const int g0 = r_begin / kRC;                             // its first 32-row chunk
     const float *Hm = H + mat * (int64_t)ld * n;
     const float *Vbase = Hm + (int64_t)k * ld + k;  // V(r, j) at Vbase[j * ld + r]
     const float *Sm = S64 + mat * s_stride;         // S(l, j) at Sm[l * 64 + j]
@@ -174,7 +189,7 @@ trailing64_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constant
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kOffBar + 64);
     float *taus = reinterpret_cast<float *>(smem + kOffTau);
     const uint32_t sbase = tc::smem_addr(smem);
-    const int nchunks = (m + kRC - 1) / kRC;
+    const int nchunks = (mloc + kRC - 1) / kRC;  // this CTA's chunks
 
     if (tid == 0) {
         tc::prefetch_tensormap(&tmC);
@@ -196,8 +211,8 @@ trailing64_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constant
         for (int s = 0; s < kStages && s < nchunks; ++s) {
             unsigned char *st = smem + s * kStageBytes;
             tc::mbar_expect_tx(&full[s], kLoadBytes);
-            tc::tma_load_3d(st, &tmC, k + s * kRC, c0, (int)mat, &full[s]);
-            tc::tma_load_3d(st + kCBytes, &tmV, k + s * kRC, k, (int)mat, &full[s]);
+            tc::tma_load_3d(st, &tmC, k + (g0 + s) * kRC, c0, (int)mat, &full[s]);
+            tc::tma_load_3d(st + kCBytes, &tmV, k + (g0 + s) * kRC, k, (int)mat, &full[s]);
         }
     }
     if (tid < kR) taus[tid] = tau[mat * n + k + tid];
@@ -217,7 +232,7 @@ trailing64_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constant
         unsigned char *st = smem + sidx * kStageBytes;
         const bool landed = tc::mbar_wait(&full[sidx], (uint32_t)(i / kStages) & 1u, kWaitLimit);
         tc::fence_after_sync();
-        split_stage64(st, lane_q + kALo + 32u * b, i, tid);
+        split_stage64(st, lane_q + kALo + 32u * b, g0 + i, tid);
         tc::tmem_st_wait();
         tc::fence_proxy_async_smem();
         tc::fence_before_sync();
@@ -251,8 +266,8 @@ trailing64_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constant
                 unsigned char *fr = smem + ((i - 1) % kStages) * kStageBytes;
                 uint64_t *fb = &full[(i - 1) % kStages];
                 tc::mbar_expect_tx(fb, kLoadBytes);
-                tc::tma_load_3d(fr, &tmC, k + nx * kRC, c0, (int)mat, fb);
-                tc::tma_load_3d(fr + kCBytes, &tmV, k + nx * kRC, k, (int)mat, fb);
+                tc::tma_load_3d(fr, &tmC, k + (g0 + nx) * kRC, c0, (int)mat, fb);
+                tc::tma_load_3d(fr + kCBytes, &tmV, k + (g0 + nx) * kRC, k, (int)mat, fb);
             }
             if (done && nx < nchunks) ++loads;
         }
@@ -266,13 +281,74 @@ trailing64_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constant
     }
     if (early_trigger) pdl_trigger();
 
-    const int ncc = (m + kRCC - 1) / kRCC;
+    const int ncc = (mloc + kRCC - 1) / kRCC;  // this CTA's 128-row chunks
     const int nqc = (nct + kCQCols - 1) / kCQCols;
     float e[kR];  // V rows of the next phase-C chunk
 
     // ---- phase B: Y = T^T W, thread = tile column c ------------------------
+    // W^T row c = hi*hi + hi*lo + lo*hi parts (three 64-column slices)
+    float a[kR];
+    auto read_w = [&]() {
+        tc::fence_after_sync();
+        float t[32];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            tc::tmem_ld_32x32(lane_q + kDA + 32u * h, t);  // hi * V_hi
+            tc::tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) a[32 * h + j] = t[j];
+            tc::tmem_ld_32x32(lane_q + kDA + 64u + 32u * h, t);  // hi * V_lo
+            tc::tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) a[32 * h + j] += t[j];
+            tc::tmem_ld_32x32(lane_q + kDA2 + 32u * h, t);  // lo * V_hi
+            tc::tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) a[32 * h + j] += t[j];
+        }
+    };
+    if constexpr (SPLIT) {
+        if (ok) read_w();
+        // the cluster's W parts, summed in rank order in every CTA: slot
+        // `rank` of each CTA's exchange area ([j / 4][thread][4] floats, 32 KB
+        // per rank, in the phase-A ring).  Every CTA passes both cluster
+        // barriers, whatever its `ok` (a CTA whose wait gave up has set the
+        // status word; the call's results are then reported invalid)
+        cg::cluster_group cl = cg::this_cluster();
+        float *xb = reinterpret_cast<float *>(smem);
+        cl.sync();  // every CTA of the cluster is done with its ring
+        if (ok) {
+            for (int rk = 0; rk < nsplit; ++rk) {
+                float *dst = cl.map_shared_rank(xb, rk) + half * (kR * kThreads);
+#pragma unroll
+                for (int j4 = 0; j4 < kR / 4; ++j4)
+                    *reinterpret_cast<float4 *>(dst + (j4 * kThreads + tid) * 4) =
+                        make_float4(a[4 * j4], a[4 * j4 + 1], a[4 * j4 + 2], a[4 * j4 + 3]);
+            }
+        }
+        cl.sync();
+        if (ok) {
+#pragma unroll
+            for (int j4 = 0; j4 < kR / 4; ++j4) {
+                float4 sum = *reinterpret_cast<const float4 *>(xb + (j4 * kThreads + tid) * 4);
+                for (int rk = 1; rk < nsplit; ++rk) {
+                    const float4 v = *reinterpret_cast<const float4 *>(xb + rk * (kR * kThreads) +
+                                                                        (j4 * kThreads + tid) * 4);
+                    sum.x += v.x;
+                    sum.y += v.y;
+                    sum.z += v.z;
+                    sum.w += v.w;
+                }
+                a[4 * j4] = sum.x;
+                a[4 * j4 + 1] = sum.y;
+                a[4 * j4 + 2] = sum.z;
+                a[4 * j4 + 3] = sum.w;
+            }
+        }
+    }
     // S (16 KB) into the ring's third stage, which phase C uses only later
-    // (for its -P pieces): all phase-A copies and MMAs are complete
+    // (for its -P pieces; the exchange slots are below it): all phase-A
+    // copies and MMAs are complete
     float *Ss = reinterpret_cast<float *>(smem + kOffCQ);  // S(l, j) at l * 64 + j
     if (ok) {
 #pragma unroll
@@ -283,27 +359,8 @@ trailing64_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constant
     }
     __syncthreads();
     if (ok) {
-        tc::fence_after_sync();
+        if constexpr (!SPLIT) read_w();
         const int c = tid;
-        float a[kR];
-        {
-            float t[32];
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                tc::tmem_ld_32x32(lane_q + kDA + 32u * h, t);  // hi * V_hi
-                tc::tmem_ld_wait();
-#pragma unroll
-                for (int j = 0; j < 32; ++j) a[32 * h + j] = t[j];
-                tc::tmem_ld_32x32(lane_q + kDA + 64u + 32u * h, t);  // hi * V_lo
-                tc::tmem_ld_wait();
-#pragma unroll
-                for (int j = 0; j < 32; ++j) a[32 * h + j] += t[j];
-                tc::tmem_ld_32x32(lane_q + kDA2 + 32u * h, t);  // lo * V_hi
-                tc::tmem_ld_wait();
-#pragma unroll
-                for (int j = 0; j < 32; ++j) a[32 * h + j] += t[j];
-            }
-        }
         // y_l = tau_l a_l, then a_j -= S(l, j) y_l for j > l (S row l read
         // as float4 from the 16-byte group holding l + 1; every thread reads
         // the same address)
@@ -338,7 +395,7 @@ trailing64_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constant
     __syncthreads();
     if (ok) {
         // V of phase-C chunk 0 into this warp's TMEM lanes (W there is read)
-        load_v64(Vbase, ld, 0, m, tid, e);
+        load_v64(Vbase, ld, r_begin, m, tid, e);
         store_v64(e, lane_q);
         tc::tmem_st_wait();
         tc::fence_proxy_async_smem();
@@ -370,7 +427,7 @@ trailing64_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constant
     if (ok) {
         ok = !__syncthreads_or(false);  // Y and V(0) staged
         issue_c();
-        if (ncc > 1) load_v64(Vbase, ld, kRCC, m, tid, e);
+        if (ncc > 1) load_v64(Vbase, ld, r_begin + kRCC, m, tid, e);
     }
     for (int j = 0; j < ncc && ok; ++j) {
         const bool done = tc::mbar_wait(cbar, c_waited & 1u, kWaitLimit);
@@ -408,11 +465,12 @@ trailing64_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constant
             tc::fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
-                tc::tma_reduce_add_3d(&tmCQ, k + kRCC * j + 32 * warp, c0 + kCQCols * q, (int)mat, cs);
+                tc::tma_reduce_add_3d(&tmCQ, k + r_begin + kRCC * j + 32 * warp, c0 + kCQCols * q, (int)mat,
+                                      cs);
                 tc::bulk_commit_group();
             }
         }
-        if (j + 2 < ncc) load_v64(Vbase, ld, (j + 2) * kRCC, m, tid, e);
+        if (j + 2 < ncc) load_v64(Vbase, ld, r_begin + (j + 2) * kRCC, m, tid, e);
     }
     if (!early_trigger) pdl_trigger();
     if (lane == 0) tc::bulk_wait_group<0>();  // each warp's reduces complete before shared memory goes away
@@ -438,20 +496,44 @@ trailing64_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constant
     }
 }
 
+// Static plan by (the call's batch, n, k): when all tiles of the call fit
+// one CTA per SM (few large matrices, or the late blocks of a larger batch),
+// each tile's rows are split over a cluster of two CTAs, halving the per-CTA
+// chain of row chunks at the cost of a W exchange and a second copy of
+// phase B; otherwise one CTA per tile.  Measured at n = 4096: one matrix
+// -19%, two -18%, 16 -0.6%.
+static int trailing64_split(int64_t batch_all, int64_t tiles, int rows)
+{
+    return (rows >= 256 && tiles * batch_all <= 148) ? kMaxSplit : 1;
+}
+
 cudaError_t launch_trailing64_tc(const TrailingMaps &maps, float *H, const float *S64, int64_t s_stride,
-                                 const float *tau, int *status, int64_t batch, int m, int n, int k,
-                                 cudaStream_t st)
+                                 const float *tau, int *status, int64_t batch, int64_t batch_all, int m, int n,
+                                 int k, cudaStream_t st)
 {
     if (n - k - kR <= 0) return cudaSuccess;
     if (m - k < kR) return cudaErrorInvalidValue;
-    cudaError_t e = cudaFuncSetAttribute(trailing64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    cudaError_t e = cudaFuncSetAttribute(trailing64_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kSmem);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(trailing64_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
     if (e != cudaSuccess) return e;
     const unsigned tiles = (unsigned)((n - k - kR + kTN - 1) / kTN);
+    const int rows = m - k;
+    const int nsplit = trailing64_split(batch_all, tiles, rows);
+    // rows per cluster rank: a multiple of the 128-row phase-C chunk
+    const int rows_per = nsplit > 1 ? (rows + nsplit * kRCC - 1) / (nsplit * kRCC) * kRCC : rows;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)nsplit;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
     for (int64_t b0 = 0; b0 < batch; b0 += 65535) {
         const int64_t nb = (batch - b0) < 65535 ? (batch - b0) : 65535;
-        e = launch_dependent(trailing64_kernel, dim3(tiles, (unsigned)nb), dim3(kThreads), kSmem, st, nullptr, 0,
-                             maps.c, maps.v64, maps.cq, H, S64, s_stride, tau, status, m, n, k, b0,
-                             kFlagEarlyTrigger);
+        e = launch_dependent(nsplit > 1 ? trailing64_kernel<true> : trailing64_kernel<false>,
+                             dim3(tiles * nsplit, (unsigned)nb), dim3(kThreads), kSmem, st,
+                             nsplit > 1 ? attr : nullptr, nsplit > 1 ? 1 : 0, maps.c, maps.v64, maps.cq, H, S64,
+                             s_stride, tau, status, m, n, k, b0, kFlagEarlyTrigger, nsplit, rows_per);
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;
