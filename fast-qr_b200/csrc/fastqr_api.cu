@@ -227,7 +227,8 @@ int enqueue_blocked(const float *A, int64_t batch, int64_t batch_all, int m, int
         if (!step(FQR_STAGE_PANEL, [&] { return fqr::launch_panel(H, tau, s32, batch, m, n, k, st); }))
             return status_from(e);
         if (k + fqr::kPanel < n && !step(FQR_STAGE_TRAILING, [&] {
-                return tc ? fqr::launch_trailing_tc(maps, H, Sws, s_stride, tau, status, batch, m, n, k, st)
+                return tc ? fqr::launch_trailing_tc(maps, H, Sws, s_stride, tau, status, batch, batch_all, m, n, k,
+                                                    st)
                           : fqr::launch_trailing(H, Sws, s_stride, tau, batch, m, n, k, st);
             }))
             return status_from(e);

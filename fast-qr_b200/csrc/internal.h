@@ -59,8 +59,12 @@ cudaError_t prepare_apply_maps(const float *H, int m, int hcols, float *C, int64
 cudaError_t launch_apply_tc(const TrailingMaps &maps, const float *H, const float *Sws, int64_t s_stride,
                             const float *tau, int *status, int64_t batch, int m, int hcols, int k,
                             int c_begin, int c_end, bool apply_t, cudaStream_t st);
+// batch_all: the whole call's batch (the launch covers `batch` of them); the
+// static plan splits each tile's rows over two CTAs when the call's tiles
+// fit one CTA per SM.
 cudaError_t launch_trailing_tc(const TrailingMaps &maps, float *H, const float *Sws, int64_t s_stride,
-                               const float *tau, int *status, int64_t batch, int m, int n, int k, cudaStream_t st);
+                               const float *tau, int *status, int64_t batch, int64_t batch_all, int m, int n, int k,
+                               cudaStream_t st);
 
 // Rank-64 blocking (two 32-column panels per trailing update) for m x n
 // matrices with n >= 2048 and m <= 4096 (m % 4 == 0, the tensor-core

@@ -30,6 +30,7 @@
 // 128-byte swizzle K-major layout as well.
 // The reference's trailing_update_kernel (submissions/candidate.py:2507-2716)
 // is SIMT FP32 with T recomputed in every CTA; nothing here follows it.
+#include <cooperative_groups.h>
 #include <mutex>
 
 #include <cudaTypedefs.h>
@@ -37,6 +38,8 @@
 #include "common.cuh"
 #include "internal.h"
 #include "tc.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace fqr {
 
@@ -92,6 +95,7 @@ constexpr int kOffCQ = 65536;
 constexpr int kCQCols = 32;
 constexpr int kCQBytes = kRCC * kCQCols * 4;  // 16 KB
 static_assert(kOffCQ + 2 * kCQBytes <= kOffT, "phase-C buffers overlap S");
+static_assert(2 * 32 * kThreads * 4 <= 2 * kCQBytes, "two W exchange slots exceed the -P area");
 static_assert(kStages * kStageBytes <= kOffT, "phase-A ring overlaps S");
 static_assert(kStageBytes % 1024 == 0 && kCBytes % 1024 == 0, "swizzle atoms need 1024-byte alignment");
 
@@ -181,13 +185,13 @@ __device__ __forceinline__ void store_v_rows(const float (&e)[kPanel], unsigned 
 
 }  // namespace
 
-template <bool ApplyT>
+template <bool ApplyT, bool SPLIT = false>
 __global__ void __launch_bounds__(kThreads, 2)
 trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmV,
                    const __grid_constant__ CUtensorMap tmCQ, const float *__restrict__ H,
                    const float *__restrict__ Sws, int64_t s_stride, const float *__restrict__ tau,
                    int *__restrict__ status, int ld, int hcols, int k, int c_begin, int c_end, int64_t b0,
-                   int flags)
+                   int flags, int nsplit, int rows_per)
 {
     const bool early_trigger = flags & kFlagEarlyTrigger;
     extern __shared__ unsigned char smem_raw[];
@@ -198,11 +202,19 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
     // tile = kTN columns of [c_begin, c_end) of the target matrix; phase A
     // reads the whole kTN-wide box (its extra columns are never used), phase C
     // touches only the tile's own columns
-    const int c0 = c_begin + blockIdx.x * kTN;  // first column of the tile
+    // SPLIT: a cluster of nsplit CTAs (consecutive in x) shares one tile, CTA
+    // `half` taking block rows [half * rows_per, (half + 1) * rows_per)
+    // (rows_per a multiple of 128); their W parts are summed through
+    // distributed shared memory before phase B
+    const int half = SPLIT ? (int)(blockIdx.x % nsplit) : 0;
+    const int c0 = c_begin + (int)(SPLIT ? blockIdx.x / nsplit : blockIdx.x) * kTN;  // first column of the tile
     const int nct = min(kTN, c_end - c0);
     // H: ld rows x hcols columns per matrix (column-major); the reflectors of
     // columns k .. k+31 (fewer at the end), tau hcols values per matrix
     const int m = ld - k;                          // rows k .. ld-1
+    const int r_begin = half * rows_per;           // this CTA's first block row
+    const int mloc = SPLIT ? max(0, min(m, r_begin + rows_per) - r_begin) : m;
+    const int g0 = r_begin / kRC;                  // its first 32-row chunk
     const int wv = min(kPanel, min(m, hcols - k));  // reflectors of the panel
     const float *Hm = H + mat * (int64_t)ld * hcols;
     const float *Vbase = Hm + (int64_t)k * ld + k;  // V(r, j) at Vbase[j * ld + r]
@@ -214,7 +226,7 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
     float *Ts = reinterpret_cast<float *>(smem + kOffT);    // S(l, c) at c * 32 + l
     float *taus = reinterpret_cast<float *>(smem + kOffTau);
     const uint32_t sbase = tc::smem_addr(smem);
-    const int nchunks = (m + kRC - 1) / kRC;
+    const int nchunks = (mloc + kRC - 1) / kRC;  // this CTA's chunks
 
     // thread 0: barriers, then the first kStages chunks (and S with chunk 0)
     // start streaming at once
@@ -238,8 +250,8 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
         for (int s = 0; s < kStages && s < nchunks; ++s) {
             unsigned char *st = smem + s * kStageBytes;
             tc::mbar_expect_tx(&full[s], kLoadBytes + (s == 0 ? 4096u : 0u));
-            tc::tma_load_3d(st, &tmC, k + s * kRC, c0, (int)mat, &full[s]);
-            tc::tma_load_3d(st + kCBytes, &tmV, k + s * kRC, k, (int)mat, &full[s]);
+            tc::tma_load_3d(st, &tmC, k + (g0 + s) * kRC, c0, (int)mat, &full[s]);
+            tc::tma_load_3d(st + kCBytes, &tmV, k + (g0 + s) * kRC, k, (int)mat, &full[s]);
             if (s == 0) tc::bulk_load(smem + kOffT, Sws + mat * s_stride, 4096u, &full[0]);
         }
     }
@@ -268,7 +280,7 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
         // ends at the barrier below
         const uint32_t lane_q = tmem + ((uint32_t)(32 * warp) << 16);
         tc::fence_after_sync();  // after the wait for chunk i-2's MMAs, which read this A buffer
-        split_stage(st, lane_q + kAHi + 64u * b, lane_q + kALo + 64u * b, i == 0, tid);
+        split_stage(st, lane_q + kAHi + 64u * b, lane_q + kALo + 64u * b, g0 + i == 0, tid);
         tc::tmem_st_wait();
         tc::fence_proxy_async_smem();
         tc::fence_before_sync();
@@ -301,8 +313,8 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
                 unsigned char *fr = smem + ((i - 1) % kStages) * kStageBytes;
                 uint64_t *fb = &full[(i - 1) % kStages];
                 tc::mbar_expect_tx(fb, kLoadBytes);
-                tc::tma_load_3d(fr, &tmC, k + nx * kRC, c0, (int)mat, fb);
-                tc::tma_load_3d(fr + kCBytes, &tmV, k + nx * kRC, k, (int)mat, fb);
+                tc::tma_load_3d(fr, &tmC, k + (g0 + nx) * kRC, c0, (int)mat, fb);
+                tc::tma_load_3d(fr + kCBytes, &tmV, k + (g0 + nx) * kRC, k, (int)mat, fb);
             }
             if (done && nx < nchunks) ++loads;
         }
@@ -324,19 +336,18 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
     if (early_trigger) pdl_trigger();
 
     // ---- phase C set-up
-    const int ncc = (m + kRCC - 1) / kRCC;
+    const int ncc = (mloc + kRCC - 1) / kRCC;  // this CTA's 128-row chunks
     // quarters per chunk that hold tile columns: a tile narrower than kTN (the
     // end of [c_begin, c_end)) must not touch the quarters beyond c_end
     const int nqc = (nct + kCQCols - 1) / kCQCols;
     float e[kPanel];  // V rows of the next phase-C chunk
-    if (ok) load_v_rows(Vbase, ld, 0, m, wv, tid, e);
+    if (ok) load_v_rows(Vbase, ld, r_begin, m, wv, tid, e);
 
     // ---- phase B: Y = T^T W, thread = tile column c ------------------------
-    if (ok) {
-        tc::fence_after_sync();
-        // W^T row c = hi*hi + hi*lo + lo*hi parts (three 32-column slices)
-        float w[32], y[32];
-        const uint32_t wrow = tmem + ((uint32_t)(32 * warp) << 16);
+    // W^T row c = hi*hi + hi*lo + lo*hi parts (three 32-column slices)
+    const uint32_t wrow = tmem + ((uint32_t)(32 * warp) << 16);
+    auto read_w = [&](float (&w)[32]) {
+        float y[32];
         tc::tmem_ld_32x32(wrow + kDA, w);
         tc::tmem_ld_wait();
         tc::tmem_ld_32x32(wrow + kDA + 32, y);
@@ -347,6 +358,59 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
         tc::tmem_ld_wait();
 #pragma unroll
         for (int j = 0; j < 32; ++j) w[j] += y[j];
+    };
+    float wsum[32];
+    if constexpr (SPLIT) {
+        // the cluster's W parts, summed in rank order in every CTA: slot
+        // `rank` of each CTA's -P staging area ([j / 4][thread][4] floats,
+        // 16 KB per rank; phase C uses the area only later).  Every CTA
+        // passes both cluster barriers, whatever its `ok` (a CTA whose wait
+        // gave up has set the status word; the results are reported invalid)
+        if (ok) {
+            tc::fence_after_sync();
+            read_w(wsum);
+        }
+        cg::cluster_group cl = cg::this_cluster();
+        float *xb = reinterpret_cast<float *>(smem + kOffCQ);
+        cl.sync();  // every CTA of the cluster is done with its phase-A ring
+        if (ok) {
+            for (int rk = 0; rk < nsplit; ++rk) {
+                float *dst = cl.map_shared_rank(xb, rk) + half * (32 * kThreads);
+#pragma unroll
+                for (int j4 = 0; j4 < 8; ++j4)
+                    *reinterpret_cast<float4 *>(dst + (j4 * kThreads + tid) * 4) =
+                        make_float4(wsum[4 * j4], wsum[4 * j4 + 1], wsum[4 * j4 + 2], wsum[4 * j4 + 3]);
+            }
+        }
+        cl.sync();
+        if (ok) {
+#pragma unroll
+            for (int j4 = 0; j4 < 8; ++j4) {
+                float4 t = *reinterpret_cast<const float4 *>(xb + (j4 * kThreads + tid) * 4);
+                for (int rk = 1; rk < nsplit; ++rk) {
+                    const float4 v =
+                        *reinterpret_cast<const float4 *>(xb + rk * (32 * kThreads) + (j4 * kThreads + tid) * 4);
+                    t.x += v.x;
+                    t.y += v.y;
+                    t.z += v.z;
+                    t.w += v.w;
+                }
+                wsum[4 * j4] = t.x;
+                wsum[4 * j4 + 1] = t.y;
+                wsum[4 * j4 + 2] = t.z;
+                wsum[4 * j4 + 3] = t.w;
+            }
+        }
+    }
+    if (ok) {
+        tc::fence_after_sync();
+        float w[32], y[32];
+        if constexpr (SPLIT) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) w[j] = wsum[j];
+        } else {
+            read_w(w);
+        }
         const int c = 32 * warp + lane;
         // T = D (I + S D)^-1 with D = diag(tau), S = strict_upper(V^T V).
         if constexpr (ApplyT) {
@@ -415,7 +479,7 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
     if (ok) {
         ok = !__syncthreads_or(false);  // Y and V(0) staged
         issue_c(0);
-        if (ncc > 1) load_v_rows(Vbase, ld, kRCC, m, wv, tid, e);
+        if (ncc > 1) load_v_rows(Vbase, ld, r_begin + kRCC, m, wv, tid, e);
     }
     for (int j = 0; j < ncc && ok; ++j) {
         const bool done = tc::mbar_wait(cbar, c_waited & 1u, kWaitLimit);
@@ -427,7 +491,7 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
         ok = !__syncthreads_or(!done);
         if (!ok) break;
         if (j + 1 < ncc) issue_c(j + 1);
-        if (j + 2 < ncc) load_v_rows(Vbase, ld, (j + 2) * kRCC, m, wv, tid, e);
+        if (j + 2 < ncc) load_v_rows(Vbase, ld, r_begin + (j + 2) * kRCC, m, wv, tid, e);
         tc::fence_after_sync();
         const uint32_t pc = tmem + ((uint32_t)(32 * warp) << 16) + ((j & 1) ? kDP1 : kDP0);
         // epilogue: thread = row j * 128 + tid of the tile.  -P goes to a
@@ -453,7 +517,8 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
             tc::fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
-                tc::tma_reduce_add_3d(&tmCQ, k + kRCC * j + 32 * warp, c0 + kCQCols * q, (int)mat, cs);
+                tc::tma_reduce_add_3d(&tmCQ, k + r_begin + kRCC * j + 32 * warp, c0 + kCQCols * q, (int)mat,
+                                      cs);
                 tc::bulk_commit_group();
             }
         }
@@ -561,17 +626,43 @@ cudaError_t launch_apply_tc(const TrailingMaps &maps, const float *H, const floa
         const int64_t nb = (batch - b0) < 65535 ? (batch - b0) : 65535;
         dim3 grid(tiles, (unsigned)nb);
         e = launch_dependent(kern, grid, dim3(kThreads), kSmem, st, nullptr, 0, maps.c, maps.v, maps.cq, H, Sws,
-                             s_stride, tau, status, ld, hcols, k, c_begin, c_end, b0, trailing_flags(ld));
+                             s_stride, tau, status, ld, hcols, k, c_begin, c_end, b0, trailing_flags(ld), 1,
+                             ld - k);
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;
 }
 
 cudaError_t launch_trailing_tc(const TrailingMaps &maps, float *H, const float *Sws, int64_t s_stride,
-                               const float *tau, int *status, int64_t batch, int m, int n, int k, cudaStream_t st)
+                               const float *tau, int *status, int64_t batch, int64_t batch_all, int m, int n, int k,
+                               cudaStream_t st)
 {
     if (n - k - kPanel <= 0) return cudaSuccess;
-    return launch_apply_tc(maps, H, Sws, s_stride, tau, status, batch, m, n, k, k + kPanel, n, true, st);
+    // Static plan by (the call's batch, n, k), as for the rank-64 update:
+    // when all tiles of the call fit one CTA per SM, two CTAs (a cluster)
+    // share each tile's rows
+    const int64_t tiles = (n - k - kPanel + kTN - 1) / kTN;
+    const int rows = m - k;
+    if (!(rows >= 256 && tiles * batch_all <= 148))
+        return launch_apply_tc(maps, H, Sws, s_stride, tau, status, batch, m, n, k, k + kPanel, n, true, st);
+    constexpr int kSplit = 2;
+    auto kern = trailing_tc_kernel<true, true>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    if (e != cudaSuccess) return e;
+    const int rows_per = (rows + kSplit * kRCC - 1) / (kSplit * kRCC) * kRCC;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kSplit;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    for (int64_t b0 = 0; b0 < batch; b0 += 65535) {
+        const int64_t nb = (batch - b0) < 65535 ? (batch - b0) : 65535;
+        e = launch_dependent(kern, dim3((unsigned)(tiles * kSplit), (unsigned)nb), dim3(kThreads), kSmem, st, attr,
+                             1, maps.c, maps.v, maps.cq, H, Sws, s_stride, tau, status, m, n, k, k + kPanel, n, b0,
+                             trailing_flags(m), kSplit, rows_per);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
 }
 
 }  // namespace fqr
