@@ -55,7 +55,7 @@ def test_last_tau_is_zero_and_zero_columns_give_zero_tau(golden):
     assert np.all(data["n96_rankdef.tau64"][:, 72:] == 0.0)
 
 
-@pytest.mark.parametrize("nb", [1, 3, 5, 8, 32])
+@pytest.mark.parametrize("nb", [1, 3, 5, 8, 32, 64])
 def test_blocked_compact_wy_equals_unblocked(golden, nb):
     """The blocked compact-WY restatement (the GPU's algorithm) equals xGEQR2."""
     data, meta = golden
@@ -179,3 +179,43 @@ def test_rect_oracle_matches_numpy_lapack(b, m, n):
     if m == n:
         h2, t2 = oracle.geqrf_f64(a)
         assert np.array_equal(h2, h) and np.array_equal(t2, t)
+
+
+def test_rank64_block_update_algebra():
+    """The rank-64 plan's algebra restated in float64. With S =
+    strict_upper(V^T V) assembled from the two panels' S11, S22 and the Gram
+    block S12 = V1^T V2, the update C - V Y with (I + D S^T) Y = D V^T C
+    (forward substitution, D = diag(tau)) equals applying the 64 reflectors
+    one by one; the in-block step (the first panel's 32 reflectors, S11) does
+    likewise; and S12 needs only the rows below the first panel, the Gram
+    step's row range (V2 is zero above them)."""
+    rng = np.random.default_rng(3)
+    m = 200
+    a = rng.standard_normal((1, m, 64)).astype(np.float32)
+    h, tau = oracle.geqrf_rect_f64(a)
+    h, tau = h[0], tau[0]
+    v = np.tril(h, -1)
+    v[np.arange(64), np.arange(64)] = 1.0
+    c = rng.standard_normal((m, 20))
+
+    def one_by_one(vs, taus, x):
+        x = x.copy()
+        for j in range(vs.shape[1]):
+            x -= taus[j] * np.outer(vs[:, j], vs[:, j] @ x)
+        return x
+
+    def block_update(vs, taus, s, x):
+        w = vs.T @ x
+        y = np.zeros_like(w)
+        for l in range(len(taus)):
+            y[l] = taus[l] * (w[l] - s[:l, l] @ y[:l])
+        return x - vs @ y
+
+    v1, v2 = v[:, :32], v[:, 32:]
+    s11, s22 = np.triu(v1.T @ v1, 1), np.triu(v2.T @ v2, 1)
+    s12 = v1[32:].T @ v2[32:]
+    assert np.allclose(s12, v1.T @ v2, rtol=0, atol=1e-12)
+    s = np.zeros((64, 64))
+    s[:32, :32], s[32:, 32:], s[:32, 32:] = s11, s22, s12
+    assert np.allclose(block_update(v, tau, s, c), one_by_one(v, tau, c), rtol=0, atol=1e-11)
+    assert np.allclose(block_update(v1, tau[:32], s11, c), one_by_one(v1, tau[:32], c), rtol=0, atol=1e-11)
