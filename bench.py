@@ -67,10 +67,12 @@ def panel_bytes(n: int, b: int = 32) -> float:
     return sum(8.0 * b * (n - k) + 4.0 * b + 4.0 * b * b for k in range(0, n, b))
 
 
-def plan_blocks(n: int) -> tuple:
+def plan_blocks(n: int, m: int | None = None) -> tuple:
     """(rank-64 blocks, columns left for rank-32 steps) of the library's static
-    plan for square n x n (rank-64 blocks for 2048 <= n <= 4096, n % 4 == 0)."""
-    outer = 2048 <= n <= 4096 and n % 4 == 0
+    plan for m x n (m = n by default): rank-64 blocks for n >= 2048 with
+    m <= 4096 and m % 4 == 0."""
+    m = n if m is None else m
+    outer = n >= 2048 and m <= 4096 and m % 4 == 0
     blocks = n // 64 if outer else 0
     return blocks, n - 64 * blocks
 
@@ -104,9 +106,9 @@ def inblock_bytes(n: int) -> float:
     return tot
 
 
-def stage_launches(n: int) -> dict:
+def stage_launches(n: int, m: int | None = None) -> dict:
     """Launches per kernel class of one blocked factorisation (one stream)."""
-    blocks, rest = plan_blocks(n)
+    blocks, rest = plan_blocks(n, m)
     rp = -(-rest // 32)
     full = blocks if rest > 0 else max(blocks - 1, 0)
     return {"small": 1, "copy_in": 1, "panel": 2 * blocks + rp, "inblock": blocks + full,
@@ -628,9 +630,11 @@ def run_rect_op(args) -> int:
         cpu = {"value": ac.shape[0] / per, "unit": "matrices/s", "cores": threads, "kind": "reference",
                "sample": f"torch.geqrf (host LAPACK) on {ac.shape[0]} of the {batch} {m}x{cols} blocks, "
                          f"median of {len(times)} reps"}
-    # blocked path: per half of the batch a copy-in, the panels and all but the last panel's trailing update
-    panels = -(-cols // 32)
-    launches = (2 if batch >= 2 else 1) * (1 + panels + (panels - 1))
+    # blocked path: per part of the batch (two, four for 2048+ columns) a
+    # copy-in and the plan's panels, in-block steps and trailing updates
+    st = stage_launches(cols, m)
+    parts = min(batch, 4 if cols >= 2048 else 2)
+    launches = parts * (st["copy_in"] + st["panel"] + st["inblock"] + st["trailing"])
     line = {
         "metric": f"matrices/s ({args.config} rect {m}x{cols})", "value": mps, "unit": "matrices/s",
         "n_gpus": 1, "steps": steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,

@@ -46,3 +46,12 @@ def test_strong_scaling_config_block(bench):
     strong = bench._config_block(argparse.Namespace(config="C5", strong=True), 8)
     assert (weak["batch_per_gpu"], weak["global_batch"]) == (16, 128)
     assert (strong["batch_per_gpu"], strong["global_batch"]) == (2, 16)
+
+
+@pytest.mark.parametrize("m,n", [(512, 384), (2304, 2080), (8192, 2048)])
+def test_rect_stage_launches_follow_the_plan(bench, m, n):
+    # tall blocks take rank-64 blocks only for n >= 2048 with m <= 4096
+    counts = bench.stage_launches(n, m)
+    assert (counts["inblock"] > 0) == (n >= 2048 and m <= 4096)
+    blocks, rest = bench.plan_blocks(n, m)
+    assert 64 * blocks + rest == n
