@@ -77,3 +77,16 @@ def test_two_rank_gloo_sharding_and_timing():
         assert t == 1.5  # max over ranks
         assert ok
         assert not bad  # one failing rank fails all
+
+
+def test_weak_and_strong_rank_inputs():
+    """bench.py's two modes: weak (every rank a full batch of a batch x world
+    global batch, drawn from seed + rank) and strong (contiguous shards of one
+    batch)."""
+    from fastqr.shard import rank_inputs
+    a, first = rank_inputs("C2", seed=3, world=4, rank=2, device="cpu", batch=3, weak=True)
+    assert (a.shape[0], first) == (3, 6)
+    a, first = rank_inputs("C2", seed=3, world=4, rank=2, device="cpu", batch=10, weak=False)
+    assert (a.shape[0], first) == (3, 6)  # shards of 3, 3, 3, 1
+    a, first = rank_inputs("C2", seed=3, world=4, rank=3, device="cpu", batch=10, weak=False)
+    assert (a.shape[0], first) == (1, 9)
