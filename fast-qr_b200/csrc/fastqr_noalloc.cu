@@ -23,7 +23,7 @@
 // Limits: on the blocked path (n > 64) at most FQR_NOALLOC_MAX_BATCH matrices
 // per call; larger batches are rejected with FQR_ENOALLOC_LIMIT before any
 // work is enqueued.  All calls on one device share the array, and each call
-// leaves its last T factors in it: two calls whose kernels may overlap on the
+// leaves its last S blocks in it: two calls whose kernels may overlap on the
 // GPU (different streams without ordering between them) race on the array and
 // give wrong results.  Issue these calls on one stream, or order them.
 #include <cuda_runtime.h>
@@ -43,23 +43,57 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 
 constexpr int kMaxDevices = 64;
 std::mutex g_mu;
-void *g_scratch_addr[kMaxDevices] = {};
+struct ScratchAddr {
+    void *ctx = nullptr;  // the CUDA context the address belongs to
+    void *addr = nullptr;
+};
+ScratchAddr g_scratch[kMaxDevices];
 
-// Device address of g_noalloc_scratch on the current device (looked up once).
+// The current CUDA context (cuCtxGetCurrent through the runtime's driver
+// entry point query; the library links no libcuda).  A module's __device__
+// arrays belong to a context: after cudaDeviceReset, or under another
+// context on the same device, the symbol's address may differ.
+typedef int (*CtxGetCurrentFn)(void **);
+void *current_context()
+{
+    static std::once_flag once;
+    static CtxGetCurrentFn fn = nullptr;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<CtxGetCurrentFn>(p);
+        else
+            cudaGetLastError();
+    });
+    void *ctx = nullptr;
+    if (fn && fn(&ctx) != 0) ctx = nullptr;
+    return ctx;
+}
+
+// Device address of g_noalloc_scratch in the current context, looked up
+// once per (device, context).
 int scratch_for_current_device(void **out)
 {
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return FQR_ECUDA;
+    // (no context current yet: the symbol lookup below creates the primary
+    // context, and the next call caches the address under it)
+    void *ctx = current_context();
     std::lock_guard<std::mutex> lock(g_mu);
-    if (!g_scratch_addr[dev]) {
+    ScratchAddr &s = g_scratch[dev];
+    if (!s.addr || s.ctx != ctx || !ctx) {
         void *p = nullptr;
         if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) {
             cudaGetLastError();  // clear the error this call left behind
+            s.addr = nullptr;
             return FQR_ECUDA;
         }
-        g_scratch_addr[dev] = p;
+        s.addr = p;
+        s.ctx = ctx;
     }
-    *out = g_scratch_addr[dev];
+    *out = s.addr;
     return FQR_OK;
 }
 
@@ -84,4 +118,18 @@ extern "C" int fqr_geqrf_f32_noalloc(const float *A, int64_t batch, int64_t n, i
     }
     return fqr::geqrf_enqueue(A, batch, n, a_bstride, a_rstride, a_cstride, H, tau, scratch,
                               need > 0 ? kNoAllocScratchBytes : 0, (cudaStream_t)stream);
+}
+
+extern "C" int fqr_noalloc_check_status(void *stream)
+{
+    // the status block is the first 256 bytes of the static array: one int
+    // word per part of a batch split over streams, all cleared by every call
+    int v[4] = {};
+    cudaStream_t st = (cudaStream_t)stream;
+    if (cudaMemcpyFromSymbolAsync(v, g_noalloc_scratch, sizeof(v), 0, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+        return FQR_ECUDA;
+    if (cudaStreamSynchronize(st) != cudaSuccess) return FQR_ECUDA;
+    int any = 0;
+    for (int i = 0; i < 4; ++i) any |= v[i];
+    return any ? FQR_ETIMEOUT : FQR_OK;
 }

@@ -12,8 +12,10 @@
 // The reference runs the same two steps as panel_factor_kernel /
 // trailing_update_kernel (submissions/candidate.py:2404-2505, :2507-2716), but
 // recomputes T redundantly in every trailing CTA and applies reflectors one
-// by one by default; here the panel kernel forms T once and the trailing
-// update is a blocked product.
+// by one by default; here the panel kernel stores S = V^T V (a by-product of
+// its reductions) and tau, T is never formed (the trailing update solves
+// (I + D S^T) Y = D W per column, D = diag(tau)), and the trailing update is
+// a blocked product.
 //
 // Working storage is H itself, column-major (column j of matrix b is
 // contiguous): the copy-in kernel transposes the row-major input once.

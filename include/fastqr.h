@@ -6,12 +6,17 @@
  * cudaStream_t passed as void*.  All calls are asynchronous on `stream`: they
  * validate arguments on the host, enqueue kernels and return.  The library
  * allocates no device memory on this path; scratch space is caller-owned
- * (see fqr_workspace_bytes).  Calls are reentrant: the only global state is
+ * (see fqr_workspace_bytes).  Calls are thread-safe: the only global state is
  * per device -- up to three internal streams and their events, created on
  * first use, on which the blocked path runs parts of a batch of two or more
  * matrices (two parts, four for n >= 2048; always ordered with the caller's
  * stream: they wait for the caller's prior work and the caller's stream waits
- * for them).
+ * for them).  Because every such call on a device forks onto the same side
+ * streams, two callers on independent streams are serialised through them:
+ * each caller's stream picks up an ordering dependency on the other's
+ * blocked-path work.  Results stay correct; concurrency between such calls
+ * is lost.  The single-launch paths (n <= 64, and the one-launch mid-size
+ * kernel where the plan takes it) use only the caller's stream.
  *
  * Output layout (the contract of torch.geqrf, and of the reference's
  * `custom_kernel(data) -> (H, tau)`):
@@ -102,19 +107,34 @@ int fqr_launch_count(int64_t batch, int64_t n);
  * allocate device memory: no workspace argument, and the library allocates
  * nothing.  Scratch comes from a fixed 16 MiB __device__ array inside the
  * library, present on every GPU that loads it until the process exits.
- * Its address is looked up on the first call made on each device (that device
- * current); make that first call before any stream capture.
+ * Its address is looked up on the first call made in each CUDA context (that
+ * device current) and again whenever the current context changes (e.g. after
+ * cudaDeviceReset).  The first call with batch >= 2 on the split blocked path
+ * of a device also creates that device's side streams and events (see the top
+ * of this file).  Make the first call on each device before any stream
+ * capture.
  * n > 64 allows at most FQR_NOALLOC_MAX_BATCH matrices per call, else
  * FQR_ENOALLOC_LIMIT is returned and nothing is enqueued; n <= 64 needs no
  * scratch and has no batch limit.  Every call on a device shares the array:
  * calls that may run concurrently on the GPU (unordered streams) race and give
  * wrong results, so issue them on one stream or order them.
- * No counterpart in the reference, whose entry points always allocate their
- * outputs and workspace through PyTorch (submissions/candidate.py:3682-3851).
+ * A bounded device-side wait that gave up is recorded in the array's status
+ * block; fqr_noalloc_check_status reports it.
+ * No counterpart in the reference: its entry points always allocate their
+ * outputs and workspace through PyTorch.
  */
 int fqr_geqrf_f32_noalloc(const float *A, int64_t batch, int64_t n, int64_t a_bstride,
                           int64_t a_rstride, int64_t a_cstride, float *H, float *tau,
                           void *stream);
+
+/* fqr_check_status for fqr_geqrf_f32_noalloc, which has no caller workspace:
+ * synchronizes `stream`, then returns FQR_ETIMEOUT if the last no-alloc call
+ * with n > 64 on the current device hit a bounded device-side wait that gave
+ * up, else FQR_OK (also when no such call has been made on this device; calls
+ * with n <= 64 use no scratch and leave the status block as it was).  Call it
+ * on the stream of that call, before the next no-alloc call clears the
+ * status block.  No counterpart in the reference. */
+int fqr_noalloc_check_status(void *stream);
 
 /*
  * Batched QR of matrices in HOST memory: the same result as fqr_geqrf_f32,
@@ -201,7 +221,7 @@ int fqr_check_status(const void *workspace, size_t workspace_bytes, int64_t batc
 enum {
     FQR_STAGE_SMALL = 0,     /* warp-per-matrix kernel (n <= 64) */
     FQR_STAGE_COPY_IN = 1,   /* row-major A -> column-major H */
-    FQR_STAGE_PANEL = 2,     /* panel factorisation + T factor */
+    FQR_STAGE_PANEL = 2,     /* panel factorisation + S = V^T V and tau */
     FQR_STAGE_TRAILING = 3,  /* trailing update C -= V T^T V^T C */
     FQR_STAGE_INBLOCK = 4,   /* rank-64 blocks: next-panel update and cross Gram block */
     FQR_NUM_STAGES = 5

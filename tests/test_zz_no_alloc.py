@@ -31,7 +31,8 @@ def _noalloc(lib, a, h, t):
                                      t.data_ptr(), stream)
 
 
-@pytest.mark.parametrize("batch,n", [(64, 32), (16, 256), (5, 100), (3, 512), (2, 1100)])
+# (2, 2048) runs the rank-64 plan, whose 64 x 64 S blocks set the scratch size
+@pytest.mark.parametrize("batch,n", [(64, 32), (16, 256), (5, 100), (3, 512), (2, 1100), (2, 2048)])
 def test_noalloc_matches_the_allocating_entry_point(batch, n):
     assert torch.cuda.is_available()
     dev = torch.device("cuda:0")
@@ -42,6 +43,8 @@ def test_noalloc_matches_the_allocating_entry_point(batch, n):
         h, t = fastqr.empty_outputs(batch, n, dev)
         rc = _noalloc(lib, a, h, t)
         assert rc == 0, fastqr.FastQRError(rc)
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        assert lib.fqr_noalloc_check_status(stream) == 0
         torch.cuda.synchronize()
         he, te = column_errors(h, t, h_ref, t_ref)
         assert float(he.max()) <= COL_TOL and float(te.max()) <= COL_TOL, (call, float(he.max()))
@@ -54,6 +57,14 @@ def test_noalloc_rejects_batches_beyond_its_scratch():
     a = torch.zeros(MAX_BATCH + 1, n, n, device=dev)
     h, t = fastqr.empty_outputs(MAX_BATCH + 1, n, dev)
     assert _noalloc(lib, a, h, t) == FQR_ENOALLOC_LIMIT
+    # the largest accepted batch at n > 64
+    a = inputs.generate_input(MAX_BATCH, n, 1, 77, device=dev)
+    h, t = fastqr.empty_outputs(MAX_BATCH, n, dev)
+    assert _noalloc(lib, a, h, t) == 0
+    h_ref, t_ref = fastqr.geqrf(a)
+    torch.cuda.synchronize()
+    he, te = column_errors(h, t, h_ref, t_ref)
+    assert float(he.max()) <= COL_TOL and float(te.max()) <= COL_TOL
     # the small path needs no scratch and has no such limit
     a32 = inputs.generate_input(MAX_BATCH + 1, 32, 0, 5, device=dev)
     h32, t32 = fastqr.empty_outputs(MAX_BATCH + 1, 32, dev)
