@@ -106,13 +106,20 @@ def inblock_bytes(n: int) -> float:
     return tot
 
 
+def mid_plan(n: int, m: int | None = None) -> bool:
+    """The library's one-launch mid-size plan: square 128 <= n <= 256, n % 4 == 0."""
+    return (m is None or m == n) and 128 <= n <= 256 and n % 4 == 0
+
+
 def stage_launches(n: int, m: int | None = None) -> dict:
-    """Launches per kernel class of one blocked factorisation (one stream)."""
+    """Launches per kernel class of one factorisation (one stream)."""
+    if mid_plan(n, m):
+        return {"small": 0, "copy_in": 0, "panel": 0, "inblock": 0, "trailing": 0, "mid": 1}
     blocks, rest = plan_blocks(n, m)
     rp = -(-rest // 32)
     full = blocks if rest > 0 else max(blocks - 1, 0)
     return {"small": 1, "copy_in": 1, "panel": 2 * blocks + rp, "inblock": blocks + full,
-            "trailing": full + max(rp - 1, 0)}
+            "trailing": full + max(rp - 1, 0), "mid": 0}
 
 
 class ClockSampler:
@@ -396,11 +403,15 @@ def kernel_roofline(cfg_name, a, h, tau, ws, flush, steps, dev) -> dict:
     per_step = stage_launches(n)[dom]
     base = {"kernel": dom, "stage_ms_per_step": per_step_ms, "stage_share": share,
             "traffic": traffic, "launches_per_step": per_step, "peak_source": pk["source"]}
-    if dom in ("small", "copy_in", "panel", "inblock"):
+    if dom in ("small", "copy_in", "panel", "inblock", "mid"):
         # the panel does O(m b^2) flops on O(m b) data: it is framed by HBM
-        # bytes, and its limiter is the column-by-column dependency chain
+        # bytes, and its limiter is the column-by-column dependency chain.
+        # The one-launch mid-size kernel does the whole factorisation: read A,
+        # write H and tau (n / 6 flop per byte, below the tensor pipe's ridge,
+        # so HBM is its roof)
         alg = batch * {"small": bytes_per_matrix(n), "copy_in": 8.0 * n * n,
-                       "panel": panel_bytes(n), "inblock": inblock_bytes(n)}[dom]
+                       "panel": panel_bytes(n), "inblock": inblock_bytes(n),
+                       "mid": bytes_per_matrix(n)}[dom]
         ach = alg / t / 1e9
         base.update({"bound": "hbm", "achieved": ach, "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": ach / pk["hbm_gbs"], "alg_bytes_per_step": alg,

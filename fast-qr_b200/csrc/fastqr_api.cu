@@ -2,6 +2,9 @@
 //
 // Static dispatch on (batch, m, n) only:
 //   m == n <= 64 : one warp per matrix, registers (qr_small.cu)
+//   m == n in [128, 256], n % 4 == 0 (and an aligned H) : one launch, one CTA
+//                  per matrix running its whole blocked factorisation
+//                  (qr_mid.cu)
 //   otherwise    : blocked compact-WY: copy-in, then per 32-column panel a
 //                  panel kernel and a trailing-update kernel (qr_blocked.cu);
 //                  for n >= 2048 (and m <= 4096) per 64 columns two panels,
@@ -14,6 +17,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "../../include/fastqr.h"
@@ -38,6 +42,12 @@ bool use_tc(int64_t n) { return fqr::trailing_tc_supported((int)n); }
 
 bool small_path(int64_t n) { return n <= 64; }
 
+// the one-launch mid-size path for square n (with a 16-byte aligned H,
+// which every torch / cudaMalloc allocation is)
+bool mid_path(int64_t n) { return fqr::mid_supported(n, n, nullptr); }
+
+std::atomic<int> g_debug_flags{0};
+
 int status_from(cudaError_t e)
 {
     if (e == cudaSuccess) return FQR_OK;
@@ -50,6 +60,11 @@ int status_from(cudaError_t e)
 extern "C" {
 
 int fqr_version(void) { return 100; }
+
+int fqr_debug_force_timeout(int enable)
+{
+    return g_debug_flags.exchange(enable ? fqr::kMidFlagForceTimeout : 0) != 0;
+}
 
 const char *fqr_status_string(int status)
 {
@@ -80,7 +95,7 @@ int fqr_launch_count(int64_t batch, int64_t n)
 {
     if (batch <= 0 || n <= 0) return 0;
     if (n > FQR_MAX_N) return -1;
-    if (small_path(n)) return 1;
+    if (small_path(n) || mid_path(n)) return 1;
     const bool outer = use_tc(n) && fqr::use_outer64(n, n);
     // copy-in + per panel (panel + trailing), the last panel has no trailing;
     // the rank-64 plan has per 64-column block two panels, the in-block
@@ -116,6 +131,11 @@ int fqr_plan_describe(int64_t batch, int64_t n, char *buf, size_t len)
     if (small_path(n)) {
         snprintf(buf, len, "small: warp-per-matrix registers, n<=%d, %lld warps, 1 launch",
                  n <= 32 ? 32 : 64, (long long)batch);
+    } else if (mid_path(n)) {
+        snprintf(buf, len,
+                 "mid: one CTA per matrix (%lld CTAs, 2 per SM), panel %d cols in registers + tcgen05 3xTF32 "
+                 "rank-%d update per panel, 1 launch",
+                 (long long)batch, fqr::kPanel, fqr::kPanel);
     } else {
         const fqr::PanelShape s = fqr::panel_shape((int)n);
         const bool outer = use_tc(n) && fqr::use_outer64(n, n);
@@ -327,6 +347,15 @@ int run_geqrf(const float *A, int64_t batch, int64_t m, int64_t n, int64_t a_bst
     // the status block first, then the S blocks
     float *Sws = (float *)((unsigned char *)workspace + kWsAlign);
     int *status = status_word ? status_word : (int *)workspace;
+    if (m == n && fqr::mid_supported(m, n, H)) {
+        // one launch; an own status word (host entry, one per chunk) or the
+        // whole status block of the workspace
+        if (tm) tm->begin(FQR_STAGE_MID);
+        cudaError_t e = fqr::launch_mid(A, batch, ni, a_bstride, a_rstride, a_cstride, H, tau, status,
+                                        status_word ? 1 : kSplitParts, g_debug_flags.load(), st);
+        if (tm) tm->end();
+        return status_from(e);
+    }
     const bool tc = use_tc(m) && ((uintptr_t)H % 16) == 0;
     if (split && !tm && batch >= 2)
         return enqueue_blocked_split(A, batch, mi, ni, a_bstride, a_rstride, a_cstride, H, tau, Sws, status,

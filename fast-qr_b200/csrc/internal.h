@@ -110,6 +110,20 @@ cudaError_t launch_trailing64_tc(const TrailingMaps &maps, float *H, const float
                                  const float *tau, int *status, int64_t batch, int64_t batch_all, int m, int n,
                                  int k, cudaStream_t st);
 
+// Mid-size square QR in one launch (qr_mid.cu): one CTA per matrix runs
+// the copy-in and every panel and trailing update of its matrix.  Taken for
+// 128 <= n <= kMidMaxN with n % 4 == 0 and a 16-byte aligned H (the
+// tensor-core update's conditions).  The launch first clears status_words
+// status words at `status`; a bounded wait that gave up sets the first.
+// flags: kMidFlagForceTimeout makes the first trailing update of every
+// matrix wait on a barrier that nothing completes (2 ms limit), so the
+// failure path runs without any fault (a test hook).
+constexpr int kMidMaxN = 256;
+constexpr int kMidFlagForceTimeout = 1;
+bool mid_supported(int64_t m, int64_t n, const void *H);
+cudaError_t launch_mid(const float *A, int64_t batch, int n, int64_t bs, int64_t rs, int64_t cs, float *H,
+                       float *tau, int *status, int status_words, int flags, cudaStream_t st);
+
 // Validates and enqueues one batched geqrf (the body of fqr_geqrf_f32);
 // returns an FQR_* status.
 int geqrf_enqueue(const float *A, int64_t batch, int64_t n, int64_t a_bstride, int64_t a_rstride,

@@ -217,6 +217,18 @@ int fqr_geqrf_rect_f32(const float *A, int64_t batch, int64_t m, int64_t n, int6
  */
 int fqr_check_status(const void *workspace, size_t workspace_bytes, int64_t batch, void *stream);
 
+/*
+ * Test hook for the failure path.  enable != 0: every later fqr_geqrf_f32 (and
+ * noalloc / host / profile) call that takes the one-launch mid-size kernel
+ * makes the first tensor-core wait of each matrix on a barrier that nothing
+ * completes, with a 2 ms limit, so that the bounded-wait failure path runs
+ * (copies and MMAs in flight drain, FQR_ETIMEOUT is recorded for
+ * fqr_check_status) without any GPU fault.  enable == 0 restores normal
+ * operation.  Process-wide; returns the previous setting.  No counterpart in
+ * the reference, whose kernels have no device-side waits.
+ */
+int fqr_debug_force_timeout(int enable);
+
 /* Kernel classes timed by fqr_geqrf_f32_profile. */
 enum {
     FQR_STAGE_SMALL = 0,     /* warp-per-matrix kernel (n <= 64) */
@@ -224,7 +236,8 @@ enum {
     FQR_STAGE_PANEL = 2,     /* panel factorisation + S = V^T V and tau */
     FQR_STAGE_TRAILING = 3,  /* trailing update C -= V T^T V^T C */
     FQR_STAGE_INBLOCK = 4,   /* rank-64 blocks: next-panel update and cross Gram block */
-    FQR_NUM_STAGES = 5
+    FQR_STAGE_MID = 5,       /* one-launch mid-size kernel (whole factorisation) */
+    FQR_NUM_STAGES = 6
 };
 
 /*

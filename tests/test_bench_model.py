@@ -25,7 +25,8 @@ def bench():
 def test_stage_launches_match_the_library(bench, n):
     # one matrix: a single part, so every launch of the plan runs once
     counts = bench.stage_launches(n)
-    total = counts["copy_in"] + counts["panel"] + counts["inblock"] + counts["trailing"]
+    total = counts["copy_in"] + counts["panel"] + counts["inblock"] + counts["trailing"] + counts["mid"]
+    assert (counts["mid"] == 1) == fastqr.plan(1, n).startswith("mid")
     assert total == fastqr.launch_count(1, n), (n, counts)
     assert ("rank 64" in fastqr.plan(1, n)) == (counts["inblock"] > 0)
 
