@@ -1,5 +1,5 @@
 // Mid-size batched QR (128 <= n <= 256, n % 4 == 0): the whole
-// factorisation of one matrix in ONE launch, one CTA (4 warps, two CTAs per
+// factorisation of one matrix in ONE launch, one CTA (8 warps, two CTAs per
 // SM) per matrix.  The blocked chain (copy-in, then per 32-column panel a
 // panel launch and a trailing-update launch) costs 16 dependent launches at
 // n = 256, each waiting for the slowest matrix of the batch; here every
@@ -20,19 +20,20 @@
 // (oracle_geqrf_blocked_f64) with T never formed: the panel keeps
 // S = strict_upper(V^T V) and tau, and the update solves (I + D S^T) Y = D W.
 //
-// Panel, column-owner layout: warp w owns panel columns w, w+4, ..., w+28
-// (slot q = column w + 4q); lane l holds rows k + 32i + l of them (row block
-// i).  Per column c, one CTA barrier:
+// Panel, column-owner layout: warp w owns panel columns w, w+8, w+16, w+24
+// (slot q = column w + 8q); lane l holds rows k + 32i + l of them (row block
+// i; only the panel's own row blocks are held: the column loop is compiled
+// once per row-block count).  Per column c, one CTA barrier:
 //   * the owner of column c has published its current values (the unscaled
 //     tail x and the pivot alpha) to shared memory before the barrier;
 //   * every warp reads x, forms sigma = x^T x and the unscaled dots
-//     d_q = x^T a_q of its own 8 columns (a reduce-scatter over the lanes and
+//     d_q = x^T a_q of its own 4 columns (a reduce-scatter over the lanes and
 //     a broadcast back; no cross-warp reduction), and the reflector from
 //     (alpha, sigma) -- the same inputs and the same reduction order in every
 //     warp, so the same bits everywhere;
 //   * w_q = a_q(c) + scale * d_q (v^T a_q), the rank-1 update of its active
 //     columns, S(q, c) = w_q for its finished columns q < c;
-//   * the owner of column c+1 publishes it as soon as it is updated.
+//   * the owner of column c+1 updates and publishes it first.
 // Out-of-envelope columns take LAPACK order as in the blocked panel
 // (common.cuh): sigma in double, then w = v^T a with the scaled v.
 #include <cudaTypedefs.h>
@@ -45,11 +46,13 @@ namespace fqr {
 
 namespace {
 
-constexpr int kThreads = 128;
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
 constexpr int kTN = 128;     // trailing columns per tile
 constexpr int kRC = 32;      // rows per phase-A chunk (MMA K = 4 x 8; one 128-byte swizzle row)
 constexpr int kRCC = 128;    // rows per phase-C chunk (MMA M)
 constexpr int kStages = 4;   // phase-A ring
+constexpr int kMaxRB = 8;    // 32-row blocks of the tallest panel (n <= 256)
 constexpr uint32_t kTmemCols = 256;
 constexpr uint64_t kWaitLimit = 1000000000ull;  // 1 s of wall time per wait
 
@@ -74,18 +77,19 @@ constexpr int kStageBytes = kLoadBytes + kVBytes;  // 24 KB
 constexpr int kRingBytes = kStages * kStageBytes;  // 96 KB
 // phase C (reuses the ring): Y_hi, Y_lo (the K-major B operand, 128 c x 32 j
 // each), V_hi, V_lo of a 128-row chunk (the K-major A operand, 128 r x 32 j
-// each) and two -P quarters (128 rows x 32 columns, [c][r] per warp slice)
+// each) and one -P piece per warp (32 rows x 32 columns, [c][r], 4 KB)
 constexpr int kOffYhi = 0;
 constexpr int kOffYlo = 16384;
 constexpr int kOffVhi = 32768;
 constexpr int kOffVlo = 49152;
 constexpr int kOffCQ = 65536;
 constexpr int kCQCols = 32;
-constexpr int kCQBytes = kRCC * kCQCols * 4;  // 16 KB
+constexpr int kCQPiece = 32 * kCQCols * 4;  // 4 KB
 // panel (reuses the ring): the published column, double-buffered
 constexpr int kOffX = 0;
-// copy-in (reuses the ring): one 32 x 33 float tile per warp
+// copy-in (reuses the ring): two 32 x 33 float tiles per warp
 constexpr int kOffCopy = 0;
+constexpr int kCopyTile = 32 * 33;
 // live across phases
 constexpr int kOffS = kRingBytes;       // S(l, c) at c * 32 + l (4 KB)
 constexpr int kOffTau = kOffS + 4096;   // tau of the panel (128 B)
@@ -93,7 +97,8 @@ constexpr int kOffBar = kOffTau + 128;  // mbarriers full[4], mma[2], phase C, t
 constexpr int kSmemUsed = kOffBar + 128;
 constexpr int kSmem = kSmemUsed + 1024;  // + alignment slack
 static_assert(2 * (kSmem + 1024) <= 228 * 1024, "two CTAs per SM");
-static_assert(kOffCQ + 2 * kCQBytes <= kRingBytes, "phase-C buffers overlap S");
+static_assert(kOffCQ + kWarps * kCQPiece <= kRingBytes, "phase-C buffers overlap S");
+static_assert(kWarps * 2 * kCopyTile * 4 <= kRingBytes, "copy-in tiles overlap S");
 static_assert(kStageBytes % 1024 == 0 && kCBytes % 1024 == 0, "swizzle atoms need 1024-byte alignment");
 
 constexpr uint32_t kIdescA = tc::idesc_tf32(128, 64, 0, 0);   // A = C_hi^T (smem), B = [V | V_lo]
@@ -105,123 +110,126 @@ constexpr uint32_t kIdescC = tc::idesc_tf32(128, 128, 0, 0);  // A = V (M = rows
 __device__ __forceinline__ void fence_proxy_async_all() { asm volatile("fence.proxy.async;" ::: "memory"); }
 
 // Copy-in: A (element (i, j) at Am[i * rs + j * cs]) -> H column-major, in
-// 32 x 32 tiles, one per warp at a time: lanes read 32 consecutive columns of
-// a row (coalesced for row-major A), the tile is transposed through shared
-// memory, and lanes write 32 consecutive rows of a column.
+// 32 x 32 tiles, two per warp at a time (64 loads in flight per lane): lanes
+// read 32 consecutive columns of a row (coalesced for row-major A), the
+// tiles are transposed through shared memory, and lanes write 32
+// consecutive rows of a column.
 __device__ __forceinline__ void mid_copy_in(const float *__restrict__ Am, int64_t rs, int64_t cs,
-                                            float *__restrict__ Hm, int n, float *tile)
+                                            float *__restrict__ Hm, int n, float *tiles)
 {
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    float *t = tile + w * (32 * 33);
     const int nb = (n + 31) >> 5;
-    for (int b = w; b < nb * nb; b += kThreads / 32) {
-        const int r0 = (b / nb) * 32, c0 = (b % nb) * 32;
-        const int c = c0 + lane;
-        float v[32];
+    for (int b0 = 2 * w; b0 < nb * nb; b0 += 2 * kWarps) {
+        float v[2][32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-            const int r = r0 + i;
-            v[i] = (r < n && c < n) ? __ldg(Am + r * rs + c * cs) : 0.0f;
+        for (int u = 0; u < 2; ++u) {
+            const int b = b0 + u;
+            const int r0 = (b / nb) * 32, c = (b % nb) * 32 + lane;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                const int r = r0 + i;
+                v[u][i] = (b < nb * nb && r < n && c < n) ? __ldg(Am + r * rs + c * cs) : 0.0f;
+            }
         }
 #pragma unroll
-        for (int i = 0; i < 32; ++i) t[lane * 33 + i] = v[i];  // t[col][row]
+        for (int u = 0; u < 2; ++u) {
+            float *t = tiles + (2 * w + u) * kCopyTile;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) t[lane * 33 + i] = v[u][i];  // t[col][row]
+        }
         __syncwarp();
-        const int r = r0 + lane;
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int b = b0 + u;
+            if (b >= nb * nb) break;
+            const float *t = tiles + (2 * w + u) * kCopyTile;
+            const int r = (b / nb) * 32 + lane, c0 = (b % nb) * 32;
 #pragma unroll 8
-        for (int j = 0; j < 32; ++j)
-            if (r < n && c0 + j < n) Hm[(int64_t)(c0 + j) * n + r] = t[j * 33 + lane];
+            for (int j = 0; j < 32; ++j)
+                if (r < n && c0 + j < n) Hm[(int64_t)(c0 + j) * n + r] = t[j * 33 + lane];
+        }
         __syncwarp();
     }
 }
 
-// Reduce-scatter of 8 per-lane values over a warp: returns the warp total of
-// slot lane >> 2 (three halving levels over lane bits 4, 3, 2, then two
-// butterfly levels over bits 1, 0).
-__device__ __forceinline__ float reduce_scatter8(const float (&d)[8], int lane)
+// Reduce-scatter of 4 per-lane values over a warp: returns the warp total of
+// slot lane >> 3 (two halving levels over lane bits 4, 3, then three
+// butterfly levels over bits 2, 1, 0).
+__device__ __forceinline__ float reduce_scatter4(const float (&d)[4], int lane)
 {
-    const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
-    float e[4], f[2];
-#pragma unroll
-    for (int t = 0; t < 4; ++t) {
-        const float send = b4 ? d[t] : d[t + 4];
-        const float keep = b4 ? d[t + 4] : d[t];
-        e[t] = keep + __shfl_xor_sync(kFull, send, 16);
-    }
+    const bool b4 = lane & 16, b3 = lane & 8;
+    float e[2];
 #pragma unroll
     for (int t = 0; t < 2; ++t) {
-        const float send = b3 ? e[t] : e[t + 2];
-        const float keep = b3 ? e[t + 2] : e[t];
-        f[t] = keep + __shfl_xor_sync(kFull, send, 8);
+        const float send = b4 ? d[t] : d[t + 2];
+        const float keep = b4 ? d[t + 2] : d[t];
+        e[t] = keep + __shfl_xor_sync(kFull, send, 16);
     }
-    const float send = b2 ? f[0] : f[1];
-    const float keep = b2 ? f[1] : f[0];
-    float g = keep + __shfl_xor_sync(kFull, send, 4);
+    const float send = b3 ? e[0] : e[1];
+    const float keep = b3 ? e[1] : e[0];
+    float g = keep + __shfl_xor_sync(kFull, send, 8);
+    g += __shfl_xor_sync(kFull, g, 4);
     g += __shfl_xor_sync(kFull, g, 2);
     g += __shfl_xor_sync(kFull, g, 1);
     return g;
 }
 
 // Panel factorisation of columns k .. k+wp-1 (wp = min(32, n - k)) over rows
-// k .. n-1 of one matrix, column-owner layout (file comment).  RB: row blocks
-// of the largest panel (n <= 32 * RB).  Leaves the factored columns in H, tau
-// in global memory, and S(l, c) = v_l^T v_c (l < c; 0 elsewhere) at
+// k .. n-1 of one matrix, column-owner layout (file comment).  NRB: the
+// panel's 32-row blocks, ceil((n - k) / 32).  Leaves the factored columns in
+// H, tau in global memory, and S(l, c) = v_l^T v_c (l < c; 0 elsewhere) at
 // Ts[c * 32 + l] and tau at taus[] in shared memory for the trailing update.
-template <int RB>
+template <int NRB>
 __device__ __forceinline__ void mid_panel(float *__restrict__ Hm, float *__restrict__ tau_m, int n, int k,
-                                          float *xs, float *Ts, float *taus)
+                                       float *xs, float *Ts, float *taus)
 {
     const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     const int nrow = n - k;            // panel rows
-    const int nrb = (nrow + 31) >> 5;  // row blocks holding them
     const int wp = min(kPanel, nrow);  // reflectors
-    float P[RB][8];
+    constexpr int XB = kMaxRB * 32;    // floats per published-column buffer
+    float P[NRB][4];
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-        const int j = w + 4 * q;
+    for (int q = 0; q < 4; ++q) {
+        const int j = w + 8 * q;
         const float *src = Hm + (int64_t)(k + j) * n + k + lane;
 #pragma unroll
-        for (int i = 0; i < RB; ++i)
-            P[i][q] = (i < nrb && j < wp && 32 * i + lane < nrow) ? __ldcg(src + 32 * i) : 0.0f;
+        for (int i = 0; i < NRB; ++i)
+            P[i][q] = (j < wp && 32 * i + lane < nrow) ? __ldcg(src + 32 * i) : 0.0f;
     }
     for (int t = tid; t < kPanel * kPanel; t += kThreads) Ts[t] = 0.0f;
     if (tid < kPanel) taus[tid] = 0.0f;
     if (w == 0) {
 #pragma unroll
-        for (int i = 0; i < RB; ++i)
-            if (i < nrb) xs[32 * i + lane] = P[i][0];
+        for (int i = 0; i < NRB; ++i) xs[32 * i + lane] = P[i][0];
     }
     __syncthreads();
 
 #pragma unroll 1
     for (int c = 0; c < wp; ++c) {
-        const float *xp = xs + (c & 1) * (RB * 32);
+        const float *xp = xs + (c & 1) * XB;
         // (1) the published column: tail x (rows > k + c) and alpha
-        float x[RB];
+        float x[NRB];
 #pragma unroll
-        for (int i = 0; i < RB; ++i) x[i] = (i < nrb) ? xp[32 * i + lane] : 0.0f;
+        for (int i = 0; i < NRB; ++i) x[i] = xp[32 * i + lane];
         const float alpha = xp[c];
         if (lane <= c) x[0] = 0.0f;
-        // sigma and the unscaled dots of this warp's 8 columns (column c's own
+        // sigma and the unscaled dots of this warp's 4 columns (column c's own
         // slot, finished columns' slots and active ones alike)
-        float s2[2] = {0.0f, 0.0f}, d[8];
+        float s2[2] = {0.0f, 0.0f}, d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-        for (int q = 0; q < 8; ++q) d[q] = 0.0f;
+        for (int i = 0; i < NRB; ++i) {
+            s2[i & 1] = fmaf(x[i], x[i], s2[i & 1]);
 #pragma unroll
-        for (int i = 0; i < RB; ++i) {
-            if (i < nrb) {
-                s2[i & 1] = fmaf(x[i], x[i], s2[i & 1]);
-#pragma unroll
-                for (int q = 0; q < 8; ++q) d[q] = fmaf(x[i], P[i][q], d[q]);
-            }
+            for (int q = 0; q < 4; ++q) d[q] = fmaf(x[i], P[i][q], d[q]);
         }
-        float rc[8];  // the pivot row k + c of this warp's columns
+        float rc[4];  // the pivot row k + c of this warp's columns
 #pragma unroll
-        for (int q = 0; q < 8; ++q) rc[q] = __shfl_sync(kFull, P[0][q], c);
+        for (int q = 0; q < 4; ++q) rc[q] = __shfl_sync(kFull, P[0][q], c);
         const float sg = warp_sum(s2[0] + s2[1]);
-        const float g = reduce_scatter8(d, lane);  // slot lane >> 2, summed over the warp
-        float D[8];
+        const float g = reduce_scatter4(d, lane);  // slot lane >> 3, summed over the warp
+        float D[4];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) D[q] = __shfl_sync(kFull, g, 4 * q);
+        for (int q = 0; q < 4; ++q) D[q] = __shfl_sync(kFull, g, 8 * q);
 
         // (2) the reflector: the same (alpha, sigma) bits in every warp
         const bool fast = reflector_fast_ok(alpha, sg);
@@ -232,76 +240,79 @@ __device__ __forceinline__ void mid_panel(float *__restrict__ Hm, float *__restr
         } else {
             double t = 0.0;
 #pragma unroll
-            for (int i = 0; i < RB; ++i) t = fma((double)x[i], (double)x[i], t);
+            for (int i = 0; i < NRB; ++i) t = fma((double)x[i], (double)x[i], t);
             sd = warp_sum(t);
             r = reflector_from_double(alpha, sd);
         }
         // v over this lane's rows (0 above the pivot, 1 on it)
-        float v[RB];
+        float v[NRB];
+        if (!r.wide) {
 #pragma unroll
-        for (int i = 0; i < RB; ++i) v[i] = reflector_apply(r, x[i]);
+            for (int i = 0; i < NRB; ++i) v[i] = x[i] * r.scale;
+        } else {
+#pragma unroll
+            for (int i = 0; i < NRB; ++i) v[i] = (float)((double)x[i] * r.scale_d);
+        }
         if (lane == c) v[0] = 1.0f;
         // w_q = v^T a_q over rows >= k + c.  Fast: from the unscaled dots, when
         // none of this warp's could have over- or underflowed (|d| < 1e28 keeps
         // scale * d finite: |scale| <= 1e10 inside the envelope); else LAPACK
         // order with the scaled v (per warp: the reflector is the same either way)
-        float wv[8];
+        float wv[4];
         const bool dots_ok =
             fast && !__any_sync(kFull, !(fabsf(g) < 1e28f) || (g != 0.0f && fabsf(g) < kDotTiny));
         if (dots_ok) {
 #pragma unroll
-            for (int q = 0; q < 8; ++q) wv[q] = fmaf(r.scale, D[q], rc[q]);
+            for (int q = 0; q < 4; ++q) wv[q] = fmaf(r.scale, D[q], rc[q]);
         } else if (sd == 0.0) {
             // exactly zero tail: H = I, v = e_c, w = the pivot row
 #pragma unroll
-            for (int q = 0; q < 8; ++q) wv[q] = rc[q];
+            for (int q = 0; q < 4; ++q) wv[q] = rc[q];
         } else {
-            float d2[8];
+            float d2[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-            for (int q = 0; q < 8; ++q) d2[q] = 0.0f;
+            for (int i = 0; i < NRB; ++i)
 #pragma unroll
-            for (int i = 0; i < RB; ++i)
-                if (i < nrb) {
+                for (int q = 0; q < 4; ++q) d2[q] = fmaf(v[i], P[i][q], d2[q]);
+            const float g2 = reduce_scatter4(d2, lane);
 #pragma unroll
-                    for (int q = 0; q < 8; ++q) d2[q] = fmaf(v[i], P[i][q], d2[q]);
-                }
-            const float g2 = reduce_scatter8(d2, lane);
-#pragma unroll
-            for (int q = 0; q < 8; ++q) wv[q] = __shfl_sync(kFull, g2, 4 * q);
+            for (int q = 0; q < 4; ++q) wv[q] = __shfl_sync(kFull, g2, 8 * q);
         }
 
-        // (3) S of the finished columns, tau, and the rank-1 update
+        // (3) the owner of column c + 1 updates and publishes it first
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            if (w + 8 * q == c + 1 && c + 1 < wp) {
+                const float tw = r.tau * wv[q];
+                float *xn = xs + ((c + 1) & 1) * XB;
+#pragma unroll
+                for (int i = 0; i < NRB; ++i) {
+                    P[i][q] = fmaf(-tw, v[i], P[i][q]);
+                    xn[32 * i + lane] = P[i][q];
+                }
+            }
+        }
+        // (4) S of the finished columns, tau, the other updates
         if (lane == 0) {
 #pragma unroll
-            for (int q = 0; q < 8; ++q)
-                if (w + 4 * q < c) Ts[c * kPanel + w + 4 * q] = wv[q];
-            if (w == (c & 3)) taus[c] = r.tau;
+            for (int q = 0; q < 4; ++q)
+                if (w + 8 * q < c) Ts[c * kPanel + w + 8 * q] = wv[q];
+            if (w == (c & 7)) taus[c] = r.tau;
         }
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            const int j = w + 4 * q;
-            if (j > c && j < wp) {
+        for (int q = 0; q < 4; ++q) {
+            const int j = w + 8 * q;
+            if (j > c + 1 && j < wp) {
                 const float tw = r.tau * wv[q];
 #pragma unroll
-                for (int i = 0; i < RB; ++i)
-                    if (i < nrb) P[i][q] = fmaf(-tw, v[i], P[i][q]);
-                if (j == c + 1) {
-                    // (4) the owner of column c + 1 publishes it for the next
-                    // step (inside the slot loop: a separate loop selecting
-                    // slot (c + 1) / 4 made the compiler index P dynamically)
-                    float *xn = xs + ((c + 1) & 1) * (RB * 32);
-#pragma unroll
-                    for (int i = 0; i < RB; ++i)
-                        if (i < nrb) xn[32 * i + lane] = P[i][q];
-                }
+                for (int i = 0; i < NRB; ++i) P[i][q] = fmaf(-tw, v[i], P[i][q]);
             } else if (j == c) {
                 // column c becomes beta on the pivot row and v below it
 #pragma unroll
-                for (int i = 0; i < RB; ++i)
-                    if (i < nrb) {
-                        if (i > 0 || lane > c) P[i][q] = v[i];
-                        else if (lane == c) P[i][q] = r.beta;
-                    }
+                for (int i = 0; i < NRB; ++i) {
+                    if (i > 0 || lane > c) P[i][q] = v[i];
+                    else if (lane == c) P[i][q] = r.beta;
+                }
             }
         }
         __syncthreads();
@@ -309,19 +320,35 @@ __device__ __forceinline__ void mid_panel(float *__restrict__ Hm, float *__restr
 
     // store the factored columns (rows k ..) and tau
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-        const int j = w + 4 * q;
+    for (int q = 0; q < 4; ++q) {
+        const int j = w + 8 * q;
         if (j < wp) {
             float *dst = Hm + (int64_t)(k + j) * n + k + lane;
 #pragma unroll
-            for (int i = 0; i < RB; ++i)
-                if (i < nrb && 32 * i + lane < nrow) dst[32 * i] = P[i][q];
+            for (int i = 0; i < NRB; ++i)
+                if (32 * i + lane < nrow) dst[32 * i] = P[i][q];
         }
     }
     if (tid < wp) tau_m[k + tid] = taus[tid];
     // the trailing update reads these columns by TMA (async proxy)
     fence_proxy_async_all();
     __syncthreads();
+}
+
+// The panel at k, compiled for its row-block count.
+__device__ __forceinline__ void mid_panel_any(float *Hm, float *tau_m, int n, int k, float *xs, float *Ts,
+                                              float *taus)
+{
+    switch ((n - k + 31) >> 5) {
+    case 1: mid_panel<1>(Hm, tau_m, n, k, xs, Ts, taus); break;
+    case 2: mid_panel<2>(Hm, tau_m, n, k, xs, Ts, taus); break;
+    case 3: mid_panel<3>(Hm, tau_m, n, k, xs, Ts, taus); break;
+    case 4: mid_panel<4>(Hm, tau_m, n, k, xs, Ts, taus); break;
+    case 5: mid_panel<5>(Hm, tau_m, n, k, xs, Ts, taus); break;
+    case 6: mid_panel<6>(Hm, tau_m, n, k, xs, Ts, taus); break;
+    case 7: mid_panel<7>(Hm, tau_m, n, k, xs, Ts, taus); break;
+    default: mid_panel<8>(Hm, tau_m, n, k, xs, Ts, taus); break;
+    }
 }
 
 // Barrier use counts, the same in every thread.  The kernel reuses its
@@ -334,66 +361,73 @@ struct MidSync {
     uint32_t cgrp;   // phase-C MMA groups issued so far (all waited for)
 };
 
-// Split of one phase-A stage.  C: thread tid owns trailing column c = tid
-// (operand row tid, 128 swizzled bytes); its lo parts go to its TMEM lane
-// (the hi operand is the raw stage).  V: 16-byte pieces, lo into the slot
-// after V; for the diagonal chunk (panel rows 0 .. 31) V is made unit lower
-// in place (H holds R and beta there).
+// Split of one phase-A stage by all 256 threads.  C: thread t owns trailing
+// column c = t % 128 (operand row c, 128 swizzled bytes) and chunk rows
+// 16 h .. 16 h + 15, h = t / 128 (the 16-byte pieces 4 h .. 4 h + 3); their lo
+// parts go to TMEM lane c, columns 16 h .. of the chunk's lo buffer (the hi
+// operand is the raw stage).  V: one 16-byte piece per thread, lo into the
+// slot after V; for the diagonal chunk (panel rows 0 .. 31) V is made unit
+// lower in place (H holds R and beta there).
 __device__ __forceinline__ void mid_split(unsigned char *st, uint32_t a_lo, bool diag, int tid)
 {
     {
-        float lv[32];
-        const unsigned char *row = st + tid * 128;
+        const int c = tid & 127, h = tid >> 7;
+        float lv[16];
+        const unsigned char *row = st + c * 128;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            const float4 v = *reinterpret_cast<const float4 *>(row + ((q ^ (tid & 7)) << 4));
-            lv[4 * q] = tc::tf32_lo(v.x);
-            lv[4 * q + 1] = tc::tf32_lo(v.y);
-            lv[4 * q + 2] = tc::tf32_lo(v.z);
-            lv[4 * q + 3] = tc::tf32_lo(v.w);
+        for (int u = 0; u < 4; ++u) {
+            const int q = 4 * h + u;
+            const float4 v = *reinterpret_cast<const float4 *>(row + ((q ^ (c & 7)) << 4));
+            lv[4 * u] = tc::tf32_lo(v.x);
+            lv[4 * u + 1] = tc::tf32_lo(v.y);
+            lv[4 * u + 2] = tc::tf32_lo(v.z);
+            lv[4 * u + 3] = tc::tf32_lo(v.w);
         }
-        tc::tmem_st_32x32(a_lo, lv);
+        tc::tmem_st_32x16(a_lo + 16u * h, lv);
     }
+    const int off = kCBytes + tid * 16;  // 256 pieces of 16 bytes: all of V
+    float4 v = *reinterpret_cast<const float4 *>(st + off);
+    if (diag) {
+        // reflector j = operand row (off - kCBytes) / 128; its 16-byte piece
+        // holds panel rows 4 * ((piece ^ j) & 7) .. + 3
+        const int vo = off - kCBytes;
+        const int j = vo >> 7;
+        const int r0 = 4 * ((((vo >> 4) & 7) ^ j) & 7);
+        float e[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-    for (int off = kCBytes + tid * 16; off < kLoadBytes; off += kThreads * 16) {
-        float4 v = *reinterpret_cast<const float4 *>(st + off);
-        if (diag) {
-            // reflector j = operand row (off - kCBytes) / 128; its 16-byte
-            // piece holds panel rows 4 * ((piece ^ j) & 7) .. + 3
-            const int vo = off - kCBytes;
-            const int j = vo >> 7;
-            const int r0 = 4 * ((((vo >> 4) & 7) ^ j) & 7);
-            float e[4] = {v.x, v.y, v.z, v.w};
+        for (int q = 0; q < 4; ++q)
+            if (r0 + q <= j) e[q] = (r0 + q == j) ? 1.0f : 0.0f;
+        v = make_float4(e[0], e[1], e[2], e[3]);
+        *reinterpret_cast<float4 *>(st + off) = v;
+    }
+    *reinterpret_cast<float4 *>(st + kVBytes + off) =
+        make_float4(tc::tf32_lo(v.x), tc::tf32_lo(v.y), tc::tf32_lo(v.z), tc::tf32_lo(v.w));
+}
+
+// Reflectors 16 h .. 16 h + 15 of row r0 + (tid % 128) of the panel's V, into
+// registers: unit lower, zero past the matrix; loads bypass L1 (H was
+// written in this launch).
+__device__ __forceinline__ void mid_load_v(const float *Vbase, int ld, int r0, int rows, int tid, float (&e)[16])
+{
+    const int r = r0 + (tid & 127), h = tid >> 7;
 #pragma unroll
-            for (int q = 0; q < 4; ++q)
-                if (r0 + q <= j) e[q] = (r0 + q == j) ? 1.0f : 0.0f;
-            v = make_float4(e[0], e[1], e[2], e[3]);
-            *reinterpret_cast<float4 *>(st + off) = v;
-        }
-        *reinterpret_cast<float4 *>(st + kVBytes + off) =
-            make_float4(tc::tf32_lo(v.x), tc::tf32_lo(v.y), tc::tf32_lo(v.z), tc::tf32_lo(v.w));
+    for (int u = 0; u < 16; ++u) {
+        const int j = 16 * h + u;
+        e[u] = (r < rows && r > j) ? __ldcg(Vbase + (int64_t)j * ld + r) : (r == j ? 1.0f : 0.0f);
     }
 }
 
-// Row r0 + tid of the panel's V (32 reflectors) into registers, unit lower,
-// zero past the matrix; loads bypass L1 (H was written in this launch).
-__device__ __forceinline__ void mid_load_v(const float *Vbase, int ld, int r0, int rows, int tid, float (&e)[kPanel])
+// ... and into phase C's K-major A operand (M = rows, K = the 32 reflectors)
+// in the 128-byte swizzle layout: row r's 128 bytes at r * 128, its 16-byte
+// piece jq (reflectors 4 jq .. 4 jq + 3) at (jq ^ (r % 8)) * 16
+__device__ __forceinline__ void mid_store_v(const float (&e)[16], unsigned char *hi, unsigned char *lo, int tid)
 {
-    const int r = r0 + tid;
+    const int r = tid & 127, h = tid >> 7;
 #pragma unroll
-    for (int j = 0; j < kPanel; ++j)
-        e[j] = (r < rows && r > j) ? __ldcg(Vbase + (int64_t)j * ld + r) : (r == j ? 1.0f : 0.0f);
-}
-
-// ... and as phase C's K-major A operand (M = rows, K = the 32 reflectors)
-// in the 128-byte swizzle layout: row tid's 128 bytes at tid * 128, its
-// 16-byte piece jq (reflectors 4 jq .. 4 jq + 3) at (jq ^ (tid % 8)) * 16
-__device__ __forceinline__ void mid_store_v(const float (&e)[kPanel], unsigned char *hi, unsigned char *lo, int tid)
-{
-#pragma unroll
-    for (int jq = 0; jq < kPanel / 4; ++jq) {
-        const uint32_t off = (uint32_t)(tid * 128 + ((jq ^ (tid & 7)) << 4));
-        const float4 v = make_float4(e[4 * jq], e[4 * jq + 1], e[4 * jq + 2], e[4 * jq + 3]);
+    for (int u = 0; u < 4; ++u) {
+        const int jq = 4 * h + u;
+        const uint32_t off = (uint32_t)(r * 128 + ((jq ^ (r & 7)) << 4));
+        const float4 v = make_float4(e[4 * u], e[4 * u + 1], e[4 * u + 2], e[4 * u + 3]);
         *reinterpret_cast<float4 *>(hi + off) = v;
         *reinterpret_cast<float4 *>(lo + off) =
             make_float4(tc::tf32_lo(v.x), tc::tf32_lo(v.y), tc::tf32_lo(v.z), tc::tf32_lo(v.w));
@@ -406,12 +440,14 @@ __device__ __forceinline__ void mid_store_v(const float (&e)[kPanel], unsigned c
 //      straight from the stage against B = [V | V_lo] (N = 64), and A = C_lo
 //      (split by the threads into TMEM) against B = V (N = 32), as in the
 //      rank-64 update (qr_trailing64.cu)
-//   B  Y = T^T W per thread (tile column c): y_l = tau_l (w_l - sum_{i<l}
-//      S(i, l) y_i), Y hi / lo to shared memory as the K-major B operand
+//   B  Y = T^T W per thread of the first warpgroup (tile column c):
+//      y_l = tau_l (w_l - sum_{i<l} S(i, l) y_i), Y hi / lo to shared memory
+//      as the K-major B operand
 //   C  P = V Y per 128-row chunk (A = V hi / lo staged in shared memory,
-//      M = 128 rows, N = 128 columns) into two TMEM accumulators in turn,
-//      -P staged in 32-column quarters and TMA reduce-added into H, as in
-//      the rank-32 update (qr_trailing_tc.cu)
+//      M = 128 rows, N = 128 columns) into two TMEM accumulators in turn;
+//      each warp stages -P in 32 x 32 pieces (the two warpgroups take two
+//      column quarters each) that TMA reduce-adds into H, as in the rank-32
+//      update (qr_trailing_tc.cu)
 // Returns false if a bounded wait gave up (after letting the copies and MMAs
 // in flight drain); every exit is CTA-uniform.  force_timeout (a test hook):
 // the first wait of the call is made on a barrier that nothing completes,
@@ -420,15 +456,16 @@ __device__ __forceinline__ bool mid_trailing(const CUtensorMap *tmC, const CUten
                                              const CUtensorMap *tmCQ, const float *Hm, int mat, int n, int k,
                                              unsigned char *smem, uint32_t tmem, MidSync &sy, bool force_timeout)
 {
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, half = tid >> 7;
     const uint32_t sbase = tc::smem_addr(smem);
-    const uint32_t lane_q = tmem + ((uint32_t)(32 * warp) << 16);  // this warp's TMEM lanes
+    const uint32_t lane_q = tmem + ((uint32_t)(32 * (warp & 3)) << 16);  // this warp's TMEM lanes
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + kOffBar);  // [kStages]
     uint64_t *mmab = full + kStages;                                // [2]
     uint64_t *cbar = full + kStages + 2;                            // phase C
     uint64_t *never = full + kStages + 3;                           // the test hook's barrier
     const float *Ts = reinterpret_cast<const float *>(smem + kOffS);
     const float *taus = reinterpret_cast<const float *>(smem + kOffTau);
+    float *piece = reinterpret_cast<float *>(smem + kOffCQ + warp * kCQPiece);  // this warp's -P piece
     const int m = n - k;
     const int nchunks = (m + kRC - 1) / kRC;
     const int ncc = (m + kRCC - 1) / kRCC;
@@ -519,7 +556,10 @@ __device__ __forceinline__ bool mid_trailing(const CUtensorMap *tmC, const CUten
         sy.chunk = g0 + nchunks;
 
         // ---- phase B: Y = T^T W, thread = tile column c ----------------------
-        if (ok) {
+        // (both warpgroups first start loading their halves of V(0))
+        float e[16];
+        if (ok) mid_load_v(Vbase, n, 0, m, tid, e);
+        if (ok && half == 0) {
             tc::fence_after_sync();
             float a[32], t[32];
             tc::tmem_ld_32x32(lane_q + kDA, a);  // hi * V_hi
@@ -532,12 +572,20 @@ __device__ __forceinline__ bool mid_trailing(const CUtensorMap *tmC, const CUten
             tc::tmem_ld_wait();
 #pragma unroll
             for (int j = 0; j < 32; ++j) a[j] += t[j];
-            // y_l = tau_l (w_l - sum_{i<l} S(i, l) y_i); a[i < l] hold y_i
+            // y_l = tau_l (w_l - sum_{i<l} S(i, l) y_i); a[i < l] hold y_i.  S
+            // column l is read four entries at a time (every thread reads the
+            // same address)
 #pragma unroll
             for (int l = 0; l < kPanel; ++l) {
                 float acc = a[l];
 #pragma unroll
-                for (int i = 0; i < l; ++i) acc = fmaf(-Ts[l * kPanel + i], a[i], acc);
+                for (int i4 = 0; i4 < (l + 3) / 4; ++i4) {
+                    const float4 s4 = *reinterpret_cast<const float4 *>(Ts + l * kPanel + 4 * i4);
+                    const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+                    for (int u = 0; u < 4; ++u)
+                        if (4 * i4 + u < l) acc = fmaf(-sv[u], a[4 * i4 + u], acc);
+                }
                 a[l] = taus[l] * acc;
             }
             // Y as the K-major B operand: column c's 32 values at c * 128,
@@ -551,8 +599,8 @@ __device__ __forceinline__ bool mid_trailing(const CUtensorMap *tmC, const CUten
                 *reinterpret_cast<float4 *>(smem + kOffYlo + off) =
                     make_float4(tc::tf32_lo(v.x), tc::tf32_lo(v.y), tc::tf32_lo(v.z), tc::tf32_lo(v.w));
             }
-            float e[kPanel];
-            mid_load_v(Vbase, n, 0, m, tid, e);
+        }
+        if (ok) {
             mid_store_v(e, smem + kOffVhi, smem + kOffVlo, tid);
             tc::fence_proxy_async_smem();
         }
@@ -583,7 +631,6 @@ __device__ __forceinline__ bool mid_trailing(const CUtensorMap *tmC, const CUten
             }
             ++cg_n;
         };
-        float e[kPanel];
         if (ok) {
             ok = !__syncthreads_or(false);  // Y and V(0) staged
             issue_c(0);
@@ -603,24 +650,26 @@ __device__ __forceinline__ bool mid_trailing(const CUtensorMap *tmC, const CUten
             if (j + 2 < ncc) mid_load_v(Vbase, n, (j + 2) * kRCC, m, tid, e);
             tc::fence_after_sync();
             const uint32_t pc = lane_q + ((j & 1) ? kDP1 : kDP0);
-            // epilogue: thread = row 128 j + tid; each warp stages its 32 rows
-            // of a quarter ([c][r], 4 KB) and lane 0 reduce-adds them into C
-            // (rows and columns past the matrix are outside the tensor map)
-            for (int q = 0; q < nqc; ++q) {
+            // epilogue: thread = row 128 j + tid % 128; warpgroup h takes
+            // column quarters 2h and 2h + 1; each warp stages its 32 rows of a
+            // quarter ([c][r], 4 KB) and lane 0 reduce-adds them into C (rows
+            // and columns past the matrix are outside the tensor map)
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int q = 2 * half + u;
+                if (q >= nqc) break;
                 float pv[32];
                 tc::tmem_ld_32x32(pc + kCQCols * q, pv);
                 tc::tmem_ld_wait();
-                const int u = j * nqc + q;
-                float *cs = reinterpret_cast<float *>(smem + kOffCQ + (u & 1) * kCQBytes) + warp * (32 * kCQCols);
-                // the warp's reduce of quarter u-2 (same slice) has read it
-                if (lane == 0) tc::bulk_wait_group_read<1>();
+                // the warp's previous reduce has read its piece
+                if (lane == 0) tc::bulk_wait_group_read<0>();
                 __syncwarp();
 #pragma unroll
-                for (int cc = 0; cc < kCQCols; ++cc) cs[cc * 32 + lane] = -pv[cc];
+                for (int cc = 0; cc < kCQCols; ++cc) piece[cc * 32 + lane] = -pv[cc];
                 tc::fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) {
-                    tc::tma_reduce_add_3d(tmCQ, k + kRCC * j + 32 * warp, c0 + kCQCols * q, mat, cs);
+                    tc::tma_reduce_add_3d(tmCQ, k + kRCC * j + 32 * (warp & 3), c0 + kCQCols * q, mat, piece);
                     tc::bulk_commit_group();
                 }
             }
@@ -657,9 +706,7 @@ __device__ __forceinline__ bool mid_trailing(const CUtensorMap *tmC, const CUten
 }  // namespace
 
 // One CTA per matrix: copy-in, then per 32-column panel the panel and the
-// trailing update, all in this launch.  RB: 32-row blocks of the tallest
-// panel (n <= 32 * RB).
-template <int RB>
+// trailing update, all in this launch.
 __global__ void __launch_bounds__(kThreads, 2)
 mid_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmV,
            const __grid_constant__ CUtensorMap tmCQ, const float *__restrict__ A, int64_t a_bs, int64_t a_rs,
@@ -702,7 +749,7 @@ mid_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUte
     MidSync sy = {0u, 0u};
     bool ok = true;
     for (int k = 0; k < n && ok; k += kPanel) {
-        mid_panel<RB>(Hm, tau + mat * n, n, k, xs, Ts, taus);
+        mid_panel_any(Hm, tau + mat * n, n, k, xs, Ts, taus);
         if (k + kPanel < n)
             ok = mid_trailing(&tmC, &tmV, &tmCQ, Hm, (int)mat, n, k, smem, tmem, sy,
                               (flags & kMidFlagForceTimeout) && k == 0);
@@ -724,18 +771,18 @@ bool mid_supported(int64_t m, int64_t n, const void *H)
 cudaError_t launch_mid(const float *A, int64_t batch, int n, int64_t bs, int64_t rs, int64_t cs, float *H,
                        float *tau, int *status, int status_words, int flags, cudaStream_t st)
 {
+    static_assert(kMidMaxN <= 32 * kMaxRB, "the panel holds at most kMaxRB row blocks");
     if (!mid_supported(n, n, H) || batch > 0x7fffffff) return cudaErrorInvalidValue;
     TrailingMaps maps;
     cudaError_t e = prepare_trailing_tc(H, batch, n, n, &maps);
     if (e != cudaSuccess) return e;
-    auto kern = n <= 128 ? mid_kernel<4> : mid_kernel<8>;
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    e = cudaFuncSetAttribute(mid_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
     if (e != cudaSuccess) return e;
     // the status words of this call start clear (the kernel only sets them)
     e = cudaMemsetAsync(status, 0, (size_t)status_words * sizeof(int), st);
     if (e != cudaSuccess) return e;
-    kern<<<dim3((unsigned)batch), dim3(kThreads), kSmem, st>>>(maps.c, maps.v, maps.cq, A, bs, rs, cs, H, tau,
-                                                               status, n, flags);
+    mid_kernel<<<dim3((unsigned)batch), dim3(kThreads), kSmem, st>>>(maps.c, maps.v, maps.cq, A, bs, rs, cs, H,
+                                                                     tau, status, n, flags);
     return cudaGetLastError();
 }
 
