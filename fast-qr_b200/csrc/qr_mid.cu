@@ -109,30 +109,6 @@ constexpr uint32_t kIdescC = tc::idesc_tf32(128, 128, 0, 0);  // A = V (M = rows
 // state spaces
 __device__ __forceinline__ void fence_proxy_async_all() { asm volatile("fence.proxy.async;" ::: "memory"); }
 
-// Named CTA barriers 1 .. 4 of the panel's column loop (0 is
-// __syncthreads), executed by whole warps: all kThreads threads must arrive
-// (bar.arrive: without waiting) before the waiters (bar.sync) go on.  The ids
-// are immediates, so the kernel reserves barriers 0 .. 4 only.
-__device__ __forceinline__ void named_bar_sync(int id)
-{
-    static_assert(kThreads == 256, "barrier counts below");
-    switch (id) {
-    case 1: asm volatile("bar.sync 1, 256;" ::: "memory"); break;
-    case 2: asm volatile("bar.sync 2, 256;" ::: "memory"); break;
-    case 3: asm volatile("bar.sync 3, 256;" ::: "memory"); break;
-    default: asm volatile("bar.sync 4, 256;" ::: "memory"); break;
-    }
-}
-__device__ __forceinline__ void named_bar_arrive(int id)
-{
-    switch (id) {
-    case 1: asm volatile("bar.arrive 1, 256;" ::: "memory"); break;
-    case 2: asm volatile("bar.arrive 2, 256;" ::: "memory"); break;
-    case 3: asm volatile("bar.arrive 3, 256;" ::: "memory"); break;
-    default: asm volatile("bar.arrive 4, 256;" ::: "memory"); break;
-    }
-}
-
 // Copy-in: A (element (i, j) at Am[i * rs + j * cs]) -> H column-major, in
 // 32 x 32 tiles, two per warp at a time (64 loads in flight per lane): lanes
 // read 32 consecutive columns of a row (coalesced for row-major A), the
@@ -199,16 +175,7 @@ __device__ __forceinline__ float reduce_scatter4(const float (&d)[4], int lane)
 }
 
 // Panel factorisation of columns k .. k+wp-1 (wp = min(32, n - k)) over rows
-// k .. n-1 of one matrix, column-owner layout (file comment).  The column loop
-// has no CTA-wide barrier; two pairs of named barriers order the two
-// published-column buffers (x of column c sits in buffer c & 1):
-//   F(b), ids 1 + b: "buffer b holds the next column": its publisher (the
-//     owner of that column) arrives, every other warp waits;
-//   E(b), ids 3 + b: "every warp has read buffer b": all warps but its next
-//     writer (the owner of column c + 2) arrive after reading column c, and
-//     that writer waits before publishing.
-// So a warp waits only for the column it needs, never for other warps'
-// updates; warps stay within one column of each other.  NRB: the
+// k .. n-1 of one matrix, column-owner layout (file comment).  NRB: the
 // panel's 32-row blocks, ceil((n - k) / 32).  Leaves the factored columns in
 // H, tau in global memory, and S(l, c) = v_l^T v_c (l < c; 0 elsewhere) at
 // Ts[c * 32 + l] and tau at taus[] in shared memory for the trailing update.
@@ -239,7 +206,6 @@ __device__ __forceinline__ void mid_panel(float *__restrict__ Hm, float *__restr
 
 #pragma unroll 1
     for (int c = 0; c < wp; ++c) {
-        if (c > 0 && w != (c & 7)) named_bar_sync(1 + (c & 1));  // F(c & 1)
         const float *xp = xs + (c & 1) * XB;
         // (1) the published column: tail x (rows > k + c) and alpha
         float x[NRB];
@@ -255,11 +221,6 @@ __device__ __forceinline__ void mid_panel(float *__restrict__ Hm, float *__restr
             s2[i & 1] = fmaf(x[i], x[i], s2[i & 1]);
 #pragma unroll
             for (int q = 0; q < 4; ++q) d[q] = fmaf(x[i], P[i][q], d[q]);
-        }
-        // x is consumed (the loads have completed): buffer c & 1 may be reused
-        if (c + 2 < wp && w != ((c + 2) & 7)) {
-            __threadfence_block();
-            named_bar_arrive(3 + (c & 1));  // E(c & 1)
         }
         float rc[4];  // the pivot row k + c of this warp's columns
 #pragma unroll
@@ -325,13 +286,10 @@ __device__ __forceinline__ void mid_panel(float *__restrict__ Hm, float *__restr
                 const float tw = r.tau * wv[q];
                 float *xn = xs + ((c + 1) & 1) * XB;
 #pragma unroll
-                for (int i = 0; i < NRB; ++i) P[i][q] = fmaf(-tw, v[i], P[i][q]);
-                // buffer (c + 1) & 1 held column c - 1: wait until every warp has read it
-                if (c >= 1) named_bar_sync(3 + ((c + 1) & 1));  // E((c + 1) & 1)
-#pragma unroll
-                for (int i = 0; i < NRB; ++i) xn[32 * i + lane] = P[i][q];
-                __threadfence_block();
-                named_bar_arrive(1 + ((c + 1) & 1));  // F((c + 1) & 1)
+                for (int i = 0; i < NRB; ++i) {
+                    P[i][q] = fmaf(-tw, v[i], P[i][q]);
+                    xn[32 * i + lane] = P[i][q];
+                }
             }
         }
         // (4) S of the finished columns, tau, the other updates
@@ -357,6 +315,7 @@ __device__ __forceinline__ void mid_panel(float *__restrict__ Hm, float *__restr
                 }
             }
         }
+        __syncthreads();
     }
 
     // store the factored columns (rows k ..) and tau
