@@ -47,6 +47,11 @@ struct TrailingMaps {
     CUtensorMap v64;  // 32 rows x 64 panel columns, 128-byte swizzle (rank-64 update)
 };
 cudaError_t prepare_trailing_tc(float *H, int64_t batch, int m, int n, TrailingMaps *maps);
+// 32 x 32 tiles (128-byte swizzle) of a batch of row-major rows x cols float
+// matrices: element (i, j) of matrix b at A[b * bs + i * rs + j]; needs a
+// 16-byte aligned A and rs, bs multiples of 4.
+cudaError_t encode_rowmajor_tiles(const float *A, int64_t batch, int rows, int cols, int64_t bs, int64_t rs,
+                                  CUtensorMap *map);
 // Maps for applying the reflectors stored in H (n x n per matrix) to a
 // target C (m x c_cols per matrix, column-major, batch stride m * c_cols);
 // H is m x hcols (column length m).
@@ -120,6 +125,7 @@ cudaError_t launch_trailing64_tc(const TrailingMaps &maps, float *H, const float
 // failure path runs without any fault (a test hook).
 constexpr int kMidMaxN = 256;
 constexpr int kMidFlagForceTimeout = 1;
+constexpr int kMidFlagTmaCopy = 2;  // internal: A is read by TMA tiles (row-major, aligned)
 bool mid_supported(int64_t m, int64_t n, const void *H);
 cudaError_t launch_mid(const float *A, int64_t batch, int n, int64_t bs, int64_t rs, int64_t cs, float *H,
                        float *tau, int *status, int status_words, int flags, cudaStream_t st);

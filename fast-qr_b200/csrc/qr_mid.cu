@@ -91,9 +91,9 @@ constexpr int kOffX = 0;
 constexpr int kOffCopy = 0;
 constexpr int kCopyTile = 32 * 33;
 // live across phases
-constexpr int kOffS = kRingBytes;       // S(l, c) at c * 32 + l (4 KB)
+constexpr int kOffS = kRingBytes;       // S(l, c) at l * 32 + c (4 KB)
 constexpr int kOffTau = kOffS + 4096;   // tau of the panel (128 B)
-constexpr int kOffBar = kOffTau + 128;  // mbarriers full[4], mma[2], phase C, test hook; TMEM address
+constexpr int kOffBar = kOffTau + 128;  // mbarriers full[4], mma[2], phase C, test hook, copy-in; TMEM address at +96
 constexpr int kSmemUsed = kOffBar + 128;
 constexpr int kSmem = kSmemUsed + 1024;  // + alignment slack
 static_assert(2 * (kSmem + 1024) <= 228 * 1024, "two CTAs per SM");
@@ -152,6 +152,57 @@ __device__ __forceinline__ void mid_copy_in(const float *__restrict__ Am, int64_
     }
 }
 
+// Copy-in by TMA (row-major A, 16-byte aligned rows and matrices): 32 x 32
+// tiles of A land in shared memory (128-byte swizzle: row r's 16-byte piece q
+// at (q ^ (r % 8)) * 16), up to 24 per round (the whole ring); each warp
+// turns its tiles into H columns, lane = tile row: eight 16-byte reads per
+// lane (8 consecutive lanes hit 8 distinct bank groups), then per tile column
+// one store of 32 consecutive rows.  Returns false if the wait for a round
+// gave up (after a second bounded wait for its copies).
+__device__ __forceinline__ bool mid_copy_in_tma(const CUtensorMap *tmA, int mat, float *__restrict__ Hm, int n,
+                                                unsigned char *smem, uint64_t *bar)
+{
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const int nbt = (n + 31) >> 5, total = nbt * nbt;
+    constexpr int kRound = kRingBytes / 4096;
+    uint32_t phase = 0;
+    for (int base = 0; base < total; base += kRound) {
+        const int cnt = min(kRound, total - base);
+        if (tid == 0) {
+            tc::mbar_expect_tx(bar, (uint32_t)cnt * 4096u);
+            for (int t = 0; t < cnt; ++t) {
+                const int b = base + t;
+                tc::tma_load_3d(smem + t * 4096, tmA, (b % nbt) * 32, (b / nbt) * 32, mat, bar);
+            }
+        }
+        const bool landed = tc::mbar_wait(bar, phase & 1u, kWaitLimit);
+        ++phase;
+        if (__syncthreads_or(!landed)) {
+            if (tid == 0) tc::mbar_wait(bar, (phase - 1) & 1u, kWaitLimit);
+            __syncthreads();
+            return false;
+        }
+        for (int t = w; t < cnt; t += kWarps) {
+            const int b = base + t, r = (b / nbt) * 32 + lane, c0 = (b % nbt) * 32;
+            const unsigned char *row = smem + t * 4096 + lane * 128;
+            float v[32];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const float4 f = *reinterpret_cast<const float4 *>(row + ((q ^ (lane & 7)) << 4));
+                v[4 * q] = f.x;
+                v[4 * q + 1] = f.y;
+                v[4 * q + 2] = f.z;
+                v[4 * q + 3] = f.w;
+            }
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (r < n && c0 + j < n) Hm[(int64_t)(c0 + j) * n + r] = v[j];
+        }
+        __syncthreads();  // the tiles are read before the next round lands
+    }
+    return true;
+}
+
 // Reduce-scatter of 4 per-lane values over a warp: returns the warp total of
 // slot lane >> 3 (two halving levels over lane bits 4, 3, then three
 // butterfly levels over bits 2, 1, 0).
@@ -178,7 +229,7 @@ __device__ __forceinline__ float reduce_scatter4(const float (&d)[4], int lane)
 // k .. n-1 of one matrix, column-owner layout (file comment).  NRB: the
 // panel's 32-row blocks, ceil((n - k) / 32).  Leaves the factored columns in
 // H, tau in global memory, and S(l, c) = v_l^T v_c (l < c; 0 elsewhere) at
-// Ts[c * 32 + l] and tau at taus[] in shared memory for the trailing update.
+// Ts[l * 32 + c] and tau at taus[] in shared memory for the trailing update.
 template <int NRB>
 __device__ __forceinline__ void mid_panel(float *__restrict__ Hm, float *__restrict__ tau_m, int n, int k,
                                        float *xs, float *Ts, float *taus)
@@ -292,12 +343,13 @@ __device__ __forceinline__ void mid_panel(float *__restrict__ Hm, float *__restr
                 }
             }
         }
-        // (4) S of the finished columns, tau, the other updates
-        if (lane == 0) {
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-                if (w + 8 * q < c) Ts[c * kPanel + w + 8 * q] = wv[q];
-            if (w == (c & 7)) taus[c] = r.tau;
+        // (4) S of the finished columns (lane q < 4 writes slot q), tau, the
+        // other updates
+        {
+            const int qq = lane & 3, j = w + 8 * qq;
+            const float sv = qq == 0 ? wv[0] : (qq == 1 ? wv[1] : (qq == 2 ? wv[2] : wv[3]));
+            if (lane < 4 && j < c) Ts[j * kPanel + c] = sv;
+            if (lane == 4 && w == (c & 7)) taus[c] = r.tau;
         }
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -309,10 +361,8 @@ __device__ __forceinline__ void mid_panel(float *__restrict__ Hm, float *__restr
             } else if (j == c) {
                 // column c becomes beta on the pivot row and v below it
 #pragma unroll
-                for (int i = 0; i < NRB; ++i) {
-                    if (i > 0 || lane > c) P[i][q] = v[i];
-                    else if (lane == c) P[i][q] = r.beta;
-                }
+                for (int i = 0; i < NRB; ++i)
+                    P[i][q] = (i > 0 || lane > c) ? v[i] : (lane == c ? r.beta : P[i][q]);
             }
         }
         __syncthreads();
@@ -572,21 +622,21 @@ __device__ __forceinline__ bool mid_trailing(const CUtensorMap *tmC, const CUten
             tc::tmem_ld_wait();
 #pragma unroll
             for (int j = 0; j < 32; ++j) a[j] += t[j];
-            // y_l = tau_l (w_l - sum_{i<l} S(i, l) y_i); a[i < l] hold y_i.  S
-            // column l is read four entries at a time (every thread reads the
-            // same address)
+            // y_l = tau_l (w_l - sum_{i<l} S(i, l) y_i), right-looking: once y_l
+            // is known it is subtracted from every later a_j (row l of S read
+            // four entries at a time; every thread reads the same address), so
+            // the dependency chain is one multiply and one FMA per reflector
 #pragma unroll
             for (int l = 0; l < kPanel; ++l) {
-                float acc = a[l];
+                a[l] *= taus[l];
 #pragma unroll
-                for (int i4 = 0; i4 < (l + 3) / 4; ++i4) {
-                    const float4 s4 = *reinterpret_cast<const float4 *>(Ts + l * kPanel + 4 * i4);
+                for (int j4 = (l + 1) / 4; j4 < kPanel / 4; ++j4) {
+                    const float4 s4 = *reinterpret_cast<const float4 *>(Ts + l * kPanel + 4 * j4);
                     const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
                     for (int u = 0; u < 4; ++u)
-                        if (4 * i4 + u < l) acc = fmaf(-sv[u], a[4 * i4 + u], acc);
+                        if (4 * j4 + u > l) a[4 * j4 + u] = fmaf(-sv[u], a[l], a[4 * j4 + u]);
                 }
-                a[l] = taus[l] * acc;
             }
             // Y as the K-major B operand: column c's 32 values at c * 128,
             // 16-byte piece jq at (jq ^ (c % 8)) * 16
@@ -709,7 +759,8 @@ __device__ __forceinline__ bool mid_trailing(const CUtensorMap *tmC, const CUten
 // trailing update, all in this launch.
 __global__ void __launch_bounds__(kThreads, 2)
 mid_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmV,
-           const __grid_constant__ CUtensorMap tmCQ, const float *__restrict__ A, int64_t a_bs, int64_t a_rs,
+           const __grid_constant__ CUtensorMap tmCQ, const __grid_constant__ CUtensorMap tmA,
+           const float *__restrict__ A, int64_t a_bs, int64_t a_rs,
            int64_t a_cs, float *__restrict__ H, float *__restrict__ tau, int *__restrict__ status, int n,
            int flags)
 {
@@ -719,15 +770,18 @@ mid_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUte
     const int tid = threadIdx.x, warp = tid >> 5;
     const int64_t mat = blockIdx.x;
     float *Hm = H + mat * (int64_t)n * n;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kOffBar);  // full[4], mma[2], phase C, test hook
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kOffBar + 64);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kOffBar);  // full[4], mma[2], phase C, test hook, copy-in
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kOffBar + 96);
+    const bool tma_copy = flags & kMidFlagTmaCopy;
     if (tid == 0) {
         tc::prefetch_tensormap(&tmC);
         tc::prefetch_tensormap(&tmV);
         tc::prefetch_tensormap(&tmCQ);
-        for (int i = 0; i < kStages + 4; ++i) tc::mbar_init(&bars[i], 1);
+        if (tma_copy) tc::prefetch_tensormap(&tmA);
+        for (int i = 0; i < kStages + 5; ++i) tc::mbar_init(&bars[i], 1);
         tc::fence_mbar_init();
     }
+    __syncthreads();  // the barriers are initialised before the copy-in waits on one
     // (every CTA that allocates tensor memory in this library holds >= 98 KB
     // of shared memory, so at most two share an SM and their 256-column
     // allocations never wait)
@@ -736,7 +790,11 @@ mid_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUte
         tc::tmem_alloc(tmem_slot, kTmemCols);
         tc::tmem_relinquish();
     }
-    mid_copy_in(A + mat * a_bs, a_rs, a_cs, Hm, n, reinterpret_cast<float *>(smem + kOffCopy));
+    bool ok = true;
+    if (tma_copy)
+        ok = mid_copy_in_tma(&tmA, (int)mat, Hm, n, smem, &bars[kStages + 4]);
+    else
+        mid_copy_in(A + mat * a_bs, a_rs, a_cs, Hm, n, reinterpret_cast<float *>(smem + kOffCopy));
     fence_proxy_async_all();  // H is read by TMA in the first trailing update
     tc::fence_before_sync();
     __syncthreads();
@@ -747,7 +805,6 @@ mid_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUte
     float *Ts = reinterpret_cast<float *>(smem + kOffS);
     float *taus = reinterpret_cast<float *>(smem + kOffTau);
     MidSync sy = {0u, 0u};
-    bool ok = true;
     for (int k = 0; k < n && ok; k += kPanel) {
         mid_panel_any(Hm, tau + mat * n, n, k, xs, Ts, taus);
         if (k + kPanel < n)
@@ -776,13 +833,23 @@ cudaError_t launch_mid(const float *A, int64_t batch, int n, int64_t bs, int64_t
     TrailingMaps maps;
     cudaError_t e = prepare_trailing_tc(H, batch, n, n, &maps);
     if (e != cudaSuccess) return e;
+    // A by TMA tiles when its rows and matrices are 16-byte aligned
+    // (row-major, contiguous columns); any other layout by plain loads
+    CUtensorMap tmA = maps.c;  // (unused unless the flag is set)
+    const bool tma_copy = cs == 1 && ((uintptr_t)A % 16) == 0 && rs % 4 == 0 && rs >= n &&
+                          (batch == 1 || (bs % 4 == 0 && bs >= (int64_t)n * rs));
+    if (tma_copy) {
+        e = encode_rowmajor_tiles(A, batch, n, n, bs, rs, &tmA);
+        if (e != cudaSuccess) return e;
+        flags |= kMidFlagTmaCopy;
+    }
     e = cudaFuncSetAttribute(mid_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
     if (e != cudaSuccess) return e;
     // the status words of this call start clear (the kernel only sets them)
     e = cudaMemsetAsync(status, 0, (size_t)status_words * sizeof(int), st);
     if (e != cudaSuccess) return e;
-    mid_kernel<<<dim3((unsigned)batch), dim3(kThreads), kSmem, st>>>(maps.c, maps.v, maps.cq, A, bs, rs, cs, H,
-                                                                     tau, status, n, flags);
+    mid_kernel<<<dim3((unsigned)batch), dim3(kThreads), kSmem, st>>>(maps.c, maps.v, maps.cq, tmA, A, bs, rs, cs,
+                                                                     H, tau, status, n, flags);
     return cudaGetLastError();
 }
 

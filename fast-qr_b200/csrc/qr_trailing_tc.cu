@@ -604,6 +604,22 @@ cudaError_t prepare_apply_maps(const float *H, int ld, int hcols, float *C, int6
     return cudaSuccess;
 }
 
+cudaError_t encode_rowmajor_tiles(const float *A, int64_t batch, int rows, int cols, int64_t bs, int64_t rs,
+                                  CUtensorMap *map)
+{
+    PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+    if (!enc) return cudaErrorNotSupported;
+    // x = column (contiguous), y = row, z = matrix; 32 x 32 boxes, 128-byte swizzle
+    const cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)batch};
+    const cuuint64_t strides[2] = {(cuuint64_t)rs * 4, (cuuint64_t)(batch > 1 ? bs : (int64_t)rows * rs) * 4};
+    const cuuint32_t box[3] = {32, 32, 1}, unit[3] = {1, 1, 1};
+    if (enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(A), dims, strides, box, unit,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return cudaErrorInvalidValue;
+    return cudaSuccess;
+}
+
 cudaError_t prepare_trailing_tc(float *H, int64_t batch, int m, int n, TrailingMaps *maps)
 {
     return prepare_apply_maps(H, m, n, H, n, batch, maps);
