@@ -57,8 +57,9 @@ constexpr uint32_t kTmemCols = 256;
 constexpr uint64_t kWaitLimit = 1000000000ull;  // 1 s of wall time per wait
 
 // tensor memory.  Phase A: kDA = C_hi^T [V | V_lo] (64 columns: hi*hi, then
-// hi*lo), kDA2 = C_lo^T V (32), kALo + 32 * (chunk & 1): C_lo^T of a chunk,
-// the A operand of the second product.  Phase C (W is dead): P of even and
+// hi*lo), kDA2 = C_lo^T V (32), kALo + 32 * (chunk % 3): C_lo^T of a chunk,
+// the A operand of the second product (three buffers: a chunk's split waits
+// only for the MMAs of the chunk two before it).  Phase C (W is dead): P of even and
 // odd 128-row chunks in turn (128 columns each), so that a chunk's MMAs run
 // during the previous chunk's epilogue.
 constexpr uint32_t kDA = 0;
@@ -93,13 +94,14 @@ constexpr int kCopyTile = 32 * 33;
 // live across phases
 constexpr int kOffS = kRingBytes;       // S(l, c) at l * 32 + c (4 KB)
 constexpr int kOffTau = kOffS + 4096;   // tau of the panel (128 B)
-constexpr int kOffBar = kOffTau + 128;  // mbarriers full[4], mma[2], phase C, test hook, copy-in; TMEM address at +96
+constexpr int kOffBar = kOffTau + 128;  // mbarriers full[4], mma[3], phase C, test hook, copy-in; TMEM address at +96
 constexpr int kSmemUsed = kOffBar + 128;
 constexpr int kSmem = kSmemUsed + 1024;  // + alignment slack
 static_assert(2 * (kSmem + 1024) <= 228 * 1024, "two CTAs per SM");
 static_assert(kOffCQ + kWarps * kCQPiece <= kRingBytes, "phase-C buffers overlap S");
 static_assert(kWarps * 2 * kCopyTile * 4 <= kRingBytes, "copy-in tiles overlap S");
 static_assert(kStageBytes % 1024 == 0 && kCBytes % 1024 == 0, "swizzle atoms need 1024-byte alignment");
+static_assert((kStages + 6) * 8 <= 96, "mbarriers overlap the TMEM address slot");
 
 constexpr uint32_t kIdescA = tc::idesc_tf32(128, 64, 0, 0);   // A = C_hi^T (smem), B = [V | V_lo]
 constexpr uint32_t kIdescA2 = tc::idesc_tf32(128, 32, 0, 0);  // A = C_lo^T (TMEM), B = V
@@ -343,13 +345,12 @@ __device__ __forceinline__ void mid_panel(float *__restrict__ Hm, float *__restr
                 }
             }
         }
-        // (4) S of the finished columns (lane q < 4 writes slot q), tau, the
-        // other updates
-        {
-            const int qq = lane & 3, j = w + 8 * qq;
-            const float sv = qq == 0 ? wv[0] : (qq == 1 ? wv[1] : (qq == 2 ? wv[2] : wv[3]));
-            if (lane < 4 && j < c) Ts[j * kPanel + c] = sv;
-            if (lane == 4 && w == (c & 7)) taus[c] = r.tau;
+        // (4) S of the finished columns, tau, the other updates
+        if (lane == 0) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+                if (w + 8 * q < c) Ts[(w + 8 * q) * kPanel + c] = wv[q];
+            if (w == (c & 7)) taus[c] = r.tau;
         }
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -361,8 +362,10 @@ __device__ __forceinline__ void mid_panel(float *__restrict__ Hm, float *__restr
             } else if (j == c) {
                 // column c becomes beta on the pivot row and v below it
 #pragma unroll
-                for (int i = 0; i < NRB; ++i)
-                    P[i][q] = (i > 0 || lane > c) ? v[i] : (lane == c ? r.beta : P[i][q]);
+                for (int i = 0; i < NRB; ++i) {
+                    if (i > 0 || lane > c) P[i][q] = v[i];
+                    else if (lane == c) P[i][q] = r.beta;
+                }
             }
         }
         __syncthreads();
@@ -404,8 +407,9 @@ __device__ __forceinline__ void mid_panel_any(float *Hm, float *tau_m, int n, in
 // Barrier use counts, the same in every thread.  The kernel reuses its
 // barriers for every tile of every panel: phase-A chunks are numbered across
 // the whole factorisation, chunk g going through ring stage g % kStages (its
-// (g / kStages)-th use) and MMA barrier g % 2 (its (g / 2)-th use); phase-C
-// MMA groups are counted the same way.
+// (g / kStages)-th use), TMEM lo buffer g % 3 and MMA barrier g % 3 (its
+// (g / 3)-th use: a wait is never two phases behind, so parities cannot
+// alias); phase-C MMA groups are counted the same way.
 struct MidSync {
     uint32_t chunk;  // phase-A chunks issued so far (all waited for)
     uint32_t cgrp;   // phase-C MMA groups issued so far (all waited for)
@@ -510,9 +514,9 @@ __device__ __forceinline__ bool mid_trailing(const CUtensorMap *tmC, const CUten
     const uint32_t sbase = tc::smem_addr(smem);
     const uint32_t lane_q = tmem + ((uint32_t)(32 * (warp & 3)) << 16);  // this warp's TMEM lanes
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + kOffBar);  // [kStages]
-    uint64_t *mmab = full + kStages;                                // [2]
-    uint64_t *cbar = full + kStages + 2;                            // phase C
-    uint64_t *never = full + kStages + 3;                           // the test hook's barrier
+    uint64_t *mmab = full + kStages;                                // [3]
+    uint64_t *cbar = full + kStages + 3;                            // phase C
+    uint64_t *never = full + kStages + 4;                           // the test hook's barrier
     const float *Ts = reinterpret_cast<const float *>(smem + kOffS);
     const float *taus = reinterpret_cast<const float *>(smem + kOffTau);
     float *piece = reinterpret_cast<float *>(smem + kOffCQ + warp * kCQPiece);  // this warp's -P piece
@@ -545,7 +549,7 @@ __device__ __forceinline__ bool mid_trailing(const CUtensorMap *tmC, const CUten
 
         // ---- phase A --------------------------------------------------------
         for (int i = 0; i < nchunks; ++i) {
-            const uint32_t g = g0 + i, si = g % kStages, b = g & 1;
+            const uint32_t g = g0 + i, si = g % kStages;
             unsigned char *st = smem + si * kStageBytes;
             bool landed;
             if (force_timeout && i == 0)
@@ -556,7 +560,8 @@ __device__ __forceinline__ bool mid_trailing(const CUtensorMap *tmC, const CUten
             // run by every thread (the TMEM stores are warp-collective); after a
             // wait that gave up it moves garbage that no MMA reads
             tc::fence_after_sync();
-            mid_split(st, lane_q + kALo + 32u * b, i == 0, tid);
+            const uint32_t lo = kALo + 32u * (g % 3u);
+            mid_split(st, lane_q + lo, i == 0, tid);
             tc::tmem_st_wait();
             tc::fence_proxy_async_smem();
             tc::fence_before_sync();
@@ -573,17 +578,18 @@ __device__ __forceinline__ bool mid_trailing(const CUtensorMap *tmC, const CUten
                     const uint64_t bv = tc::smem_desc_sw128(sV + ko);  // V rows, then V_lo rows
                     const uint32_t acc = (i > 0 || s > 0) ? 1u : 0u;
                     tc::mma_tf32(tmem + kDA, ac, bv, kIdescA, acc);
-                    tc::mma_tf32_ts(tmem + kDA2, tmem + kALo + 32u * b + 8u * s, bv, kIdescA2, acc);
+                    tc::mma_tf32_ts(tmem + kDA2, tmem + lo + 8u * s, bv, kIdescA2, acc);
                 }
-                tc::mma_commit(&mmab[b]);
+                tc::mma_commit(&mmab[g % 3]);
             }
             ++mma_n;
-            if (i >= 1) {
-                // chunk i-1's MMAs: afterwards its stage and TMEM lo buffer are free
-                const uint32_t gp = g - 1;
-                const bool done = tc::mbar_wait(&mmab[gp & 1], (gp >> 1) & 1u, kWaitLimit);
+            if (i >= 2) {
+                // chunk i-2's MMAs: afterwards its stage and TMEM lo buffer are
+                // free (chunk i-1's may still run)
+                const uint32_t gp = g - 2;
+                const bool done = tc::mbar_wait(&mmab[gp % 3], (gp / 3) & 1u, kWaitLimit);
                 if (done) ++mma_done;
-                const int nx = i - 1 + kStages;
+                const int nx = i - 2 + kStages;
                 if (!done) {
                     bad = true;  // made uniform by the next __syncthreads_or
                 } else if (tid == 0 && nx < nchunks) {
@@ -598,9 +604,13 @@ __device__ __forceinline__ bool mid_trailing(const CUtensorMap *tmC, const CUten
         }
         ok = !__syncthreads_or(!ok || bad);
         if (ok) {
-            const uint32_t gl = g0 + nchunks - 1;
-            const bool done = tc::mbar_wait(&mmab[gl & 1], (gl >> 1) & 1u, kWaitLimit);
-            if (done) ++mma_done;
+            // the last two chunks' MMAs
+            bool done = true;
+            for (int i = nchunks >= 2 ? nchunks - 2 : 0; i < nchunks && done; ++i) {
+                const uint32_t gl = g0 + i;
+                done = tc::mbar_wait(&mmab[gl % 3], (gl / 3) & 1u, kWaitLimit);
+                if (done) ++mma_done;
+            }
             ok = !__syncthreads_or(!done);
         }
         sy.chunk = g0 + nchunks;
@@ -740,7 +750,7 @@ __device__ __forceinline__ bool mid_trailing(const CUtensorMap *tmC, const CUten
             }
             for (int i = mma_done; i < mma_n; ++i) {
                 const uint32_t g = g0 + i;
-                if (!tc::mbar_wait(&mmab[g & 1], (g >> 1) & 1u, kWaitLimit)) break;
+                if (!tc::mbar_wait(&mmab[g % 3], (g / 3) & 1u, kWaitLimit)) break;
             }
             for (int u = cg_done; u < cg_n; ++u)
                 if (!tc::mbar_wait(cbar, (sy.cgrp + (uint32_t)(u - cg_done)) & 1u, kWaitLimit)) break;
@@ -770,7 +780,7 @@ mid_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUte
     const int tid = threadIdx.x, warp = tid >> 5;
     const int64_t mat = blockIdx.x;
     float *Hm = H + mat * (int64_t)n * n;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kOffBar);  // full[4], mma[2], phase C, test hook, copy-in
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kOffBar);  // full[4], mma[3], phase C, test hook, copy-in
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kOffBar + 96);
     const bool tma_copy = flags & kMidFlagTmaCopy;
     if (tid == 0) {
@@ -778,7 +788,7 @@ mid_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUte
         tc::prefetch_tensormap(&tmV);
         tc::prefetch_tensormap(&tmCQ);
         if (tma_copy) tc::prefetch_tensormap(&tmA);
-        for (int i = 0; i < kStages + 5; ++i) tc::mbar_init(&bars[i], 1);
+        for (int i = 0; i < kStages + 6; ++i) tc::mbar_init(&bars[i], 1);
         tc::fence_mbar_init();
     }
     __syncthreads();  // the barriers are initialised before the copy-in waits on one
@@ -792,7 +802,7 @@ mid_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUte
     }
     bool ok = true;
     if (tma_copy)
-        ok = mid_copy_in_tma(&tmA, (int)mat, Hm, n, smem, &bars[kStages + 4]);
+        ok = mid_copy_in_tma(&tmA, (int)mat, Hm, n, smem, &bars[kStages + 5]);
     else
         mid_copy_in(A + mat * a_bs, a_rs, a_cs, Hm, n, reinterpret_cast<float *>(smem + kOffCopy));
     fence_proxy_async_all();  // H is read by TMA in the first trailing update
