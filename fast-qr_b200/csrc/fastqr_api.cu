@@ -44,10 +44,9 @@ bool small_path(int64_t n) { return n <= 64; }
 
 // the one-launch mid-size path for square n (with a 16-byte aligned H,
 // which every torch / cudaMalloc allocation is)
-std::atomic<int> g_debug_flags{0};
-std::atomic<int> g_debug_plan{0};  // 1: the blocked path instead of the mid-size kernel
+bool mid_path(int64_t n) { return fqr::mid_supported(n, n, nullptr); }
 
-bool mid_path(int64_t n) { return g_debug_plan.load() == 0 && fqr::mid_supported(n, n, nullptr); }
+std::atomic<int> g_debug_flags{0};
 
 int status_from(cudaError_t e)
 {
@@ -61,8 +60,6 @@ int status_from(cudaError_t e)
 extern "C" {
 
 int fqr_version(void) { return 100; }
-
-int fqr_debug_plan(int mode) { return g_debug_plan.exchange(mode == 1 ? 1 : 0); }
 
 int fqr_debug_force_timeout(int enable)
 {
@@ -350,7 +347,7 @@ int run_geqrf(const float *A, int64_t batch, int64_t m, int64_t n, int64_t a_bst
     // the status block first, then the S blocks
     float *Sws = (float *)((unsigned char *)workspace + kWsAlign);
     int *status = status_word ? status_word : (int *)workspace;
-    if (m == n && g_debug_plan.load() == 0 && fqr::mid_supported(m, n, H)) {
+    if (m == n && fqr::mid_supported(m, n, H)) {
         // one launch; an own status word (host entry, one per chunk) or the
         // whole status block of the workspace
         if (tm) tm->begin(FQR_STAGE_MID);

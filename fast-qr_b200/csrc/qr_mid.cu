@@ -6,9 +6,8 @@
 // matrix runs its own chain inside its CTA:
 //   copy-in   A (any strides) -> H (column-major), through shared memory
 //   per panel k = 0, 32, ...:
-//     panel     32 columns x (n - k) rows: the blocked path's panel
-//               (panel_body.cuh) run by this CTA's 8 warps, one 32-row block
-//               each, with S = V^T V kept in shared memory
+//     panel     32 columns x (n - k) rows in registers, column-owner layout
+//               (below); S = V^T V and tau stay in shared memory
 //     trailing  C := C - V (T^T (V^T C)) on the tensor cores, tile by tile
 //               (128 trailing columns per tile), 3xTF32 as in the blocked
 //               path's updates, with the C tile streamed from H by TMA (H
@@ -20,11 +19,27 @@
 // algorithm is the blocked compact-WY restatement of oracle/geqr2.c
 // (oracle_geqrf_blocked_f64) with T never formed: the panel keeps
 // S = strict_upper(V^T V) and tau, and the update solves (I + D S^T) Y = D W.
+//
+// Panel, column-owner layout: warp w owns panel columns w, w+8, w+16, w+24
+// (slot q = column w + 8q); lane l holds rows k + 32i + l of them (row block
+// i; only the panel's own row blocks are held: the column loop is compiled
+// once per row-block count).  Per column c, one CTA barrier:
+//   * the owner of column c has published its current values (the unscaled
+//     tail x and the pivot alpha) to shared memory before the barrier;
+//   * every warp reads x, forms sigma = x^T x and the unscaled dots
+//     d_q = x^T a_q of its own 4 columns (a reduce-scatter over the lanes and
+//     a broadcast back; no cross-warp reduction), and the reflector from
+//     (alpha, sigma) -- the same inputs and the same reduction order in every
+//     warp, so the same bits everywhere;
+//   * w_q = a_q(c) + scale * d_q (v^T a_q), the rank-1 update of its active
+//     columns, S(q, c) = w_q for its finished columns q < c;
+//   * the owner of column c+1 updates and publishes it first.
+// Out-of-envelope columns take LAPACK order as in the blocked panel
+// (common.cuh): sigma in double, then w = v^T a with the scaled v.
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
 #include "internal.h"
-#include "panel_body.cuh"
 #include "tc.cuh"
 
 namespace fqr {
@@ -37,7 +52,7 @@ constexpr int kTN = 128;     // trailing columns per tile
 constexpr int kRC = 32;      // rows per phase-A chunk (MMA K = 4 x 8; one 128-byte swizzle row)
 constexpr int kRCC = 128;    // rows per phase-C chunk (MMA M)
 constexpr int kStages = 4;   // phase-A ring
-constexpr int kMaxRB = 8;    // 32-row blocks of the tallest panel (one per warp)
+constexpr int kMaxRB = 8;    // 32-row blocks of the tallest panel (n <= 256)
 constexpr uint32_t kTmemCols = 256;
 constexpr uint64_t kWaitLimit = 1000000000ull;  // 1 s of wall time per wait
 
@@ -71,8 +86,8 @@ constexpr int kOffVlo = 49152;
 constexpr int kOffCQ = 65536;
 constexpr int kCQCols = 32;
 constexpr int kCQPiece = 32 * kCQCols * 4;  // 4 KB
-// panel (reuses the ring): its staging blocks (8 warps x 32 x 36 floats)
-constexpr int kOffStage = 0;
+// panel (reuses the ring): the published column, double-buffered
+constexpr int kOffX = 0;
 // copy-in (reuses the ring): two 32 x 33 float tiles per warp
 constexpr int kOffCopy = 0;
 constexpr int kCopyTile = 32 * 33;
@@ -84,7 +99,6 @@ constexpr int kSmemUsed = kOffBar + 128;
 constexpr int kSmem = kSmemUsed + 1024;  // + alignment slack
 static_assert(2 * (kSmem + 1024) <= 228 * 1024, "two CTAs per SM");
 static_assert(kOffCQ + kWarps * kCQPiece <= kRingBytes, "phase-C buffers overlap S");
-static_assert(kWarps * 32 * kStagePitch * 4 <= kRingBytes, "panel staging overlaps S");
 static_assert(kWarps * 2 * kCopyTile * 4 <= kRingBytes, "copy-in tiles overlap S");
 static_assert(kStageBytes % 1024 == 0 && kCBytes % 1024 == 0, "swizzle atoms need 1024-byte alignment");
 static_assert((kStages + 6) * 8 <= 96, "mbarriers overlap the TMEM address slot");
@@ -189,6 +203,205 @@ __device__ __forceinline__ bool mid_copy_in_tma(const CUtensorMap *tmA, int mat,
         __syncthreads();  // the tiles are read before the next round lands
     }
     return true;
+}
+
+// Reduce-scatter of 4 per-lane values over a warp: returns the warp total of
+// slot lane >> 3 (two halving levels over lane bits 4, 3, then three
+// butterfly levels over bits 2, 1, 0).
+__device__ __forceinline__ float reduce_scatter4(const float (&d)[4], int lane)
+{
+    const bool b4 = lane & 16, b3 = lane & 8;
+    float e[2];
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+        const float send = b4 ? d[t] : d[t + 2];
+        const float keep = b4 ? d[t + 2] : d[t];
+        e[t] = keep + __shfl_xor_sync(kFull, send, 16);
+    }
+    const float send = b3 ? e[0] : e[1];
+    const float keep = b3 ? e[1] : e[0];
+    float g = keep + __shfl_xor_sync(kFull, send, 8);
+    g += __shfl_xor_sync(kFull, g, 4);
+    g += __shfl_xor_sync(kFull, g, 2);
+    g += __shfl_xor_sync(kFull, g, 1);
+    return g;
+}
+
+// Panel factorisation of columns k .. k+wp-1 (wp = min(32, n - k)) over rows
+// k .. n-1 of one matrix, column-owner layout (file comment).  NRB: the
+// panel's 32-row blocks, ceil((n - k) / 32).  Leaves the factored columns in
+// H, tau in global memory, and S(l, c) = v_l^T v_c (l < c; 0 elsewhere) at
+// Ts[l * 32 + c] and tau at taus[] in shared memory for the trailing update.
+template <int NRB>
+__device__ __forceinline__ void mid_panel(float *__restrict__ Hm, float *__restrict__ tau_m, int n, int k,
+                                       float *xs, float *Ts, float *taus)
+{
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const int nrow = n - k;            // panel rows
+    const int wp = min(kPanel, nrow);  // reflectors
+    constexpr int XB = kMaxRB * 32;    // floats per published-column buffer
+    float P[NRB][4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const int j = w + 8 * q;
+        const float *src = Hm + (int64_t)(k + j) * n + k + lane;
+#pragma unroll
+        for (int i = 0; i < NRB; ++i)
+            P[i][q] = (j < wp && 32 * i + lane < nrow) ? __ldcg(src + 32 * i) : 0.0f;
+    }
+    for (int t = tid; t < kPanel * kPanel; t += kThreads) Ts[t] = 0.0f;
+    if (tid < kPanel) taus[tid] = 0.0f;
+    if (w == 0) {
+#pragma unroll
+        for (int i = 0; i < NRB; ++i) xs[32 * i + lane] = P[i][0];
+    }
+    __syncthreads();
+
+#pragma unroll 1
+    for (int c = 0; c < wp; ++c) {
+        const float *xp = xs + (c & 1) * XB;
+        // (1) the published column: tail x (rows > k + c) and alpha
+        float x[NRB];
+#pragma unroll
+        for (int i = 0; i < NRB; ++i) x[i] = xp[32 * i + lane];
+        const float alpha = xp[c];
+        if (lane <= c) x[0] = 0.0f;
+        // sigma and the unscaled dots of this warp's 4 columns (column c's own
+        // slot, finished columns' slots and active ones alike)
+        float s2[2] = {0.0f, 0.0f}, d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int i = 0; i < NRB; ++i) {
+            s2[i & 1] = fmaf(x[i], x[i], s2[i & 1]);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) d[q] = fmaf(x[i], P[i][q], d[q]);
+        }
+        float rc[4];  // the pivot row k + c of this warp's columns
+#pragma unroll
+        for (int q = 0; q < 4; ++q) rc[q] = __shfl_sync(kFull, P[0][q], c);
+        const float sg = warp_sum(s2[0] + s2[1]);
+        const float g = reduce_scatter4(d, lane);  // slot lane >> 3, summed over the warp
+        float D[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) D[q] = __shfl_sync(kFull, g, 8 * q);
+
+        // (2) the reflector: the same (alpha, sigma) bits in every warp
+        const bool fast = reflector_fast_ok(alpha, sg);
+        Reflector r;
+        double sd = 1.0;
+        if (fast) {
+            r = reflector_from_float(alpha, sg);
+        } else {
+            double t = 0.0;
+#pragma unroll
+            for (int i = 0; i < NRB; ++i) t = fma((double)x[i], (double)x[i], t);
+            sd = warp_sum(t);
+            r = reflector_from_double(alpha, sd);
+        }
+        // v over this lane's rows (0 above the pivot, 1 on it)
+        float v[NRB];
+        if (!r.wide) {
+#pragma unroll
+            for (int i = 0; i < NRB; ++i) v[i] = x[i] * r.scale;
+        } else {
+#pragma unroll
+            for (int i = 0; i < NRB; ++i) v[i] = (float)((double)x[i] * r.scale_d);
+        }
+        if (lane == c) v[0] = 1.0f;
+        // w_q = v^T a_q over rows >= k + c.  Fast: from the unscaled dots, when
+        // none of this warp's could have over- or underflowed (|d| < 1e28 keeps
+        // scale * d finite: |scale| <= 1e10 inside the envelope); else LAPACK
+        // order with the scaled v (per warp: the reflector is the same either way)
+        float wv[4];
+        const bool dots_ok =
+            fast && !__any_sync(kFull, !(fabsf(g) < 1e28f) || (g != 0.0f && fabsf(g) < kDotTiny));
+        if (dots_ok) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) wv[q] = fmaf(r.scale, D[q], rc[q]);
+        } else if (sd == 0.0) {
+            // exactly zero tail: H = I, v = e_c, w = the pivot row
+#pragma unroll
+            for (int q = 0; q < 4; ++q) wv[q] = rc[q];
+        } else {
+            float d2[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+            for (int i = 0; i < NRB; ++i)
+#pragma unroll
+                for (int q = 0; q < 4; ++q) d2[q] = fmaf(v[i], P[i][q], d2[q]);
+            const float g2 = reduce_scatter4(d2, lane);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) wv[q] = __shfl_sync(kFull, g2, 8 * q);
+        }
+
+        // (3) the owner of column c + 1 updates and publishes it first
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            if (w + 8 * q == c + 1 && c + 1 < wp) {
+                const float tw = r.tau * wv[q];
+                float *xn = xs + ((c + 1) & 1) * XB;
+#pragma unroll
+                for (int i = 0; i < NRB; ++i) {
+                    P[i][q] = fmaf(-tw, v[i], P[i][q]);
+                    xn[32 * i + lane] = P[i][q];
+                }
+            }
+        }
+        // (4) S of the finished columns, tau, the other updates
+        if (lane == 0) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+                if (w + 8 * q < c) Ts[(w + 8 * q) * kPanel + c] = wv[q];
+            if (w == (c & 7)) taus[c] = r.tau;
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int j = w + 8 * q;
+            if (j > c + 1 && j < wp) {
+                const float tw = r.tau * wv[q];
+#pragma unroll
+                for (int i = 0; i < NRB; ++i) P[i][q] = fmaf(-tw, v[i], P[i][q]);
+            } else if (j == c) {
+                // column c becomes beta on the pivot row and v below it
+#pragma unroll
+                for (int i = 0; i < NRB; ++i) {
+                    if (i > 0 || lane > c) P[i][q] = v[i];
+                    else if (lane == c) P[i][q] = r.beta;
+                }
+            }
+        }
+        __syncthreads();
+    }
+
+    // store the factored columns (rows k ..) and tau
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const int j = w + 8 * q;
+        if (j < wp) {
+            float *dst = Hm + (int64_t)(k + j) * n + k + lane;
+#pragma unroll
+            for (int i = 0; i < NRB; ++i)
+                if (32 * i + lane < nrow) dst[32 * i] = P[i][q];
+        }
+    }
+    if (tid < wp) tau_m[k + tid] = taus[tid];
+    // the trailing update reads these columns by TMA (async proxy)
+    fence_proxy_async_all();
+    __syncthreads();
+}
+
+// The panel at k, compiled for its row-block count.
+__device__ __forceinline__ void mid_panel_any(float *Hm, float *tau_m, int n, int k, float *xs, float *Ts,
+                                              float *taus)
+{
+    switch ((n - k + 31) >> 5) {
+    case 1: mid_panel<1>(Hm, tau_m, n, k, xs, Ts, taus); break;
+    case 2: mid_panel<2>(Hm, tau_m, n, k, xs, Ts, taus); break;
+    case 3: mid_panel<3>(Hm, tau_m, n, k, xs, Ts, taus); break;
+    case 4: mid_panel<4>(Hm, tau_m, n, k, xs, Ts, taus); break;
+    case 5: mid_panel<5>(Hm, tau_m, n, k, xs, Ts, taus); break;
+    case 6: mid_panel<6>(Hm, tau_m, n, k, xs, Ts, taus); break;
+    case 7: mid_panel<7>(Hm, tau_m, n, k, xs, Ts, taus); break;
+    default: mid_panel<8>(Hm, tau_m, n, k, xs, Ts, taus); break;
+    }
 }
 
 // Barrier use counts, the same in every thread.  The kernel reuses its
@@ -598,18 +811,12 @@ mid_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUte
     tc::fence_after_sync();
     const uint32_t tmem = *tmem_slot;
 
+    float *xs = reinterpret_cast<float *>(smem + kOffX);
     float *Ts = reinterpret_cast<float *>(smem + kOffS);
     float *taus = reinterpret_cast<float *>(smem + kOffTau);
     MidSync sy = {0u, 0u};
     for (int k = 0; k < n && ok; k += kPanel) {
-        // the blocked path's panel (8 warps x 32 rows: every panel of n <= 256
-        // in one CTA); S row-major into shared memory, tau to global memory
-        panel_body<kWarps, 1, false, false>(H, tau, Ts, 0, kPanel, 1, n, n, k, mat,
-                                            reinterpret_cast<float *>(smem + kOffStage));
-        __syncthreads();
-        if (tid < kPanel) taus[tid] = (k + tid < n) ? __ldcg(tau + mat * n + k + tid) : 0.0f;
-        fence_proxy_async_all();  // the trailing update reads the panel's columns by TMA
-        __syncthreads();
+        mid_panel_any(Hm, tau + mat * n, n, k, xs, Ts, taus);
         if (k + kPanel < n)
             ok = mid_trailing(&tmC, &tmV, &tmCQ, Hm, (int)mat, n, k, smem, tmem, sy,
                               (flags & kMidFlagForceTimeout) && k == 0);

@@ -229,15 +229,6 @@ int fqr_check_status(const void *workspace, size_t workspace_bytes, int64_t batc
  */
 int fqr_debug_force_timeout(int enable);
 
-/*
- * Diagnostic plan override, process-wide; returns the previous mode.
- * mode 0: the static plan (default).  mode 1: square sizes the one-launch
- * mid-size kernel would take run the blocked multi-launch path instead, so
- * that the two can be compared on the same inputs (tests, benchmarks).
- * No counterpart in the reference.
- */
-int fqr_debug_plan(int mode);
-
 /* Kernel classes timed by fqr_geqrf_f32_profile. */
 enum {
     FQR_STAGE_SMALL = 0,     /* warp-per-matrix kernel (n <= 64) */
