@@ -107,8 +107,10 @@ def inblock_bytes(n: int) -> float:
 
 
 def mid_plan(n: int, m: int | None = None) -> bool:
-    """The library's one-launch mid-size plan: square 128 <= n <= 256, n % 4 == 0."""
-    return (m is None or m == n) and 128 <= n <= 256 and n % 4 == 0
+    """The library's one-launch mid-size kernel is not in its static plan (it
+    runs only under fqr_debug_plan(1)); every square size takes the warp
+    kernel (n <= 64) or the blocked path."""
+    return False
 
 
 def stage_launches(n: int, m: int | None = None) -> dict:

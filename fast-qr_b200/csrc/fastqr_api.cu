@@ -2,9 +2,9 @@
 //
 // Static dispatch on (batch, m, n) only:
 //   m == n <= 64 : one warp per matrix, registers (qr_small.cu)
-//   m == n in [128, 256], n % 4 == 0 (and an aligned H) : one launch, one CTA
-//                  per matrix running its whole blocked factorisation
-//                  (qr_mid.cu)
+//   (m == n in [128, 256], n % 4 == 0, with fqr_debug_plan(1) only: one
+//                  launch, one CTA per matrix running its whole blocked
+//                  factorisation, qr_mid.cu)
 //   otherwise    : blocked compact-WY: copy-in, then per 32-column panel a
 //                  panel kernel and a trailing-update kernel (qr_blocked.cu);
 //                  for n >= 2048 (and m <= 4096) per 64 columns two panels,
@@ -42,11 +42,14 @@ bool use_tc(int64_t n) { return fqr::trailing_tc_supported((int)n); }
 
 bool small_path(int64_t n) { return n <= 64; }
 
-// the one-launch mid-size path for square n (with a 16-byte aligned H,
-// which every torch / cudaMalloc allocation is)
-bool mid_path(int64_t n) { return fqr::mid_supported(n, n, nullptr); }
-
 std::atomic<int> g_debug_flags{0};
+std::atomic<int> g_debug_plan{0};  // 1: the one-launch mid-size kernel where it applies
+
+// The one-launch mid-size kernel (qr_mid.cu) is not in the static plan: the
+// blocked path measured faster at every batch size tried for 128 <= n <= 256
+// (B200, batch 1 .. 1024).  fqr_debug_plan(1) selects it (aligned H, which
+// every torch / cudaMalloc allocation is).
+bool mid_path(int64_t n) { return g_debug_plan.load() == 1 && fqr::mid_supported(n, n, nullptr); }
 
 int status_from(cudaError_t e)
 {
@@ -60,6 +63,10 @@ int status_from(cudaError_t e)
 extern "C" {
 
 int fqr_version(void) { return 100; }
+
+int fqr_debug_plan(int mode) { return g_debug_plan.exchange(mode == 1 ? 1 : 0); }
+
+int fqr::debug_flags() { return g_debug_flags.load(); }
 
 int fqr_debug_force_timeout(int enable)
 {
@@ -347,7 +354,7 @@ int run_geqrf(const float *A, int64_t batch, int64_t m, int64_t n, int64_t a_bst
     // the status block first, then the S blocks
     float *Sws = (float *)((unsigned char *)workspace + kWsAlign);
     int *status = status_word ? status_word : (int *)workspace;
-    if (m == n && fqr::mid_supported(m, n, H)) {
+    if (m == n && g_debug_plan.load() == 1 && fqr::mid_supported(m, n, H)) {
         // one launch; an own status word (host entry, one per chunk) or the
         // whole status block of the workspace
         if (tm) tm->begin(FQR_STAGE_MID);

@@ -125,6 +125,9 @@ cudaError_t launch_trailing64_tc(const TrailingMaps &maps, float *H, const float
 // failure path runs without any fault (a test hook).
 constexpr int kMidMaxN = 256;
 constexpr int kMidFlagForceTimeout = 1;
+// The process-wide test-hook flags (fqr_debug_force_timeout): the tensor-core
+// kernels make their first wait on a barrier that nothing completes.
+int debug_flags();
 constexpr int kMidFlagTmaCopy = 2;  // internal: A is read by TMA tiles (row-major, aligned)
 bool mid_supported(int64_t m, int64_t n, const void *H);
 cudaError_t launch_mid(const float *A, int64_t batch, int n, int64_t bs, int64_t rs, int64_t cs, float *H,

@@ -65,6 +65,10 @@ constexpr uint64_t kWaitLimit = 1000000000ull;  // 1 s of wall time per wait
 // kernel flags: trigger the next kernel's launch at the start of phase C
 // (else after it)
 constexpr int kFlagEarlyTrigger = 1;
+// test hook (fqr_debug_force_timeout): the first phase-A wait of every CTA is
+// made on a barrier that nothing completes, with a 2 ms limit, so that the
+// failure path (drain, status word) runs without any fault
+constexpr int kFlagForceTimeout = 2;
 
 // shared memory map (bytes, from a 1024-byte aligned base).  Phase A: a ring
 // of kStages chunks, each C^T (128 c x 32 r, 16 KB), V (32 j x 32 r, 4 KB)
@@ -79,10 +83,11 @@ constexpr int kLoadBytes = kCBytes + kVBytes;            // 20 KB arrive by TMA 
 constexpr int kStageBytes = kLoadBytes + kVBytes;        // 24 KB
 constexpr int kOffT = 96 * 1024;                         // S, column-major 32 x 32 (4 KB), after phase C's area
 constexpr int kOffTau = kOffT + 4096;                    // tau of the panel (128 B)
-constexpr int kOffBar = kOffTau + 128;  // mbarriers: full[3], mma[2], phase C; TMEM address
+constexpr int kOffBar = kOffTau + 128;  // mbarriers: full[4], mma[2], phase C, test hook; TMEM address at +64
 constexpr int kSmemUsed = kOffBar + 128;
 constexpr int kSmem = kSmemUsed + 1024;                  // + alignment slack: ~109 KB, 2 CTAs per SM
 static_assert(2 * (kSmem + 1024) <= 228 * 1024, "two CTAs per SM");
+static_assert((kStages + 4) * 8 <= 64, "mbarriers overlap the TMEM address slot");
 // Phase C (reuses the phase-A area): V chunk as the K-major A operand
 // (128 r x 32 j) and Y as the K-major B operand (128 c x 32 j), raw + lo, and
 // two -P quarters (128 rows x 32 columns; each warp's 32 rows a 4 KB slice,
@@ -222,6 +227,7 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + kOffBar);  // [kStages]
     uint64_t *mmab = full + kStages;                                // [2]
     uint64_t *cbar = full + kStages + 2;                            // phase-C MMA
+    uint64_t *never = full + kStages + 3;                           // the test hook's barrier
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kOffBar + 64);
     float *Ts = reinterpret_cast<float *>(smem + kOffT);    // S(l, c) at c * 32 + l
     float *taus = reinterpret_cast<float *>(smem + kOffTau);
@@ -237,7 +243,7 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
         tc::prefetch_tensormap(&tmC);
         tc::prefetch_tensormap(&tmV);
         tc::prefetch_tensormap(&tmCQ);
-        for (int i = 0; i < kStages + 3; ++i) tc::mbar_init(&full[i], 1);
+        for (int i = 0; i < kStages + 4; ++i) tc::mbar_init(&full[i], 1);
         tc::fence_mbar_init();
     }
     if (warp == 0) {
@@ -274,7 +280,9 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
     for (int i = 0; i < nchunks; ++i) {
         const int sidx = i % kStages, b = i & 1;
         unsigned char *st = smem + sidx * kStageBytes;
-        const bool landed = tc::mbar_wait(&full[sidx], (uint32_t)(i / kStages) & 1u, kWaitLimit);
+        const bool landed = (flags & kFlagForceTimeout) && i == 0
+                                ? tc::mbar_wait(never, 0u, 2000000ull)
+                                : tc::mbar_wait(&full[sidx], (uint32_t)(i / kStages) & 1u, kWaitLimit);
         // run by every thread (the TMEM stores are warp-collective); after a
         // wait that gave up it moves garbage that no MMA reads: the loop
         // ends at the barrier below
@@ -627,7 +635,10 @@ cudaError_t prepare_trailing_tc(float *H, int64_t batch, int m, int n, TrailingM
 
 // Static plan by n: a large launch triggers the next kernel early (its CTAs
 // are placed while the last wave finishes).
-static int trailing_flags(int ld) { return ld > 256 ? kFlagEarlyTrigger : 0; }
+static int trailing_flags(int ld)
+{
+    return (ld > 256 ? kFlagEarlyTrigger : 0) | ((debug_flags() & kMidFlagForceTimeout) ? kFlagForceTimeout : 0);
+}
 
 cudaError_t launch_apply_tc(const TrailingMaps &maps, const float *H, const float *Sws, int64_t s_stride,
                             const float *tau, int *status, int64_t batch, int ld, int hcols, int k, int c_begin,

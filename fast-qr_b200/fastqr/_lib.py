@@ -21,6 +21,7 @@ SIGNATURES = {
     "fqr_geqrf_f32_noalloc": (ctypes.c_int, [_p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p]),
     "fqr_noalloc_check_status": (ctypes.c_int, [_p]),
     "fqr_debug_force_timeout": (ctypes.c_int, [ctypes.c_int]),
+    "fqr_debug_plan": (ctypes.c_int, [ctypes.c_int]),
     "fqr_geqrf_f32_host": (ctypes.c_int, [_p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p,
                                           ctypes.c_size_t, _p]),
     "fqr_host_workspace_bytes": (ctypes.c_size_t, [_i64, _i64]),

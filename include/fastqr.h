@@ -218,16 +218,26 @@ int fqr_geqrf_rect_f32(const float *A, int64_t batch, int64_t m, int64_t n, int6
 int fqr_check_status(const void *workspace, size_t workspace_bytes, int64_t batch, void *stream);
 
 /*
- * Test hook for the failure path.  enable != 0: every later fqr_geqrf_f32 (and
- * noalloc / host / profile) call that takes the one-launch mid-size kernel
- * makes the first tensor-core wait of each matrix on a barrier that nothing
- * completes, with a 2 ms limit, so that the bounded-wait failure path runs
- * (copies and MMAs in flight drain, FQR_ETIMEOUT is recorded for
- * fqr_check_status) without any GPU fault.  enable == 0 restores normal
+ * Test hook for the failure path.  enable != 0: in every later call, each CTA
+ * of the rank-32 tensor-core trailing update (and of the one-launch mid-size
+ * kernel) makes its first wait on a barrier that nothing completes, with a
+ * 2 ms limit, so that the bounded-wait failure path runs (copies and MMAs in
+ * flight drain, FQR_ETIMEOUT is recorded for fqr_check_status) without any
+ * GPU fault.  enable == 0 restores normal
  * operation.  Process-wide; returns the previous setting.  No counterpart in
  * the reference, whose kernels have no device-side waits.
  */
 int fqr_debug_force_timeout(int enable);
+
+/*
+ * Diagnostic plan override, process-wide; returns the previous mode.
+ * mode 0: the static plan (default).  mode 1: square 128 <= n <= 256 with
+ * n % 4 == 0 run the one-launch mid-size kernel (one CTA per matrix runs its
+ * whole factorisation) instead of the blocked multi-launch path; that kernel
+ * measured slower than the blocked path at every batch size tried, so the
+ * static plan does not take it.  No counterpart in the reference.
+ */
+int fqr_debug_plan(int mode);
 
 /* Kernel classes timed by fqr_geqrf_f32_profile. */
 enum {

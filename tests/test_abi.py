@@ -61,19 +61,23 @@ def test_workspace_and_plan_depend_on_shape_only():
     assert fastqr.workspace_bytes(256, 256) == 256 * 32 * 32 * 4 + 256  # T factors + status
     assert fastqr.workspace_bytes(3, 100) % 256 == 0
     assert fastqr.plan(1024, 32).startswith("small")
-    # 128 <= n <= 256 with n % 4 == 0: the one-launch mid-size kernel
-    assert fastqr.plan(256, 256).startswith("mid")
-    assert fastqr.plan(3, 176).startswith("mid") and fastqr.plan(3, 130).startswith("blocked")
-    assert fastqr.plan(3, 100).startswith("blocked") and fastqr.plan(3, 260).startswith("blocked")
+    assert fastqr.plan(256, 256).startswith("blocked")
+    # the one-launch mid-size kernel only under the diagnostic override
+    lib = fastqr.load()
+    assert lib.fqr_debug_plan(1) == 0
+    try:
+        assert fastqr.plan(256, 256).startswith("mid") and fastqr.launch_count(256, 256) == 1
+        assert fastqr.plan(3, 176).startswith("mid") and fastqr.plan(3, 130).startswith("blocked")
+        assert fastqr.plan(3, 100).startswith("blocked") and fastqr.plan(3, 260).startswith("blocked")
+    finally:
+        assert lib.fqr_debug_plan(0) == 1
     assert "cluster 8" in fastqr.plan(16, 4096)
     with pytest.raises(fastqr.FastQRError):
         fastqr.plan(1, 10000)
     assert fastqr.launch_count(1024, 32) == 1
-    assert fastqr.launch_count(256, 256) == 1 and fastqr.launch_count(1, 128) == 1
-    # blocked: two parts of a batch on two streams, each copy-in + 16 panels
-    # + 15 trailing updates
-    assert fastqr.launch_count(256, 512) == 2 * (1 + 16 + 15)
-    assert fastqr.launch_count(1, 512) == 1 + 16 + 15
+    # two parts of a batch on two streams, each copy-in + 8 panels + 7 trailing
+    assert fastqr.launch_count(256, 256) == 2 * (1 + 8 + 7)
+    assert fastqr.launch_count(1, 256) == 1 + 8 + 7
     # n >= 2048: rank-64 blocks (panel, in-block update, panel, then Gram
     # block + trailing update for all but the last block); four parts for
     # n >= 2048: 32 blocks each

@@ -1,6 +1,8 @@
-"""GPU tests of the one-launch mid-size path (128 <= n <= 256, n % 4 == 0):
+"""GPU tests of the one-launch mid-size kernel (128 <= n <= 256, n % 4 == 0):
 one CTA per matrix runs the copy-in, every panel and every tensor-core
-trailing update of its matrix.
+trailing update of its matrix.  The static plan takes the blocked path for
+these sizes (measured faster); the module selects the kernel with the
+diagnostic override fqr_debug_plan(1) and restores the plan afterwards.
 
 Parity against the CPU oracle per column (1e-3 of float64 on well-conditioned
 inputs, the north star's tolerance) and the QR gates, at every n the path takes
@@ -23,11 +25,13 @@ COL_TOL = 1e-3
 FQR_ETIMEOUT = 4
 
 
-@pytest.fixture(scope="module")
+@pytest.fixture(scope="module", autouse=True)
 def dev():
     assert torch.cuda.is_available(), "GPU tests need a CUDA device"
-    fastqr.load()
-    return torch.device("cuda:0")
+    lib = fastqr.load()
+    lib.fqr_debug_plan(1)
+    yield torch.device("cuda:0")
+    lib.fqr_debug_plan(0)
 
 
 @pytest.mark.parametrize("n", [128, 132, 144, 160, 172, 176, 192, 196, 224, 228, 252, 256])
@@ -120,13 +124,23 @@ def test_mid_profile_reports_one_kernel(dev):
     assert st["mid"] > 0 and st["panel"] == 0 and st["trailing"] == 0 and st["copy_in"] == 0
 
 
-def test_bounded_wait_gives_up_and_reports_timeout(dev):
-    """The failure path, without a fault: the test hook makes every matrix's
-    first tensor-core wait use a barrier that nothing completes (2 ms limit).
-    The CTA then lets its copies in flight land, frees its tensor memory and
-    exits; fqr_check_status reports FQR_ETIMEOUT.  The next normal call clears
-    the status and is correct."""
+@pytest.mark.parametrize("plan", [1, 0])
+def test_bounded_wait_gives_up_and_reports_timeout(plan, dev):
+    """The failure path, without a fault: the test hook makes the first
+    tensor-core wait of every CTA use a barrier that nothing completes (2 ms
+    limit).  The CTA then lets its copies in flight land, frees its tensor
+    memory and exits; fqr_check_status reports FQR_ETIMEOUT.  The next normal
+    call clears the status and is correct.  plan 1: the one-launch kernel;
+    plan 0: the static plan (the blocked path's rank-32 tcgen05 update)."""
     lib = fastqr.load()
+    assert lib.fqr_debug_plan(plan) == 1
+    try:
+        _timeout_then_recover(lib, dev)
+    finally:
+        lib.fqr_debug_plan(1)
+
+
+def _timeout_then_recover(lib, dev):
     n, batch = 256, 4
     a = inputs.generate_input(batch, n, 0, 3, device=dev)
     h, t = fastqr.empty_outputs(batch, n, dev)
