@@ -60,13 +60,13 @@ int status_from(cudaError_t e)
 
 }  // namespace
 
+int fqr::debug_flags() { return g_debug_flags.load(); }
+
 extern "C" {
 
 int fqr_version(void) { return 100; }
 
 int fqr_debug_plan(int mode) { return g_debug_plan.exchange(mode == 1 ? 1 : 0); }
-
-int fqr::debug_flags() { return g_debug_flags.load(); }
 
 int fqr_debug_force_timeout(int enable)
 {
