@@ -5,11 +5,13 @@
 One step = one batched geqrf over the configuration's batch (per GPU), inputs
 resident in HBM, L2 flushed (256 MiB write) before every step.  The headline
 configuration is C2 (256 x 256^2, graded columns): BASELINE.json's configs[1].
-Multi-GPU (torchrun, one process per GPU): weak scaling, each rank factors a
-full configuration batch of its own (contiguous shard of a global batch of
-batch x N), no collective on the data path; time = max over ranks.
-``--strong`` splits the configuration's own batch over the ranks instead
-(C5 on 8 GPUs: 2 matrices per GPU).
+Multi-GPU (torchrun, one process per GPU): strong scaling by default -- the
+configuration's own batch is split into contiguous shards, north_star's
+partition (C5 on 8 GPUs: 2 matrices per GPU); no collective on the data path;
+time = max over ranks.  The line also carries the weak-scaling number (every
+rank a full configuration batch); ``--weak`` makes that the value.
+At N = 1 the line carries ``per_config`` (all five configurations measured in
+the same run) and ``gpu_baseline`` (torch.geqrf on CUDA, same inputs).
 
 Prints ONE JSON line on rank 0.  ``--impl reference`` times the reference's
 own CPU implementation of the path -- torch.geqrf on the host (its
@@ -249,7 +251,8 @@ def run_reference(args) -> int:
     line = {
         "impl": "reference", "metric": f"matrices/s ({args.config} geqrf)", "value": value,
         "unit": "matrices/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1e3 * batch / value, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": 1e3 * batch / value, "higher_is_better": True,
+        "scaling": "strong" if args.strong else "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": _config_block(args, world),
         "tflops": value * flops_per_matrix(n) / 1e12,
@@ -272,6 +275,85 @@ def _config_block(args, world) -> dict:
             "parallelism": f"batch-sharded x{world}, no collective"}
 
 
+PER_CONFIG_STEPS = {"C1": 100, "C2": 50, "C3": 10, "C4": 10, "C5": 3}
+
+
+def timed_steps(step, steps, flush, stream) -> float:
+    """Mean device milliseconds of `steps` calls of step() on `stream`, the L2
+    flushed (a 256 MiB write, outside the events) before each."""
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    for i in range(steps):
+        flush.fill_(float(i))
+        starts[i].record(stream)
+        step()
+        ends[i].record(stream)
+    torch.cuda.synchronize()
+    return sum(s_.elapsed_time(e_) for s_, e_ in zip(starts, ends)) / steps
+
+
+def torch_cuda_geqrf(a, flush, stream, budget_s: float = 20.0) -> dict:
+    """The GPU comparator: torch.geqrf on the same resident inputs on the GPU
+    (cuSOLVER / MAGMA through the torch build), timed like fastqr (device
+    events, L2 flushed).  A bounded sub-batch when the whole batch would take
+    long; the value is matrices/s of that sample."""
+    batch = a.shape[0]
+    torch.geqrf(a[:1])
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    torch.geqrf(a[:1])
+    torch.cuda.synchronize()
+    one = max(time.perf_counter() - t0, 1e-6)
+    sample = int(max(1, min(batch, (budget_s / 4.0) / one)))
+    x = a[:sample]
+    torch.geqrf(x)
+    ms = timed_steps(lambda: torch.geqrf(x), 3, flush, stream)
+    return {"value": sample / (ms / 1e3), "unit": "matrices/s", "impl": "torch.geqrf (CUDA)",
+            "ms_per_call": ms, "sample": f"{sample} of the {batch} matrices per call, mean of 3 calls"}
+
+
+def per_config_block(args, dev, flush, stream) -> dict:
+    """Every BASELINE configuration (C1..C5) measured in this run: device ms
+    per step (L2 flushed), matrices/s, TFLOP/s at 4n^3/3 flops per matrix,
+    the dominant kernel's roofline fraction, the QR gates on a few matrices,
+    and the torch.geqrf-on-CUDA comparator on the same inputs."""
+    import fastqr
+    from gpu_gates import gates
+
+    out = {}
+    for name in ("C1", "C2", "C3", "C4", "C5"):
+        cfg = inputs.CONFIGS[name]
+        n, batch = cfg["n"], cfg["batch"]
+        a = inputs.baseline_input(name, args.seed, dev)
+        h, tau = fastqr.empty_outputs(batch, n, dev)
+        ws = torch.empty(max(1, fastqr.workspace_bytes(batch, n)), dtype=torch.uint8, device=dev)
+
+        def step():
+            fastqr.geqrf(a, out=(h, tau), workspace=ws)
+
+        for _ in range(3):
+            step()
+        steps = PER_CONFIG_STEPS[name]
+        ms = timed_steps(step, steps, flush, stream)
+        chk = 2 if n >= 4096 else 4
+        g = gates(a[:chk], h[:chk], tau[:chk], chunk=chk)
+        roof = kernel_roofline(name, a, h, tau, ws, flush, min(steps, 3), dev)
+        mps = batch / (ms / 1e3)
+        row = {"n": n, "batch": batch, "steps": steps, "ms_per_step": ms, "matrices_per_s": mps,
+               "tflops": mps * flops_per_matrix(n) / 1e12, "hbm_gbs_alg": mps * bytes_per_matrix(n) / 1e9,
+               "dominant_kernel": roof["kernel"], "roofline_bound": roof["bound"],
+               "roofline_achieved": roof["achieved"], "roofline_unit": roof["unit"], "roofline_frac": roof["frac"],
+               "gpu_launches_per_step": fastqr.launch_count(batch, n), "verified": bool(g["ok"])}
+        if not args.no_gpu_baseline:
+            ref = torch_cuda_geqrf(a, flush, stream)
+            row["gpu_baseline"] = ref
+            row["vs_gpu_baseline"] = mps / ref["value"]
+        out[name] = row
+        del a, h, tau, ws
+        torch.cuda.empty_cache()
+    return out
+
+
 def run_fastqr(args) -> int:
     import torch.distributed as dist
 
@@ -288,9 +370,9 @@ def run_fastqr(args) -> int:
     n = cfg["n"]
     steps = args.steps
 
-    # weak scaling: every rank a full configuration batch; strong (--strong):
-    # the configuration's batch split into contiguous shards (C5 on 8 GPUs:
-    # 2 matrices per GPU)
+    # strong scaling (default): the configuration's batch split into
+    # contiguous shards, north_star's partition (C5 on 8 GPUs: 2 matrices per
+    # GPU); weak (--weak): every rank a full configuration batch
     a, first = rank_inputs(args.config, args.seed, world, rank, dev, weak=not args.strong)
     batch = a.shape[0]
     if batch < 1:
@@ -336,6 +418,28 @@ def run_fastqr(args) -> int:
     ms = total_ms / steps
     value = global_batch / (ms / 1e3)
 
+    # the other scaling mode beside it (N > 1): every rank a full batch when
+    # the line is strong, the configuration's batch split when it is weak
+    other = None
+    if world > 1:
+        a2, _ = rank_inputs(args.config, args.seed, world, rank, dev, weak=args.strong)
+        b2 = a2.shape[0]
+        h2, t2 = fastqr.empty_outputs(b2, n, dev)
+        ws2 = torch.empty(max(1, fastqr.workspace_bytes(b2, n)), dtype=torch.uint8, device=dev)
+
+        def step2():
+            fastqr.geqrf(a2, out=(h2, t2), workspace=ws2)
+
+        for _ in range(args.warmup):
+            step2()
+        dist.barrier()
+        torch.cuda.synchronize(dev)
+        ms2 = max_over_ranks(timed_steps(step2, steps, flush, stream), dev)
+        gb2 = world * b2 if args.strong else cfg["batch"]
+        other = {"scaling": "weak" if args.strong else "strong", "value": gb2 / (ms2 / 1e3),
+                 "ms_per_step": ms2, "global_batch": gb2, "batch_per_gpu": b2}
+        del a2, h2, t2, ws2
+
     # per-kernel times for the roofline: same steps again, kernels timed alone
     roof = kernel_roofline(args.config, a, h, tau, ws, flush, steps, dev)
 
@@ -343,6 +447,18 @@ def run_fastqr(args) -> int:
     e2e = end_to_end(a, n, batch, dev, max(3, min(steps, 50)))
     e2e_value = max_over_ranks(e2e["ms"], dev)
     e2e_mps = global_batch / (e2e_value / 1e3)
+
+    # the GPU comparator on the same inputs, and every configuration (N = 1)
+    gpu_ref = None
+    per_cfg = None
+    per_clk = None
+    if world == 1:
+        if not args.no_gpu_baseline:
+            gpu_ref = torch_cuda_geqrf(a, flush, stream)
+        if not args.no_per_config:
+            with ClockSampler(dev.index) as pclk:
+                per_cfg = per_config_block(args, dev, flush, stream)
+            per_clk = pclk.summary()
 
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu:
@@ -370,6 +486,14 @@ def run_fastqr(args) -> int:
             "plan": fastqr.plan(batch, n),
             "clocks": clk.summary(),
         }
+        if other is not None:
+            line["other_scaling"] = other
+        if gpu_ref is not None:
+            line["gpu_baseline"] = gpu_ref
+            line["vs_gpu_baseline"] = value / gpu_ref["value"]
+        if per_cfg is not None:
+            line["per_config"] = per_cfg
+            line["per_config_clocks"] = per_clk
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -676,8 +800,13 @@ def main() -> int:
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--strong", action="store_true",
-                    help="strong scaling: split the configuration's batch over the ranks "
-                         "(default: weak, every rank factors a full batch)")
+                    help="strong scaling (the default): split the configuration's batch over the ranks")
+    ap.add_argument("--weak", action="store_true",
+                    help="weak scaling: every rank factors a full configuration batch")
+    ap.add_argument("--no-per-config", action="store_true",
+                    help="skip the per_config block (all five configurations, N = 1)")
+    ap.add_argument("--no-gpu-baseline", action="store_true",
+                    help="skip the torch.geqrf-on-CUDA comparator")
     ap.add_argument("--cols", type=int, default=None,
                     help="--op rect: columns of the tall blocks (default 3/4 of n)")
     ap.add_argument("--op", default="geqrf", choices=["geqrf", "orgqr", "ormqr", "rect"],
@@ -687,6 +816,7 @@ def main() -> int:
     if args.steps is None:
         args.steps = DEFAULT_STEPS[args.config]
     args.warmup = max(args.warmup, 3)
+    args.strong = not args.weak
     if args.impl == "reference":
         return run_reference(args)
     if args.op == "rect":
