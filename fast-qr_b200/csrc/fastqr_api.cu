@@ -248,9 +248,12 @@ int enqueue_blocked(const float *A, int64_t batch, int64_t batch_all, int m, int
                 return status_from(e);
         }
     }
-    // rank-32 steps (the whole matrix, or the columns the rank-64 blocks left)
+    // rank-32 steps (the whole matrix, or the columns the rank-64 blocks
+    // left); a wide block (m < n) has m reflectors, and every trailing update
+    // also covers its columns m .. n-1
     const fqr::SBlock s32{Sws, s_stride, 1, fqr::kPanel};
-    for (; k < n; k += fqr::kPanel) {
+    const int kend = m < n ? m : n;
+    for (; k < kend; k += fqr::kPanel) {
         if (!step(FQR_STAGE_PANEL, [&] { return fqr::launch_panel(H, tau, s32, batch, m, n, k, st); }))
             return status_from(e);
         if (k + fqr::kPanel < n && !step(FQR_STAGE_TRAILING, [&] {
@@ -328,14 +331,15 @@ int enqueue_blocked_split(const float *A, int64_t batch, int m, int n, int64_t a
 // status_word: where the tensor-core kernels record a bounded wait that gave
 // up (NULL: the words after the S blocks in the workspace).  split: whether
 // a batch of two or more may run as two halves on two streams.
-// m: rows (m >= n; m == n for the square entry points).
+// m: rows (m == n for the square entry points; m < n, a wide block, only
+// through the rectangular entry, with tau [batch][n]).
 int run_geqrf(const float *A, int64_t batch, int64_t m, int64_t n, int64_t a_bstride, int64_t a_rstride,
               int64_t a_cstride, float *H, float *tau, void *workspace, size_t workspace_bytes,
               cudaStream_t st, StageTimer *tm, int *status_word = nullptr, bool split = true)
 {
     if (batch < 0 || n < 0 || m < 0) return FQR_EINVAL;
     if (batch == 0 || n == 0) return FQR_OK;
-    if (m > FQR_MAX_N || n > FQR_MAX_N || m < n) return FQR_EUNSUPPORTED;
+    if (m > FQR_MAX_N || n > FQR_MAX_N) return FQR_EUNSUPPORTED;
     if ((int64_t)m * n > (int64_t)FQR_MAX_N * FQR_MAX_N) return FQR_EUNSUPPORTED;
     if (!A || !H || !tau) return FQR_EINVAL;
     if (a_rstride == 0 || a_cstride == 0 || (batch > 1 && a_bstride == 0)) return FQR_EINVAL;
@@ -404,7 +408,7 @@ int fqr_geqrf_f32(const float *A, int64_t batch, int64_t n, int64_t a_bstride, i
 
 size_t fqr_geqrf_rect_workspace_bytes(int64_t batch, int64_t m, int64_t n)
 {
-    if (batch <= 0 || n <= 0 || m < n || m > FQR_MAX_N) return 0;
+    if (batch <= 0 || n <= 0 || m <= 0 || m > FQR_MAX_N || n > FQR_MAX_N) return 0;
     if (m == n) return fqr_workspace_bytes(batch, n);
     return fqr::ws_total_bytes(batch, m, n);
 }
@@ -413,8 +417,14 @@ int fqr_geqrf_rect_f32(const float *A, int64_t batch, int64_t m, int64_t n, int6
                        int64_t a_rstride, int64_t a_cstride, float *H, float *tau, void *workspace,
                        size_t workspace_bytes, void *stream)
 {
-    return run_geqrf(A, batch, m, n, a_bstride, a_rstride, a_cstride, H, tau, workspace, workspace_bytes,
-                     (cudaStream_t)stream, nullptr);
+    const int rc = run_geqrf(A, batch, m, n, a_bstride, a_rstride, a_cstride, H, tau, workspace,
+                             workspace_bytes, (cudaStream_t)stream, nullptr);
+    if (rc != FQR_OK || m >= n || batch <= 0 || m <= 0) return rc;
+    // a wide block has m reflectors: tau[b][m .. n-1] = 0
+    if (cudaMemset2DAsync(tau + m, (size_t)n * sizeof(float), 0, (size_t)(n - m) * sizeof(float), (size_t)batch,
+                          (cudaStream_t)stream) != cudaSuccess)
+        return FQR_ECUDA;
+    return FQR_OK;
 }
 
 int fqr_check_status(const void *workspace, size_t workspace_bytes, int64_t batch, void *stream)

@@ -219,4 +219,14 @@ int fqr_ormqr_f32(const float *H, const float *tau, int64_t batch, int64_t n, fl
                           (cudaStream_t)stream);
 }
 
+// C Q = (Q^T C^T)^T and C Q^T = (Q C^T)^T: a row-major mrows x n C is, read
+// column-major, the n x mrows matrix C^T, so the right-side product is the
+// left-side one on the same buffer with the transpose flag flipped.
+int fqr_ormqr_right_f32(const float *H, const float *tau, int64_t batch, int64_t n, float *C, int64_t mrows,
+                        int transpose, void *workspace, size_t workspace_bytes, void *stream)
+{
+    return fqr::run_apply(H, tau, batch, n, C, mrows, transpose ? 2 : 1, workspace, workspace_bytes,
+                          (cudaStream_t)stream);
+}
+
 }  // extern "C"

@@ -81,7 +81,7 @@ cudaError_t launch_trailing_tc(const TrailingMaps &maps, float *H, const float *
 // per-block chain of latency-bound kernels: at n = 512 and 1024 the step
 // was 5 to 7% slower, so smaller n keep rank-32 steps.
 constexpr int kOuter = 64;
-constexpr bool use_outer64(int64_t m, int64_t n) { return n >= 2048 && m <= 4096 && m % 4 == 0; }
+constexpr bool use_outer64(int64_t m, int64_t n) { return n >= 2048 && m >= n && m <= 4096 && m % 4 == 0; }
 
 // Workspace layout: a 256-byte status block (one int status word per part of
 // a split batch), then one S block per matrix: 32 x 32 floats (column-major)

@@ -33,6 +33,7 @@ SIGNATURES = {
     "fqr_orgqr_workspace_bytes": (ctypes.c_size_t, [_i64, _i64]),
     "fqr_orgqr_f32": (ctypes.c_int, [_p, _p, _i64, _i64, _p, _p, ctypes.c_size_t, _p]),
     "fqr_ormqr_f32": (ctypes.c_int, [_p, _p, _i64, _i64, _p, _i64, ctypes.c_int, _p, ctypes.c_size_t, _p]),
+    "fqr_ormqr_right_f32": (ctypes.c_int, [_p, _p, _i64, _i64, _p, _i64, ctypes.c_int, _p, ctypes.c_size_t, _p]),
     "fqr_check_status": (ctypes.c_int, [_p, ctypes.c_size_t, _i64, _p]),
     "fqr_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "fqr_plan_describe": (ctypes.c_int, [_i64, _i64, ctypes.c_char_p, ctypes.c_size_t]),

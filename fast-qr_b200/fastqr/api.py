@@ -31,8 +31,8 @@ def _check_input(a: torch.Tensor, square: bool = True) -> torch.Tensor:
         a = a.unsqueeze(0)
     if square and (a.ndim != 3 or a.shape[-1] != a.shape[-2]):
         raise ValueError(f"input must have shape (batch, n, n), got {tuple(a.shape)}")
-    if not square and (a.ndim != 3 or a.shape[-2] < a.shape[-1]):
-        raise ValueError(f"input must have shape (batch, m, n) with m >= n, got {tuple(a.shape)}")
+    if not square and a.ndim != 3:
+        raise ValueError(f"input must have shape (batch, m, n), got {tuple(a.shape)}")
     return a
 
 
@@ -67,29 +67,32 @@ def empty_outputs(batch: int, n: int, device) -> tuple[torch.Tensor, torch.Tenso
 def geqrf(a: torch.Tensor, *, out: tuple[torch.Tensor, torch.Tensor] | None = None,
           workspace: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
     """Batched Householder QR of float32 CUDA matrices, square (batch, n, n)
-    (``fqr_geqrf_f32``) or tall (batch, m, n) with m > n
+    (``fqr_geqrf_f32``), tall (batch, m, n) with m > n or wide with m < n
     (``fqr_geqrf_rect_f32``).
 
     Returns ``(H, tau)`` as torch.geqrf does: H (batch, m, n) column-major
-    (strides (m*n, 1, m)), tau (batch, n).  ``out`` may supply preallocated
-    outputs of that layout; ``workspace`` a uint8 CUDA tensor of at least
-    ``workspace_bytes(batch, n, m)`` bytes.  Wide inputs (m < n) raise.
+    (strides (m*n, 1, m)), tau (batch, min(m, n)).  ``out`` may supply
+    preallocated outputs of that layout; ``workspace`` a uint8 CUDA tensor of
+    at least ``workspace_bytes(batch, n, m)`` bytes.
     """
     squeeze = a.ndim == 2
     a = _check_input(a, square=False)
     batch, m, n = a.shape
+    k = min(m, n)
     lib = load()
     if out is None:
         h = torch.empty_strided((batch, m, n), (m * n, 1, m), device=a.device, dtype=torch.float32)
-        tau = torch.empty((batch, n), device=a.device, dtype=torch.float32)
+        tau = torch.empty((batch, k), device=a.device, dtype=torch.float32)
     else:
         h, tau = out
         if h.shape != (batch, m, n) or h.stride() != (m * n, 1, m) or h.dtype != torch.float32:
             raise ValueError("out H must be float32 (batch, m, n) with strides (m*n, 1, m)")
-        if tau.shape != (batch, n) or not tau.is_contiguous() or tau.dtype != torch.float32:
-            raise ValueError("out tau must be contiguous float32 (batch, n)")
+        if tau.shape != (batch, k) or not tau.is_contiguous() or tau.dtype != torch.float32:
+            raise ValueError("out tau must be contiguous float32 (batch, min(m, n))")
         if h.device != a.device or tau.device != a.device:
             raise ValueError("outputs must be on the input's device")
+    # a wide block's library call writes tau [batch][n] (the first m per row)
+    tau_lib = tau if m >= n else torch.empty((batch, n), device=a.device, dtype=torch.float32)
     need = workspace_bytes(batch, n, m)
     if need:
         if workspace is None:
@@ -106,10 +109,12 @@ def geqrf(a: torch.Tensor, *, out: tuple[torch.Tensor, torch.Tensor] | None = No
             rc = lib.fqr_geqrf_f32(a.data_ptr(), batch, n, bs, rs, cs, h.data_ptr(), tau.data_ptr(),
                                    ws_ptr, ws_len, stream)
         else:
-            rc = lib.fqr_geqrf_rect_f32(a.data_ptr(), batch, m, n, bs, rs, cs, h.data_ptr(), tau.data_ptr(),
+            rc = lib.fqr_geqrf_rect_f32(a.data_ptr(), batch, m, n, bs, rs, cs, h.data_ptr(), tau_lib.data_ptr(),
                                         ws_ptr, ws_len, stream)
     if rc:
         raise FastQRError(rc)
+    if tau_lib is not tau:
+        tau.copy_(tau_lib[:, :m])
     if squeeze:
         return h[0], tau[0]
     return h, tau
@@ -173,38 +178,49 @@ def householder_product(h: torch.Tensor, tau: torch.Tensor, *, out: torch.Tensor
     return q[0] if squeeze else q
 
 
-def ormqr(h: torch.Tensor, tau: torch.Tensor, c: torch.Tensor, *, transpose: bool = False,
+def ormqr(h: torch.Tensor, tau: torch.Tensor, c: torch.Tensor, *, left: bool = True, transpose: bool = False,
           out: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
-    """Q C (or Q^T C with ``transpose=True``) for the Q of geqrf's (H, tau), as
-    ``torch.ormqr(H, tau, C, left=True, transpose=transpose)`` for square
-    float32 CUDA batches (``fqr_ormqr_f32``).  C: (batch, n, ncols); the result
-    is a column-major tensor (``out`` when given: column-major, and C itself
-    for an in-place update)."""
+    """op(Q) C (``left=True``) or C op(Q) (``left=False``), op(Q) = Q or Q^T
+    with ``transpose=True``, for the Q of geqrf's square (H, tau), as
+    ``torch.ormqr(H, tau, C, left=left, transpose=transpose)`` for float32
+    CUDA batches.  Left: C (batch, n, ncols), the result column-major
+    (``fqr_ormqr_f32``).  Right: C (batch, mrows, n), the result row-major,
+    torch's default layout (``fqr_ormqr_right_f32``).  ``out`` when given must
+    have that layout (C itself for an in-place update)."""
     squeeze = h.ndim == 2
     h, tau = _check_factors(h, tau)
     batch, n, _ = h.shape
     if c.ndim == 2:
         c = c.unsqueeze(0)
-    if c.device != h.device or c.dtype != torch.float32 or c.ndim != 3 or c.shape[:2] != (batch, n):
-        raise ValueError("C must be a float32 (batch, n, ncols) tensor on H's device")
-    ncols = c.shape[2]
+    if c.device != h.device or c.dtype != torch.float32 or c.ndim != 3 or c.shape[0] != batch:
+        raise ValueError("C must be a float32 (batch, rows, cols) tensor on H's device")
+    if left:
+        if c.shape[1] != n:
+            raise ValueError("left: C must be (batch, n, ncols)")
+        other = c.shape[2]
+        shape, strides = (batch, n, other), (n * other, 1, n)
+    else:
+        if c.shape[2] != n:
+            raise ValueError("right: C must be (batch, mrows, n)")
+        other = c.shape[1]
+        shape, strides = (batch, other, n), (other * n, n, 1)
     if out is None:
-        out = torch.empty_strided((batch, n, ncols), (n * ncols, 1, n), device=c.device, dtype=torch.float32)
+        out = torch.empty_strided(shape, strides, device=c.device, dtype=torch.float32)
     else:
         out = out.unsqueeze(0) if out.ndim == 2 else out
-        if out.shape != (batch, n, ncols) or out.stride() != (n * ncols, 1, n) or out.dtype != torch.float32 \
-                or out.device != c.device:
-            raise ValueError("out must be float32 (batch, n, ncols) with strides (n*ncols, 1, n) on C's device")
+        if out.shape != shape or out.stride() != strides or out.dtype != torch.float32 or out.device != c.device:
+            raise ValueError(f"out must be float32 {shape} with strides {strides} on C's device")
     if out.data_ptr() != c.data_ptr():
         out.copy_(c)
     lib = load()
     ws_ptr, need = _apply_workspace(lib, batch, n, workspace, h.device)
+    fn, name = (lib.fqr_ormqr_f32, "fqr_ormqr_f32") if left else (lib.fqr_ormqr_right_f32, "fqr_ormqr_right_f32")
     with torch.cuda.device(h.device):
         stream = torch.cuda.current_stream(h.device).cuda_stream
-        rc = lib.fqr_ormqr_f32(h.data_ptr(), tau.data_ptr(), batch, n, out.data_ptr(), ncols,
-                               1 if transpose else 0, ws_ptr, need, stream)
+        rc = fn(h.data_ptr(), tau.data_ptr(), batch, n, out.data_ptr(), other, 1 if transpose else 0, ws_ptr, need,
+                stream)
     if rc:
-        raise FastQRError(rc, "fqr_ormqr_f32")
+        raise FastQRError(rc, name)
     return out[0] if squeeze else out
 
 

@@ -192,14 +192,29 @@ int fqr_ormqr_f32(const float *H, const float *tau, int64_t batch, int64_t n, fl
                   int transpose, void *workspace, size_t workspace_bytes, void *stream);
 
 /*
- * Rectangular batched QR, m >= n: torch.geqrf on [batch, m, n].  Replaces the
+ * C := C Q (transpose == 0) or C := C Q^T, in place, right side: torch.ormqr
+ * with left=False, which the reference's tail projection uses
+ * (submissions/candidate.py:7231).  C: batch x mrows x n, ROW-major per
+ * matrix (element (r, j) of matrix b at C[b*mrows*n + r*n + j], torch's
+ * default layout), device pointer; H, tau and workspace as for
+ * fqr_ormqr_f32.  (C read column-major is C^T, and C Q = (Q^T C^T)^T.)
+ */
+int fqr_ormqr_right_f32(const float *H, const float *tau, int64_t batch, int64_t n, float *C, int64_t mrows,
+                        int transpose, void *workspace, size_t workspace_bytes, void *stream);
+
+/*
+ * Rectangular batched QR: torch.geqrf on [batch, m, n].  Replaces the
  * reference's tall-block geqrf, torch.geqrf(data[:, :, :cols]) in
  * _embedded_rectangular_geqrf (submissions/candidate.py:7204-7214).
  *   A:   any strides, element (b, i, j) at A[b*a_bstride + i*a_rstride + j*a_cstride]
  *   H:   m x n column-major per matrix, H[b*m*n + j*m + i] (strides (m*n, 1, m))
- *   tau: [batch][n]
- * m == n is exactly fqr_geqrf_f32.  m < n returns FQR_EUNSUPPORTED.  Both
- * m and n are at most FQR_MAX_N.  The workspace is
+ *   tau: [batch][n]; a wide block (m < n) has min(m, n) = m reflectors,
+ *        tau[b][0 .. m-1], and tau[b][m .. n-1] is set to 0 (torch.geqrf
+ *        returns the first m)
+ * m == n is exactly fqr_geqrf_f32.  A wide block is factored like LAPACK
+ * xGEQRF: m reflectors from the first m columns, every trailing update also
+ * applied to columns m .. n-1 (which end as R's right part).  Both m and n
+ * are at most FQR_MAX_N.  The workspace is
  * fqr_geqrf_rect_workspace_bytes(batch, m, n) bytes, 256-byte aligned; the
  * status word for fqr_check_status sits in it as for fqr_geqrf_f32.
  */

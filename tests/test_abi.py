@@ -162,8 +162,10 @@ def test_orgqr_ormqr_validation_without_gpu():
 def test_rect_entry_validation_without_gpu():
     lib = fastqr.load()
     dummy = ctypes.c_void_p(16)
-    # wide matrices are not supported; sizes beyond the table neither
-    assert lib.fqr_geqrf_rect_f32(dummy, 1, 8, 16, 128, 16, 1, dummy, dummy, None, 0, None) == 2
+    # wide blocks (m < n) take the blocked path too: a workspace is required;
+    # sizes beyond the table are unsupported
+    assert lib.fqr_geqrf_rect_f32(dummy, 1, 8, 16, 128, 16, 1, dummy, dummy, None, 0, None) == 5
+    assert fastqr.workspace_bytes(4, 100, 20) == 4 * 32 * 32 * 4 + 256
     assert lib.fqr_geqrf_rect_f32(dummy, 1, 8193, 16, 8193 * 16, 16, 1, dummy, dummy, None, 0, None) == 2
     # null pointers, negative sizes, empty problems
     assert lib.fqr_geqrf_rect_f32(None, 2, 100, 20, 2000, 20, 1, None, None, None, 0, None) == 1
@@ -175,7 +177,7 @@ def test_rect_entry_validation_without_gpu():
     assert fastqr.workspace_bytes(4, 20, 100) == 4 * 32 * 32 * 4 + 256
     assert fastqr.workspace_bytes(4, 20, 20) == 0  # square n <= 64: the small path
     assert fastqr.workspace_bytes(4, 100, 100) == fastqr.workspace_bytes(4, 100)
-    assert lib.fqr_geqrf_rect_workspace_bytes(4, 10, 20) == 0
+    assert lib.fqr_geqrf_rect_workspace_bytes(4, 10, 20) == 4 * 32 * 32 * 4 + 256  # wide: blocked path
 
 
 def test_python_geqrf_rejects_wide_input():

@@ -123,3 +123,25 @@ def test_column_range_update_leaves_other_columns(dev):
     q64 = oracle.orgqr_f64(h.cpu().numpy(), tau.cpu().numpy())
     want = np.transpose(q64, (0, 2, 1)) @ c.cpu().double().numpy()
     assert frob(out.cpu().double().numpy() - want) / frob(want) <= 1e-5
+
+
+@pytest.mark.parametrize("n", [64, 100, 256, 384])
+@pytest.mark.parametrize("mrows", [1, 50, 256])
+@pytest.mark.parametrize("transpose", [False, True])
+def test_ormqr_right_side_matches_torch_float64(dev, n, mrows, transpose):
+    """C Q and C Q^T (torch.ormqr with left=False, the reference's tail
+    projection, submissions/candidate.py:7231) against float64 products with
+    Q from the same factors: 1e-5 relative (Frobenius), result row-major."""
+    a, h, tau = factor(2, n, 1, 300 + n + mrows, dev)
+    c = torch.randn(2, mrows, n, generator=torch.Generator().manual_seed(n + mrows)).to(dev)
+    out = fastqr.ormqr(h, tau, c, left=False, transpose=transpose)
+    assert out.shape == (2, mrows, n) and out.stride() == (mrows * n, n, 1)
+    q = torch.linalg.householder_product(h.double(), tau.double())
+    want = c.double() @ (q.transpose(1, 2) if transpose else q)
+    err = ((out.double() - want).flatten(1).norm(dim=1) / want.flatten(1).norm(dim=1)).max()
+    assert float(err) <= 1e-5, float(err)
+    # in place, and the round trip C Q Q^T = C
+    back = fastqr.ormqr(h, tau, out, left=False, transpose=not transpose, out=out)
+    assert back.data_ptr() == out.data_ptr()
+    rt = ((back.double() - c.double()).flatten(1).norm(dim=1) / c.double().flatten(1).norm(dim=1)).max()
+    assert float(rt) <= 1e-5, float(rt)

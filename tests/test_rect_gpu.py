@@ -109,3 +109,22 @@ def test_rect_embedded_route_shape(dev):
     # the leading columns of the square factorisation are the same reflectors
     hs, ts = fastqr.geqrf(a)
     assert float((hs[:, :, :cols] - h).abs().max()) <= 1e-4 * float(hs.abs().max())
+
+
+@pytest.mark.parametrize("m,n", [(20, 32), (96, 130), (128, 256), (200, 512), (256, 300)])
+def test_wide_blocks_match_lapack(m, n, dev):
+    """Wide blocks (m < n): LAPACK xGEQRF's result -- m reflectors from the
+    first m columns, the rest of R = Q^T A[:, m:] -- against float64 geqrf
+    (torch on the CPU, i.e. LAPACK): per column 1e-3 on H's reflector columns
+    and tau, and ||A - Q R||_F / ||A||_F <= 1e-4 with R the m x n upper part."""
+    a = inputs.generate_input(3, max(m, n), 1, 40 + m + n, device="cpu")[:, :m, :n].contiguous()
+    h, tau = fastqr.geqrf(a.to(dev))
+    torch.cuda.synchronize()
+    assert h.shape == (3, m, n) and h.stride() == (m * n, 1, m) and tau.shape == (3, m)
+    h64, t64 = torch.geqrf(a.double())
+    he, te = column_errors(h[:, :, :m].cpu(), tau.cpu(), h64[:, :, :m], t64)
+    assert float(he.max()) <= 1e-3 and float(te.max()) <= 1e-3, (float(he.max()), float(te.max()))
+    q = torch.linalg.householder_product(h[:, :, :m].double(), tau.double())
+    r = torch.triu(h.double())
+    rec = ((q @ r - a.double().to(dev)).flatten(1).norm(dim=1) / a.double().flatten(1).norm(dim=1).to(dev)).max()
+    assert float(rec) <= 1e-4, float(rec)
