@@ -16,6 +16,7 @@ import torch
 
 import fastqr
 import oracle
+from fastqr import inputs
 from gpu_gates import column_errors, gates
 
 pytestmark = pytest.mark.gpu
