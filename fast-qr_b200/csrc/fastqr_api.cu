@@ -256,10 +256,16 @@ int enqueue_blocked(const float *A, int64_t batch, int64_t batch_all, int m, int
     for (; k < kend; k += fqr::kPanel) {
         if (!step(FQR_STAGE_PANEL, [&] { return fqr::launch_panel(H, tau, s32, batch, m, n, k, st); }))
             return status_from(e);
-        if (k + fqr::kPanel < n && !step(FQR_STAGE_TRAILING, [&] {
-                return tc ? fqr::launch_trailing_tc(maps, H, Sws, s_stride, tau, status, batch, batch_all, m, n, k,
-                                                    st)
-                          : fqr::launch_trailing(H, Sws, s_stride, tau, batch, m, n, k, st);
+        // the panel's reflectors (fewer than 32 only in the last panel) reach
+        // every column right of them: k + 32 .. n-1, or, for the last panel of
+        // a wide block, k + m - k .. n-1
+        const int w = fqr::kPanel < m - k ? (fqr::kPanel < n - k ? fqr::kPanel : n - k) : (m - k < n - k ? m - k : n - k);
+        const int cb = k + w;
+        if (cb < n && !step(FQR_STAGE_TRAILING, [&] {
+                if (!tc) return fqr::launch_trailing(H, Sws, s_stride, tau, batch, m, n, k, cb, st);
+                if (w == fqr::kPanel)
+                    return fqr::launch_trailing_tc(maps, H, Sws, s_stride, tau, status, batch, batch_all, m, n, k, st);
+                return fqr::launch_apply_tc(maps, H, Sws, s_stride, tau, status, batch, m, n, k, cb, n, true, st);
             }))
             return status_from(e);
     }
@@ -417,14 +423,18 @@ int fqr_geqrf_rect_f32(const float *A, int64_t batch, int64_t m, int64_t n, int6
                        int64_t a_rstride, int64_t a_cstride, float *H, float *tau, void *workspace,
                        size_t workspace_bytes, void *stream)
 {
-    const int rc = run_geqrf(A, batch, m, n, a_bstride, a_rstride, a_cstride, H, tau, workspace,
-                             workspace_bytes, (cudaStream_t)stream, nullptr);
-    if (rc != FQR_OK || m >= n || batch <= 0 || m <= 0) return rc;
-    // a wide block has m reflectors: tau[b][m .. n-1] = 0
-    if (cudaMemset2DAsync(tau + m, (size_t)n * sizeof(float), 0, (size_t)(n - m) * sizeof(float), (size_t)batch,
+    // a wide block has m reflectors: tau[b][m .. n-1] = 0, set first (the
+    // updates read the tau of all 32 columns of the last panel), once the
+    // arguments have passed the checks run_geqrf makes
+    const bool wide = m > 0 && m < n && batch > 0 && n <= FQR_MAX_N;
+    if (wide && (!A || !H || !tau)) return FQR_EINVAL;
+    if (wide && (!workspace || workspace_bytes < fqr::ws_total_bytes(batch, m, n))) return FQR_EWORKSPACE;
+    if (wide &&
+        cudaMemset2DAsync(tau + m, (size_t)n * sizeof(float), 0, (size_t)(n - m) * sizeof(float), (size_t)batch,
                           (cudaStream_t)stream) != cudaSuccess)
         return FQR_ECUDA;
-    return FQR_OK;
+    return run_geqrf(A, batch, m, n, a_bstride, a_rstride, a_cstride, H, tau, workspace, workspace_bytes,
+                     (cudaStream_t)stream, nullptr);
 }
 
 int fqr_check_status(const void *workspace, size_t workspace_bytes, int64_t batch, void *stream)

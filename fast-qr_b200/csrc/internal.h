@@ -30,10 +30,11 @@ struct SBlock {
 };
 cudaError_t launch_panel(float *H, float *tau, const SBlock &sb, int64_t batch, int m, int n, int k,
                          cudaStream_t st);
-// SIMT fp32 trailing update (any m); S blocks (32 x 32, column-major) at
-// Sws + mat * s_stride.
+// SIMT fp32 trailing update (any m) of columns c_begin .. n-1 with the
+// reflectors of columns k .. k+31 (tau of the others 0); S blocks (32 x 32,
+// column-major) at Sws + mat * s_stride.
 cudaError_t launch_trailing(float *H, const float *Sws, int64_t s_stride, const float *tau, int64_t batch, int m,
-                            int n, int k, cudaStream_t st);
+                            int n, int k, int c_begin, cudaStream_t st);
 
 // Tensor-core (tcgen05, 3xTF32) trailing update; needs a row count m with
 // m % 4 == 0, m >= 128 and a 16-byte aligned H.  Sets *status to nonzero if a bounded wait gave up.

@@ -153,7 +153,7 @@ cudaError_t launch_copy_in(const float *A, int64_t batch, int m, int n, int64_t 
 __global__ void __launch_bounds__(256)
 trailing_simt_kernel(float *__restrict__ H, const float *__restrict__ Sws, int64_t s_stride,
                      const float *__restrict__ tau,
-                     int ld, int n, int k)
+                     int ld, int n, int k, int c_begin)
 {
     __shared__ float Vs[32][33];
     __shared__ float Cs[32][33];
@@ -161,7 +161,7 @@ trailing_simt_kernel(float *__restrict__ H, const float *__restrict__ Sws, int64
     __shared__ float Ts[32][33];
     const int lane = threadIdx.x & 31, tg = threadIdx.x >> 5;
     const int64_t mat = blockIdx.y;
-    const int c0 = k + kPanel + blockIdx.x * 32;
+    const int c0 = c_begin + blockIdx.x * 32;
     const int nct = (n - c0) < 32 ? (n - c0) : 32;
     const int m = ld - k;  // rows k .. ld-1 (ld = the matrix's row count)
     float *Hm = H + mat * (int64_t)ld * n;
@@ -245,9 +245,9 @@ trailing_simt_kernel(float *__restrict__ H, const float *__restrict__ Sws, int64
 }
 
 cudaError_t launch_trailing(float *H, const float *Sws, int64_t s_stride, const float *tau, int64_t batch, int m,
-                            int n, int k, cudaStream_t st)
+                            int n, int k, int c_begin, cudaStream_t st)
 {
-    const int nc = n - k - kPanel;
+    const int nc = n - c_begin;
     if (nc <= 0) return cudaSuccess;
     const unsigned tiles = (unsigned)((nc + 31) / 32);
     for (int64_t b0 = 0; b0 < batch; b0 += 65535) {
@@ -255,7 +255,7 @@ cudaError_t launch_trailing(float *H, const float *Sws, int64_t s_stride, const 
         dim3 grid(tiles, (unsigned)nb);
         cudaError_t e = launch_dependent(trailing_simt_kernel, grid, dim3(256), 0, st, nullptr, 0,
                                          H + b0 * (int64_t)m * n, Sws + b0 * s_stride, s_stride, tau + b0 * n,
-                                         m, n, k);
+                                         m, n, k, c_begin);
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;
