@@ -45,27 +45,28 @@ __device__ __forceinline__ void small_step(float (&a)[NC][NP], int k, int lane, 
     const int kl = k & 31;
     const bool owner = lane == kl;
     float x[W];
-    float s0 = 0.0f, s1 = 0.0f;
     float d0[NC], d1[NC];
-    bool anynz = false;
+    uint32_t nzbits = 0;  // OR of |x_i|'s bit patterns: 0 iff the tail is exactly zero
 #pragma unroll
     for (int c = 0; c < NC; ++c) d0[c] = d1[c] = 0.0f;
     const float alpha = __shfl_sync(kFull, a[S][0], kl);
 #pragma unroll
     for (int i = 1; i < W; ++i) {
         x[i] = __shfl_sync(kFull, a[S][i], kl);
-        anynz |= (x[i] != 0.0f);
+        nzbits |= __float_as_uint(x[i]) & 0x7fffffffu;
         if (i & 1) {
-            s0 = fmaf(x[i], x[i], s0);
 #pragma unroll
             for (int c = 0; c < NC; ++c) d0[c] = fmaf(x[i], a[c][i], d0[c]);
         } else {
-            s1 = fmaf(x[i], x[i], s1);
 #pragma unroll
             for (int c = 0; c < NC; ++c) d1[c] = fmaf(x[i], a[c][i], d1[c]);
         }
     }
-    const float sigma = s0 + s1;
+    const bool anynz = nzbits != 0;
+    // sigma = x^T x is the owner's own dot (its slot S holds column k, whose
+    // rows 1.. are x): the same FMAs in the same order, one shuffle instead of
+    // a second reduction in every lane
+    const float sigma = __shfl_sync(kFull, d0[S] + d1[S], kl);
     Reflector r = reflector_identity(alpha);
     bool fast = true;
     if (anynz) {
