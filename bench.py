@@ -115,36 +115,15 @@ def mid_plan(n: int, m: int | None = None) -> bool:
     return False
 
 
-def fused_panels(n: int, m: int | None = None, batch: int = 1) -> int:
-    """Rank-32 panels factored by the trailing update before them (the
-    library's static rule: the tensor-core path, a full 32-column panel, at
-    most 256 rows below the next panel, no 2-CTA row split of the update's
-    tiles -- which takes >= 256 rows and tiles x batch <= 148)."""
-    m = n if m is None else m
-    if not (m % 4 == 0 and m >= 128):
-        return 0
-    blocks, _ = plan_blocks(n, m)
-    cnt = 0
-    for k in range(64 * blocks, n, 32):
-        if k + 32 >= min(m, n) or m - k < 32 or n - k <= 32 or m - k - 32 > 256:
-            continue
-        tiles = -(-(n - k - 32) // 128)
-        if m - k >= 256 and tiles * batch <= 148:
-            continue
-        cnt += 1
-    return cnt
-
-
-def stage_launches(n: int, m: int | None = None, batch: int = 1) -> dict:
-    """Launches per kernel class of one factorisation (one stream; `batch`:
-    the call's batch, which decides the fused panels)."""
+def stage_launches(n: int, m: int | None = None) -> dict:
+    """Launches per kernel class of one factorisation (one stream)."""
     if mid_plan(n, m):
         return {"small": 0, "copy_in": 0, "panel": 0, "inblock": 0, "trailing": 0, "mid": 1}
     blocks, rest = plan_blocks(n, m)
     rp = -(-rest // 32)
     full = blocks if rest > 0 else max(blocks - 1, 0)
-    return {"small": 1, "copy_in": 1, "panel": 2 * blocks + rp - fused_panels(n, m, batch),
-            "inblock": blocks + full, "trailing": full + max(rp - 1, 0), "mid": 0}
+    return {"small": 1, "copy_in": 1, "panel": 2 * blocks + rp, "inblock": blocks + full,
+            "trailing": full + max(rp - 1, 0), "mid": 0}
 
 
 class ClockSampler:
@@ -547,7 +526,7 @@ def kernel_roofline(cfg_name, a, h, tau, ws, flush, steps, dev) -> dict:
     traffic = _traffic_from_profiles(cfg_name, dom)
     share = {kname: round(v / max(sum(per_step_ms.values()), 1e-12), 4) for kname, v in per_step_ms.items()}
     # launches of the dominant kernel class per profiled step (one stream)
-    per_step = stage_launches(n, batch=batch)[dom]
+    per_step = stage_launches(n)[dom]
     base = {"kernel": dom, "stage_ms_per_step": per_step_ms, "stage_share": share,
             "traffic": traffic, "launches_per_step": per_step, "peak_source": pk["source"]}
     if dom in ("small", "copy_in", "panel", "inblock", "mid"):
@@ -790,7 +769,7 @@ def run_rect_op(args) -> int:
                          f"median of {len(times)} reps"}
     # blocked path: per part of the batch (two, four for 2048+ columns) a
     # copy-in and the plan's panels, in-block steps and trailing updates
-    st = stage_launches(cols, m, batch)
+    st = stage_launches(cols, m)
     parts = min(batch, 4 if cols >= 2048 else 2)
     launches = parts * (st["copy_in"] + st["panel"] + st["inblock"] + st["trailing"])
     line = {

@@ -62,12 +62,6 @@ int status_from(cudaError_t e)
 
 int fqr::debug_flags() { return g_debug_flags.load(); }
 
-bool fqr::fuse_next_panel(bool tc, int64_t batch_all, int m, int n, int k)
-{
-    return tc && m - k >= fqr::kPanel && n - k > fqr::kPanel && m - k - fqr::kPanel <= 256 &&
-           !fqr::trailing_tc_split(batch_all, m, n, k);
-}
-
 extern "C" {
 
 int fqr_version(void) { return 100; }
@@ -117,14 +111,9 @@ int fqr_launch_count(int64_t batch, int64_t n)
     const int64_t blocks = outer ? n / fqr::kOuter : 0;
     const int64_t rest = n - blocks * fqr::kOuter;
     const int64_t panels = (rest + fqr::kPanel - 1) / fqr::kPanel;
-    // rank-32 panels that the trailing update before them factors (no launch
-    // of their own): the same static rule as the enqueue
-    int64_t fused = 0;
-    for (int64_t k = blocks * fqr::kOuter; k + fqr::kPanel < n; k += fqr::kPanel)
-        if (fqr::fuse_next_panel(use_tc(n), batch, (int)n, (int)n, (int)k)) ++fused;
-    auto range = [blocks, rest, panels, fused](int64_t b) {
+    auto range = [blocks, rest, panels](int64_t b) {
         const int64_t chunks = (b + 65534) / 65535;
-        int64_t t = 1 + panels - fused + (panels > 0 ? panels - 1 : 0) * chunks;
+        int64_t t = 1 + panels + (panels > 0 ? panels - 1 : 0) * chunks;
         if (blocks > 0) {
             const int64_t full = rest > 0 ? blocks : blocks - 1;  // blocks with a trailing update
             t += blocks * 3 + full * (1 + chunks);
@@ -262,31 +251,23 @@ int enqueue_blocked(const float *A, int64_t batch, int64_t batch_all, int m, int
     // rank-32 steps (the whole matrix, or the columns the rank-64 blocks
     // left); a wide block (m < n) has m reflectors, and every trailing update
     // also covers its columns m .. n-1
+    const fqr::SBlock s32{Sws, s_stride, 1, fqr::kPanel};
     const int kend = m < n ? m : n;
-    bool have_panel = false;  // the previous trailing launch factored panel k
     for (; k < kend; k += fqr::kPanel) {
-        float *Sk = Sws + ((k / fqr::kPanel) & 1) * fqr::kSBuf;       // this panel's S blocks
-        float *Sn = Sws + (((k / fqr::kPanel) + 1) & 1) * fqr::kSBuf;  // the next panel's
-        const fqr::SBlock s32{Sk, s_stride, 1, fqr::kPanel};
-        if (!have_panel &&
-            !step(FQR_STAGE_PANEL, [&] { return fqr::launch_panel(H, tau, s32, batch, m, n, k, st); }))
+        if (!step(FQR_STAGE_PANEL, [&] { return fqr::launch_panel(H, tau, s32, batch, m, n, k, st); }))
             return status_from(e);
-        have_panel = false;
         // the panel's reflectors (fewer than 32 only in the last panel) reach
         // every column right of them: k + 32 .. n-1, or, for the last panel of
         // a wide block, k + m - k .. n-1
         const int w = fqr::kPanel < m - k ? (fqr::kPanel < n - k ? fqr::kPanel : n - k) : (m - k < n - k ? m - k : n - k);
         const int cb = k + w;
-        const bool fuse = cb < n && k + fqr::kPanel < kend && fqr::fuse_next_panel(tc, batch_all, m, n, k);
         if (cb < n && !step(FQR_STAGE_TRAILING, [&] {
-                if (!tc) return fqr::launch_trailing(H, Sk, s_stride, tau, batch, m, n, k, cb, st);
+                if (!tc) return fqr::launch_trailing(H, Sws, s_stride, tau, batch, m, n, k, cb, st);
                 if (w == fqr::kPanel)
-                    return fqr::launch_trailing_tc(maps, H, Sk, s_stride, tau, status, batch, batch_all, m, n, k, st,
-                                                   fuse ? Sn : nullptr);
-                return fqr::launch_apply_tc(maps, H, Sk, s_stride, tau, status, batch, m, n, k, cb, n, true, st);
+                    return fqr::launch_trailing_tc(maps, H, Sws, s_stride, tau, status, batch, batch_all, m, n, k, st);
+                return fqr::launch_apply_tc(maps, H, Sws, s_stride, tau, status, batch, m, n, k, cb, n, true, st);
             }))
             return status_from(e);
-        have_panel = fuse;
     }
     return FQR_OK;
 }

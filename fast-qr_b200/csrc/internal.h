@@ -62,21 +62,15 @@ cudaError_t prepare_apply_maps(const float *H, int m, int hcols, float *C, int64
 // V = the unit-lower reflectors of columns k .. k+31 of H (fewer at the end;
 // H is m x hcols, tau hcols values per matrix),
 // T = D (I + S D)^-1 from S blocks at Sws + mat * s_stride (floats) and tau.
-// S_next (geqrf only, c_begin = k + 32, at most 256 rows below k + 32): the
-// CTA of the first tile then also factors the next panel (columns k+32 ..
-// k+63) into the S blocks at S_next (32 x 32, column-major, s_stride apart).
 cudaError_t launch_apply_tc(const TrailingMaps &maps, const float *H, const float *Sws, int64_t s_stride,
                             const float *tau, int *status, int64_t batch, int m, int hcols, int k,
-                            int c_begin, int c_end, bool apply_t, cudaStream_t st, float *S_next = nullptr);
-// Whether launch_trailing_tc runs the tile rows over 2-CTA clusters for this
-// call (then S_next must be null).
-bool trailing_tc_split(int64_t batch_all, int m, int n, int k);
+                            int c_begin, int c_end, bool apply_t, cudaStream_t st);
 // batch_all: the whole call's batch (the launch covers `batch` of them); the
 // static plan splits each tile's rows over two CTAs when the call's tiles
 // fit one CTA per SM.
 cudaError_t launch_trailing_tc(const TrailingMaps &maps, float *H, const float *Sws, int64_t s_stride,
                                const float *tau, int *status, int64_t batch, int64_t batch_all, int m, int n, int k,
-                               cudaStream_t st, float *S_next = nullptr);
+                               cudaStream_t st);
 
 // Rank-64 blocking (two 32-column panels per trailing update) for m x n
 // matrices with n >= 2048 and m <= 4096 (m % 4 == 0, the tensor-core
@@ -91,25 +85,15 @@ constexpr int kOuter = 64;
 constexpr bool use_outer64(int64_t m, int64_t n) { return n >= 2048 && m >= n && m <= 4096 && m % 4 == 0; }
 
 // Workspace layout: a 256-byte status block (one int status word per part of
-// a split batch), then one S area per matrix: two 32 x 32 float blocks
-// (column-major, by panel parity) for rank-32 plans, 64 x 64 floats
-// (row-major, S(l, c) at l * 64 + c) for rank-64 plans, whose rank-32 steps
-// after the blocks use the same two 32 x 32 slots at its start.  S = V^T V (strictly upper); the compact-WY T factor is
+// a split batch), then one S block per matrix: 32 x 32 floats (column-major)
+// for rank-32 plans, 64 x 64 floats (row-major, S(l, c) at l * 64 + c) for
+// rank-64 plans.  S = V^T V (strictly upper); the compact-WY T factor is
 // T = D (I + S D)^-1, D = diag(tau).
 constexpr size_t kWsAlign = 256;
-// Rank-32 steps keep two 32 x 32 S blocks per matrix, by panel parity (the
-// trailing update that factors the next panel writes its S while other CTAs
-// of the launch still read the current one), at kSBuf floats apart.
-constexpr int64_t kSBuf = kPanel * kPanel;
 constexpr int64_t s_block_floats(int64_t m, int64_t n)
 {
-    return use_outer64(m, n) ? kOuter * kOuter : 2 * kPanel * kPanel;
+    return use_outer64(m, n) ? kOuter * kOuter : kPanel * kPanel;
 }
-// Whether the rank-32 trailing update at column k also factors the next panel
-// (static: the tensor-core path, a full 32-column panel at k, a next panel of
-// at most 256 rows -- the 4-warp shape -- and no 2-CTA row split of the
-// update's tiles).
-bool fuse_next_panel(bool tc, int64_t batch_all, int m, int n, int k);
 constexpr size_t ws_t_bytes(int64_t batch, int64_t m, int64_t n)
 {
     return ((size_t)batch * (size_t)s_block_floats(m, n) * sizeof(float) + kWsAlign - 1) / kWsAlign * kWsAlign;

@@ -37,7 +37,6 @@
 
 #include "common.cuh"
 #include "internal.h"
-#include "panel_body.cuh"
 #include "tc.cuh"
 
 namespace cg = cooperative_groups;
@@ -70,9 +69,6 @@ constexpr int kFlagEarlyTrigger = 1;
 // made on a barrier that nothing completes, with a 2 ms limit, so that the
 // failure path (drain, status word) runs without any fault
 constexpr int kFlagForceTimeout = 2;
-// after its update, the CTA of the first tile (columns k+32 .. k+159, which
-// hold the next panel) factors the next panel: one launch fewer per step
-constexpr int kFlagNextPanel = 4;
 
 // shared memory map (bytes, from a 1024-byte aligned base).  Phase A: a ring
 // of kStages chunks, each C^T (128 c x 32 r, 16 KB), V (32 j x 32 r, 4 KB)
@@ -92,10 +88,6 @@ constexpr int kSmemUsed = kOffBar + 128;
 constexpr int kSmem = kSmemUsed + 1024;                  // + alignment slack: ~109 KB, 2 CTAs per SM
 static_assert(2 * (kSmem + 1024) <= 228 * 1024, "two CTAs per SM");
 static_assert((kStages + 4) * 8 <= 64, "mbarriers overlap the TMEM address slot");
-// with the fused next panel's static shared arrays (~6.2 KB) two CTAs must
-// still share an SM (228 KB, 1 KB reserved per CTA)
-static_assert(2 * (kSmem + 6400 + 1024) <= 228 * 1024, "two CTAs per SM with the fused panel");
-static_assert(4 * 32 * kStagePitch * 4 <= kOffT, "the fused panel's staging overlaps S");
 // Phase C (reuses the phase-A area): V chunk as the K-major A operand
 // (128 r x 32 j) and Y as the K-major B operand (128 c x 32 j), raw + lo, and
 // two -P quarters (128 rows x 32 columns; each warp's 32 rows a 4 KB slice,
@@ -204,7 +196,7 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
                    const __grid_constant__ CUtensorMap tmCQ, const float *__restrict__ H,
                    const float *__restrict__ Sws, int64_t s_stride, const float *__restrict__ tau,
                    int *__restrict__ status, int ld, int hcols, int k, int c_begin, int c_end, int64_t b0,
-                   int flags, int nsplit, int rows_per, float *__restrict__ Snext)
+                   int flags, int nsplit, int rows_per)
 {
     const bool early_trigger = flags & kFlagEarlyTrigger;
     extern __shared__ unsigned char smem_raw[];
@@ -564,22 +556,6 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
         tc::fence_after_sync();
         tc::tmem_dealloc(tmem, kTmemCols);
     }
-
-    // the next panel (kFlagNextPanel; at most 256 rows: the 4-warp panel
-    // shape): this CTA's reduce-adds have completed (each warp waited for
-    // its bulk groups above) and no other CTA of the launch writes columns
-    // k+32 .. k+63 or reads the next S block (S is double-buffered by panel
-    // parity); the next launch waits for this grid
-    if constexpr (ApplyT && !SPLIT) {
-        if ((flags & kFlagNextPanel) && blockIdx.x == 0 && ok) {
-            asm volatile("fence.proxy.async.global;" ::: "memory");
-            __syncthreads();
-            // the 4-warp, 2-row-block shape covers any panel of up to 256 rows
-            // (one instance: its static shared arrays keep two CTAs per SM)
-            panel_body<4, 2, false, false>(const_cast<float *>(H), const_cast<float *>(tau), Snext, s_stride, 1,
-                                           kPanel, ld, hcols, k + kPanel, mat, reinterpret_cast<float *>(smem));
-        }
-    }
 }
 
 bool trailing_tc_supported(int ld)
@@ -666,9 +642,8 @@ static int trailing_flags(int ld)
 
 cudaError_t launch_apply_tc(const TrailingMaps &maps, const float *H, const float *Sws, int64_t s_stride,
                             const float *tau, int *status, int64_t batch, int ld, int hcols, int k, int c_begin,
-                            int c_end, bool apply_t, cudaStream_t st, float *S_next)
+                            int c_end, bool apply_t, cudaStream_t st)
 {
-    if (S_next && (!apply_t || c_begin != k + kPanel || ld - k - kPanel > 256)) return cudaErrorInvalidValue;
     if (c_end <= c_begin || k >= hcols || k >= ld) return cudaSuccess;
     auto kern = apply_t ? trailing_tc_kernel<true> : trailing_tc_kernel<false>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
@@ -678,32 +653,25 @@ cudaError_t launch_apply_tc(const TrailingMaps &maps, const float *H, const floa
         const int64_t nb = (batch - b0) < 65535 ? (batch - b0) : 65535;
         dim3 grid(tiles, (unsigned)nb);
         e = launch_dependent(kern, grid, dim3(kThreads), kSmem, st, nullptr, 0, maps.c, maps.v, maps.cq, H, Sws,
-                             s_stride, tau, status, ld, hcols, k, c_begin, c_end, b0,
-                             trailing_flags(ld) | (S_next ? kFlagNextPanel : 0), 1, ld - k, S_next);
+                             s_stride, tau, status, ld, hcols, k, c_begin, c_end, b0, trailing_flags(ld), 1,
+                             ld - k);
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;
 }
 
-// Static plan by (the call's batch, n, k), as for the rank-64 update: when
-// all tiles of the call fit one CTA per SM, two CTAs (a cluster) share each
-// tile's rows.
-bool trailing_tc_split(int64_t batch_all, int m, int n, int k)
-{
-    const int64_t tiles = (n - k - kPanel + kTN - 1) / kTN;
-    return m - k >= 256 && tiles * batch_all <= 148;
-}
-
 cudaError_t launch_trailing_tc(const TrailingMaps &maps, float *H, const float *Sws, int64_t s_stride,
                                const float *tau, int *status, int64_t batch, int64_t batch_all, int m, int n, int k,
-                               cudaStream_t st, float *S_next)
+                               cudaStream_t st)
 {
     if (n - k - kPanel <= 0) return cudaSuccess;
+    // Static plan by (the call's batch, n, k), as for the rank-64 update:
+    // when all tiles of the call fit one CTA per SM, two CTAs (a cluster)
+    // share each tile's rows
     const int64_t tiles = (n - k - kPanel + kTN - 1) / kTN;
     const int rows = m - k;
-    if (!trailing_tc_split(batch_all, m, n, k))
-        return launch_apply_tc(maps, H, Sws, s_stride, tau, status, batch, m, n, k, k + kPanel, n, true, st, S_next);
-    if (S_next) return cudaErrorInvalidValue;  // the row-split variant does not factor the next panel
+    if (!(rows >= 256 && tiles * batch_all <= 148))
+        return launch_apply_tc(maps, H, Sws, s_stride, tau, status, batch, m, n, k, k + kPanel, n, true, st);
     constexpr int kSplit = 2;
     auto kern = trailing_tc_kernel<true, true>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
@@ -718,7 +686,7 @@ cudaError_t launch_trailing_tc(const TrailingMaps &maps, float *H, const float *
         const int64_t nb = (batch - b0) < 65535 ? (batch - b0) : 65535;
         e = launch_dependent(kern, dim3((unsigned)(tiles * kSplit), (unsigned)nb), dim3(kThreads), kSmem, st, attr,
                              1, maps.c, maps.v, maps.cq, H, Sws, s_stride, tau, status, m, n, k, k + kPanel, n, b0,
-                             trailing_flags(m), kSplit, rows_per, static_cast<float *>(nullptr));
+                             trailing_flags(m), kSplit, rows_per);
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;

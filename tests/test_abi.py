@@ -58,8 +58,7 @@ def test_argument_validation_without_gpu():
 
 def test_workspace_and_plan_depend_on_shape_only():
     assert fastqr.workspace_bytes(1024, 32) == 0
-    # status block, then two 32 x 32 S blocks per matrix (by panel parity)
-    assert fastqr.workspace_bytes(256, 256) == 256 * 2 * 32 * 32 * 4 + 256
+    assert fastqr.workspace_bytes(256, 256) == 256 * 32 * 32 * 4 + 256  # T factors + status
     assert fastqr.workspace_bytes(3, 100) % 256 == 0
     assert fastqr.plan(1024, 32).startswith("small")
     assert fastqr.plan(256, 256).startswith("blocked")
@@ -76,30 +75,25 @@ def test_workspace_and_plan_depend_on_shape_only():
     with pytest.raises(fastqr.FastQRError):
         fastqr.plan(1, 10000)
     assert fastqr.launch_count(1024, 32) == 1
-    # two parts of a batch on two streams, each copy-in + the first panel + 7
-    # trailing updates, each of which factors the next panel (rows <= 256)
-    assert fastqr.launch_count(256, 256) == 2 * (1 + 1 + 7)
-    # one matrix: the first update's tiles split over 2-CTA clusters (256
-    # rows, 2 tiles) and does not factor the second panel
-    assert fastqr.launch_count(1, 256) == 1 + 2 + 7
+    # two parts of a batch on two streams, each copy-in + 8 panels + 7 trailing
+    assert fastqr.launch_count(256, 256) == 2 * (1 + 8 + 7)
+    assert fastqr.launch_count(1, 256) == 1 + 8 + 7
     # n >= 2048: rank-64 blocks (panel, in-block update, panel, then Gram
     # block + trailing update for all but the last block); four parts for
     # n >= 2048: 32 blocks each
     assert "rank 64" in fastqr.plan(16, 4096) and "rank 32" in fastqr.plan(64, 1024)
     assert fastqr.launch_count(16, 2048) == 4 * (1 + 32 * 3 + 31 * 2)
     assert fastqr.launch_count(3, 2048) == 3 * (1 + 32 * 3 + 31 * 2)
-    # the updates at k >= 800 (fewer than 256 rows below the next panel, no
-    # row split) factor the next panel
-    assert fastqr.launch_count(64, 1024) == 2 * (1 + 32 - 6 + 31)
+    assert fastqr.launch_count(64, 1024) == 2 * (1 + 32 + 31)
     # 2100 = 32 blocks of 64 + a 32- and a 20-column panel (every block has a
     # trailing update, the first rank-32 panel too)
-    assert fastqr.launch_count(1, 2100) == 1 + 32 * 3 + 32 * 2 + 2 + 1 - 1
+    assert fastqr.launch_count(1, 2100) == 1 + 32 * 3 + 32 * 2 + 2 + 1
     # rows above 4096: rank-32 steps only
-    assert fastqr.launch_count(1, 8192) == 1 + 256 - 6 + 255
+    assert fastqr.launch_count(1, 8192) == 1 + 256 + 255
     # a status block, then one S block per matrix (64 x 64 for rank-64 plans)
     assert fastqr.workspace_bytes(16, 4096) == 256 + 16 * 64 * 64 * 4
-    assert fastqr.workspace_bytes(64, 1024) == 256 + 64 * 2 * 32 * 32 * 4
-    assert fastqr.workspace_bytes(2, 8192) == 256 + 2 * 2 * 32 * 32 * 4
+    assert fastqr.workspace_bytes(64, 1024) == 256 + 64 * 32 * 32 * 4
+    assert fastqr.workspace_bytes(2, 8192) == 256 + 2 * 32 * 32 * 4
 
 
 def test_python_api_rejects_cpu_tensors():
@@ -171,7 +165,7 @@ def test_rect_entry_validation_without_gpu():
     # wide blocks (m < n) take the blocked path too: a workspace is required;
     # sizes beyond the table are unsupported
     assert lib.fqr_geqrf_rect_f32(dummy, 1, 8, 16, 128, 16, 1, dummy, dummy, None, 0, None) == 5
-    assert fastqr.workspace_bytes(4, 100, 20) == 4 * 2 * 32 * 32 * 4 + 256
+    assert fastqr.workspace_bytes(4, 100, 20) == 4 * 32 * 32 * 4 + 256
     assert lib.fqr_geqrf_rect_f32(dummy, 1, 8193, 16, 8193 * 16, 16, 1, dummy, dummy, None, 0, None) == 2
     # null pointers, negative sizes, empty problems
     assert lib.fqr_geqrf_rect_f32(None, 2, 100, 20, 2000, 20, 1, None, None, None, 0, None) == 1
@@ -180,10 +174,10 @@ def test_rect_entry_validation_without_gpu():
     # tall matrices always take the blocked path: a workspace is required,
     # even for n <= 64
     assert lib.fqr_geqrf_rect_f32(dummy, 1, 100, 20, 2000, 20, 1, dummy, dummy, None, 0, None) == 5
-    assert fastqr.workspace_bytes(4, 20, 100) == 4 * 2 * 32 * 32 * 4 + 256
+    assert fastqr.workspace_bytes(4, 20, 100) == 4 * 32 * 32 * 4 + 256
     assert fastqr.workspace_bytes(4, 20, 20) == 0  # square n <= 64: the small path
     assert fastqr.workspace_bytes(4, 100, 100) == fastqr.workspace_bytes(4, 100)
-    assert lib.fqr_geqrf_rect_workspace_bytes(4, 10, 20) == 4 * 2 * 32 * 32 * 4 + 256  # wide: blocked path
+    assert lib.fqr_geqrf_rect_workspace_bytes(4, 10, 20) == 4 * 32 * 32 * 4 + 256  # wide: blocked path
 
 
 def test_python_geqrf_rejects_wide_input():
