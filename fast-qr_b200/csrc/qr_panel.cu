@@ -383,8 +383,10 @@ cudaError_t launch_panel(float *H, float *tau, const SBlock &sb, int64_t batch, 
     const PanelShape s = panel_shape(ld - k);
     if (s.cluster > 8) return cudaErrorInvalidValue;
     if (s.warps == 4 && s.rows_per_thread_blocks == 1)
-        return launch_panel_t<4, 1>(H, tau, sb, batch, ld, n, k, 1, st);
-    if (s.warps == 4) return launch_panel_t<4, 2>(H, tau, sb, batch, ld, n, k, 1, st);
+        return launch_panel_t<4, 1>(H, tau, sb, batch, ld, n, k, s.cluster, st);
+    if (s.warps == 4) return launch_panel_t<4, 2>(H, tau, sb, batch, ld, n, k, s.cluster, st);
+    if (s.warps == 8 && s.rows_per_thread_blocks == 1)
+        return launch_panel_t<8, 1>(H, tau, sb, batch, ld, n, k, s.cluster, st);
     if (s.warps == 8) return launch_panel_t<8, 2>(H, tau, sb, batch, ld, n, k, s.cluster, st);
     return launch_panel_t<16, 2>(H, tau, sb, batch, ld, n, k, s.cluster, st);
 }

@@ -120,17 +120,17 @@ def test_host_entry_validation_without_gpu():
 
 
 def test_host_workspace_plan():
-    # one staging slot per chunk, at most 16 chunks, each >= 1 MiB of input
-    # or 1/16 of the batch; sizes depend on (batch, n) only
+    # at most 16 staging slots, each holding one body chunk (>= 1 MiB of input
+    # or 1/16 of the batch; the two edge chunks are smaller); sizes depend on
+    # (batch, n) only
     for batch, n in [(1024, 32), (256, 256), (512, 512), (64, 1024), (16, 4096), (1, 8), (3, 100)]:
         mat = n * n * 4
         need = fastqr.host_workspace_bytes(batch, n)
         assert need % 256 == 0
         assert need >= 2 * mat  # at least one A and one H staging block
-        # about the batch's own size twice (A and H staging), rounded per chunk
-        chunks = min(16, batch)
-        per = -(-batch // chunks)
-        assert need <= 256 + chunks * (per * (2 * mat + n * 4) + fastqr.workspace_bytes(per, n) + 1024)
+        # about the batch's own size twice (A and H staging), at most 1.5x with
+        # the slots rounded per chunk, plus per-slot S blocks
+        assert need <= 256 + 1.5 * batch * (2 * mat + n * 4) + 16 * (fastqr.workspace_bytes(batch, n) + 1024)
     # C2: 16 chunks of 16 matrices, one slot each of (A + H + tau + S blocks)
     slot = 2 * 16 * 256 * 256 * 4 + 16 * 256 * 4 + fastqr.workspace_bytes(16, 256)
     assert fastqr.host_workspace_bytes(256, 256) == 256 + 16 * slot
