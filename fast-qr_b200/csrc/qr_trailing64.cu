@@ -74,8 +74,9 @@ constexpr int kCQCols = 32;
 constexpr int kCQBytes = kRCC * kCQCols * 4;  // 16 KB: 4 warps x 4 KB
 static_assert(kOffCQ + 2 * kCQBytes <= kOffTau, "phase-C buffers overlap tau");
 static_assert(kR * kR * 4 <= 2 * kCQBytes, "S does not fit the -P area");
-constexpr int kMaxSplit = 2;  // W exchange slots (32 KB each) below the S area
-static_assert(kMaxSplit * kR * kThreads * 4 <= kOffCQ, "W exchange slots overlap S");
+constexpr int kMaxSplit = 8;                        // cluster ranks per tile at most (a power of two)
+constexpr int kXchgBytes = kR * kThreads * 4;       // 32 KB: one W part, any nsplit
+static_assert(2 * kXchgBytes <= kOffCQ, "W exchange areas overlap S");
 static_assert(kStageBytes % 1024 == 0 && kCBytes % 1024 == 0 && kVBytes % 1024 == 0, "1024-byte atoms");
 
 constexpr uint32_t kIdescA = tc::idesc_tf32(128, 128, 0, 0);  // A = C_hi^T (smem), B = [V | V_lo]
@@ -309,40 +310,60 @@ trailing64_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constant
     };
     if constexpr (SPLIT) {
         if (ok) read_w();
-        // the cluster's W parts, summed in rank order in every CTA: slot
-        // `rank` of each CTA's exchange area ([j / 4][thread][4] floats, 32 KB
-        // per rank, in the phase-A ring).  Every CTA passes both cluster
-        // barriers, whatever its `ok` (a CTA whose wait gave up has set the
-        // status word; the call's results are then reported invalid)
+        // The cluster's W parts are summed by a reduce-scatter and an
+        // all-gather over distributed shared memory: rank r owns the slice of
+        // q = 64 / nsplit reflector columns [r q, r q + q).  Every rank writes
+        // slice r of its part into rank r's area A (slot = source rank), each
+        // rank sums its slice over the sources in rank order, then writes the
+        // sum into every rank's area B (slot = owner rank).  So all ranks hold
+        // bitwise the same W, and 64 KB serve any nsplit (2, 4 or 8): area A
+        // and B are nsplit x q x 128 threads floats each.  Both lie in the
+        // phase-A ring.  Every CTA passes all three cluster barriers, whatever
+        // its `ok` (a CTA whose wait gave up has set the status word; the
+        // call's results are then reported invalid).
         cg::cluster_group cl = cg::this_cluster();
-        float *xb = reinterpret_cast<float *>(smem);
+        const int q = kR / nsplit;  // 32, 16 or 8 floats per slice
+        float *xa = reinterpret_cast<float *>(smem);               // [src][q / 4][thread][4]
+        float *xg = reinterpret_cast<float *>(smem + kXchgBytes);  // [owner][q / 4][thread][4]
         cl.sync();  // every CTA of the cluster is done with its ring
         if (ok) {
-            for (int rk = 0; rk < nsplit; ++rk) {
-                float *dst = cl.map_shared_rank(xb, rk) + half * (kR * kThreads);
+            // register indices stay compile-time constants (a[] in registers);
+            // only the destination rank and offset are computed
 #pragma unroll
-                for (int j4 = 0; j4 < kR / 4; ++j4)
-                    *reinterpret_cast<float4 *>(dst + (j4 * kThreads + tid) * 4) =
-                        make_float4(a[4 * j4], a[4 * j4 + 1], a[4 * j4 + 2], a[4 * j4 + 3]);
+            for (int j4 = 0; j4 < kR / 4; ++j4) {
+                const int j = 4 * j4, own = j / q, jq = (j - own * q) / 4;
+                *reinterpret_cast<float4 *>(cl.map_shared_rank(xa, own) + half * (q * kThreads) +
+                                            (jq * kThreads + tid) * 4) = make_float4(a[j], a[j + 1], a[j + 2], a[j + 3]);
+            }
+        }
+        cl.sync();
+        if (ok) {
+            for (int j4 = 0; j4 < q / 4; ++j4) {
+                float4 sum = *reinterpret_cast<const float4 *>(xa + (j4 * kThreads + tid) * 4);
+                for (int rk = 1; rk < nsplit; ++rk) {
+                    const float4 v =
+                        *reinterpret_cast<const float4 *>(xa + rk * (q * kThreads) + (j4 * kThreads + tid) * 4);
+                    sum.x += v.x;
+                    sum.y += v.y;
+                    sum.z += v.z;
+                    sum.w += v.w;
+                }
+                for (int rk = 0; rk < nsplit; ++rk)
+                    *reinterpret_cast<float4 *>(cl.map_shared_rank(xg, rk) + half * (q * kThreads) +
+                                                (j4 * kThreads + tid) * 4) = sum;
             }
         }
         cl.sync();
         if (ok) {
 #pragma unroll
             for (int j4 = 0; j4 < kR / 4; ++j4) {
-                float4 sum = *reinterpret_cast<const float4 *>(xb + (j4 * kThreads + tid) * 4);
-                for (int rk = 1; rk < nsplit; ++rk) {
-                    const float4 v = *reinterpret_cast<const float4 *>(xb + rk * (kR * kThreads) +
-                                                                        (j4 * kThreads + tid) * 4);
-                    sum.x += v.x;
-                    sum.y += v.y;
-                    sum.z += v.z;
-                    sum.w += v.w;
-                }
-                a[4 * j4] = sum.x;
-                a[4 * j4 + 1] = sum.y;
-                a[4 * j4 + 2] = sum.z;
-                a[4 * j4 + 3] = sum.w;
+                // column 4 j4 lives in owner j / q's slot, at float4 (j mod q) / 4
+                const int j = 4 * j4, own = j / q, jq = (j - own * q) / 4;
+                const float4 v = *reinterpret_cast<const float4 *>(xg + own * (q * kThreads) + (jq * kThreads + tid) * 4);
+                a[j] = v.x;
+                a[j + 1] = v.y;
+                a[j + 2] = v.z;
+                a[j + 3] = v.w;
             }
         }
     }
@@ -498,13 +519,23 @@ trailing64_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constant
 
 // Static plan by (the call's batch, n, k): when all tiles of the call fit
 // one CTA per SM (few large matrices, or the late blocks of a larger batch),
-// each tile's rows are split over a cluster of two CTAs, halving the per-CTA
-// chain of row chunks at the cost of a W exchange and a second copy of
-// phase B; otherwise one CTA per tile.  Measured at n = 4096: one matrix
-// -19%, two -18%, 16 -0.6%.
+// each tile's rows are split over a cluster of 2, 4 or 8 CTAs: the largest
+// split that still fits two CTAs per SM (296 on 148 SMs) and leaves each rank
+// >= 256 rows.  That shortens the per-CTA chain of row chunks, at the cost of
+// the W exchange and of phase B run in every rank.  Otherwise one CTA per
+// tile.  Measured at n = 4096 (ms per call): one matrix 14.75 -> 11.96 (two
+// ranks) -> 10.14 (up to eight), two 16.75 -> 13.50 -> 12.03, four 19.4 ->
+// 16.05 -> 15.65; 16 matrices unchanged.  Splitting the many-tile case too (to
+// keep the tiles in flight L2-resident for phase C's re-read) was slower:
+// 16 matrices 26.6 -> 32.2 ms (1024-row ranks), 36.9 ms (512-row ranks).
 static int trailing64_split(int64_t batch_all, int64_t tiles, int rows)
 {
-    return (rows >= 256 && tiles * batch_all <= 148) ? kMaxSplit : 1;
+    if (rows < 256 || tiles * batch_all > 148) return 1;
+    int ns = 2;
+    while (ns < kMaxSplit && tiles * batch_all * ns * 2 <= 296 && rows >= ns * 2 * 256) ns *= 2;
+    // every rank must own at least one row (rows per rank: a multiple of 128)
+    while (ns > 1 && (int64_t)(ns - 1) * ((rows + ns * kRCC - 1) / (ns * kRCC) * kRCC) >= rows) ns /= 2;
+    return ns;
 }
 
 cudaError_t launch_trailing64_tc(const TrailingMaps &maps, float *H, const float *S64, int64_t s_stride,

@@ -224,6 +224,20 @@ def test_config_c5(dev):
     assert float(he.max()) <= COL_TOL and float(te.max()) <= COL_TOL, (float(he.max()), float(te.max()))
 
 
+def test_c5_shard_of_eight_gpus(dev):
+    """C5 over 8 GPUs leaves 2 matrices per GPU. The rank-64 update then
+    splits each tile's rows over clusters of 4 CTAs (8 in the later blocks),
+    with W summed by a reduce-scatter and an all-gather over distributed
+    shared memory. Checks H and tau per column against float64 geqrf, plus
+    the QR gates."""
+    a = inputs.baseline_input("C5", seed=0, device=dev, batch=2, first=14)
+    h, t = fastqr.geqrf(a)
+    assert gates(a, h, t, chunk=1)["ok"]
+    h64, t64 = torch.geqrf(a.double())
+    he, te = column_errors(h, t, h64, t64)
+    assert float(he.max()) <= COL_TOL and float(te.max()) <= COL_TOL, (float(he.max()), float(te.max()))
+
+
 @pytest.mark.parametrize("n,batch", [(1024, 2), (2048, 1), (1500, 1)])
 def test_large_n_properties(n, batch, dev):
     a = inputs.generate_input(batch, n, 2, 31 + n, device=dev)
