@@ -100,6 +100,9 @@ constexpr int kOffCQ = 65536;
 constexpr int kCQCols = 32;
 constexpr int kCQBytes = kRCC * kCQCols * 4;  // 16 KB
 static_assert(kOffCQ + 2 * kCQBytes <= kOffT, "phase-C buffers overlap S");
+constexpr int kMaxSplit = 8;                     // cluster ranks per tile at most (a power of two)
+constexpr int kXchgBytes = kPanel * kThreads * 4;  // 16 KB: one W part, any split
+static_assert(kOffCQ + 2 * kXchgBytes <= kOffT, "W exchange areas overlap S");
 static_assert(2 * 32 * kThreads * 4 <= 2 * kCQBytes, "two W exchange slots exceed the -P area");
 static_assert(kStages * kStageBytes <= kOffT, "phase-A ring overlaps S");
 static_assert(kStageBytes % 1024 == 0 && kCBytes % 1024 == 0, "swizzle atoms need 1024-byte alignment");
@@ -369,44 +372,65 @@ trailing_tc_kernel(const __grid_constant__ CUtensorMap tmC, const __grid_constan
     };
     float wsum[32];
     if constexpr (SPLIT) {
-        // the cluster's W parts, summed in rank order in every CTA: slot
-        // `rank` of each CTA's -P staging area ([j / 4][thread][4] floats,
-        // 16 KB per rank; phase C uses the area only later).  Every CTA
-        // passes both cluster barriers, whatever its `ok` (a CTA whose wait
-        // gave up has set the status word; the results are reported invalid)
+        // The cluster's W parts are summed by a reduce-scatter and an
+        // all-gather over distributed shared memory: rank r owns the slice of
+        // q = 32 / nsplit columns [r q, r q + q).  Every rank writes slice r of
+        // its part into rank r's area A (slot = source rank), each rank sums
+        // its slice over the sources in rank order and writes the sum into
+        // every rank's area B (slot = owner rank), so all ranks hold bitwise
+        // the same W.  Areas A and B (16 KB each, any nsplit of 2, 4 or 8) lie
+        // in the -P staging area, which phase C uses only later.  Every CTA
+        // passes all three cluster barriers, whatever its `ok` (a CTA whose
+        // wait gave up has set the status word; the results are reported
+        // invalid).
         if (ok) {
             tc::fence_after_sync();
             read_w(wsum);
         }
         cg::cluster_group cl = cg::this_cluster();
-        float *xb = reinterpret_cast<float *>(smem + kOffCQ);
+        const int q = kPanel / nsplit;  // 16, 8 or 4 floats per slice
+        float *xa = reinterpret_cast<float *>(smem + kOffCQ);                // [src][q / 4][thread][4]
+        float *xg = reinterpret_cast<float *>(smem + kOffCQ + kXchgBytes);   // [owner][q / 4][thread][4]
         cl.sync();  // every CTA of the cluster is done with its phase-A ring
         if (ok) {
-            for (int rk = 0; rk < nsplit; ++rk) {
-                float *dst = cl.map_shared_rank(xb, rk) + half * (32 * kThreads);
+            // register indices stay compile-time constants; only the
+            // destination rank and offset are computed
 #pragma unroll
-                for (int j4 = 0; j4 < 8; ++j4)
-                    *reinterpret_cast<float4 *>(dst + (j4 * kThreads + tid) * 4) =
-                        make_float4(wsum[4 * j4], wsum[4 * j4 + 1], wsum[4 * j4 + 2], wsum[4 * j4 + 3]);
+            for (int j4 = 0; j4 < kPanel / 4; ++j4) {
+                const int j = 4 * j4, own = j / q, jq = (j - own * q) / 4;
+                *reinterpret_cast<float4 *>(cl.map_shared_rank(xa, own) + half * (q * kThreads) +
+                                            (jq * kThreads + tid) * 4) =
+                    make_float4(wsum[j], wsum[j + 1], wsum[j + 2], wsum[j + 3]);
             }
         }
         cl.sync();
         if (ok) {
-#pragma unroll
-            for (int j4 = 0; j4 < 8; ++j4) {
-                float4 t = *reinterpret_cast<const float4 *>(xb + (j4 * kThreads + tid) * 4);
+            for (int j4 = 0; j4 < q / 4; ++j4) {
+                float4 t = *reinterpret_cast<const float4 *>(xa + (j4 * kThreads + tid) * 4);
                 for (int rk = 1; rk < nsplit; ++rk) {
                     const float4 v =
-                        *reinterpret_cast<const float4 *>(xb + rk * (32 * kThreads) + (j4 * kThreads + tid) * 4);
+                        *reinterpret_cast<const float4 *>(xa + rk * (q * kThreads) + (j4 * kThreads + tid) * 4);
                     t.x += v.x;
                     t.y += v.y;
                     t.z += v.z;
                     t.w += v.w;
                 }
-                wsum[4 * j4] = t.x;
-                wsum[4 * j4 + 1] = t.y;
-                wsum[4 * j4 + 2] = t.z;
-                wsum[4 * j4 + 3] = t.w;
+                for (int rk = 0; rk < nsplit; ++rk)
+                    *reinterpret_cast<float4 *>(cl.map_shared_rank(xg, rk) + half * (q * kThreads) +
+                                                (j4 * kThreads + tid) * 4) = t;
+            }
+        }
+        cl.sync();
+        if (ok) {
+#pragma unroll
+            for (int j4 = 0; j4 < kPanel / 4; ++j4) {
+                const int j = 4 * j4, own = j / q, jq = (j - own * q) / 4;
+                const float4 v =
+                    *reinterpret_cast<const float4 *>(xg + own * (q * kThreads) + (jq * kThreads + tid) * 4);
+                wsum[j] = v.x;
+                wsum[j + 1] = v.y;
+                wsum[j + 2] = v.z;
+                wsum[j + 3] = v.w;
             }
         }
     }
@@ -660,19 +684,35 @@ cudaError_t launch_apply_tc(const TrailingMaps &maps, const float *H, const floa
     return cudaSuccess;
 }
 
+// Ranks per tile: 1 (one CTA per tile) unless all tiles of the call fit one
+// CTA per SM and a tile has >= 256 rows; then the largest split of 2, 4 or 8
+// that still fits two CTAs per SM (296 on 148 SMs) with >= 128 rows (one
+// phase-C chunk) per rank.  Measured at n = 1024 (ms per call): one matrix
+// 1.78 -> 1.68, two 2.01 -> 1.87, eight 1.99 -> 1.88 against two ranks;
+// >= 256 rows per rank gained ~1%; many-tile calls are unchanged.
+static int trailing_split(int64_t batch_all, int64_t tiles, int rows)
+{
+    if (rows < 256 || tiles * batch_all > 148) return 1;
+    int ns = 2;
+    while (ns < kMaxSplit && tiles * batch_all * ns * 2 <= 296 && rows >= ns * 2 * kRCC) ns *= 2;
+    // every rank must own at least one row (rows per rank: a multiple of 128)
+    while (ns > 1 && (int64_t)(ns - 1) * ((rows + ns * kRCC - 1) / (ns * kRCC) * kRCC) >= rows) ns /= 2;
+    return ns;
+}
+
 cudaError_t launch_trailing_tc(const TrailingMaps &maps, float *H, const float *Sws, int64_t s_stride,
                                const float *tau, int *status, int64_t batch, int64_t batch_all, int m, int n, int k,
                                cudaStream_t st)
 {
     if (n - k - kPanel <= 0) return cudaSuccess;
     // Static plan by (the call's batch, n, k), as for the rank-64 update:
-    // when all tiles of the call fit one CTA per SM, two CTAs (a cluster)
-    // share each tile's rows
+    // when all tiles of the call fit one CTA per SM, a cluster of CTAs shares
+    // each tile's rows (trailing_split)
     const int64_t tiles = (n - k - kPanel + kTN - 1) / kTN;
     const int rows = m - k;
-    if (!(rows >= 256 && tiles * batch_all <= 148))
+    const int kSplit = trailing_split(batch_all, tiles, rows);
+    if (kSplit == 1)
         return launch_apply_tc(maps, H, Sws, s_stride, tau, status, batch, m, n, k, k + kPanel, n, true, st);
-    constexpr int kSplit = 2;
     auto kern = trailing_tc_kernel<true, true>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
     if (e != cudaSuccess) return e;
