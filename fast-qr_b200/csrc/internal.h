@@ -66,8 +66,8 @@ cudaError_t launch_apply_tc(const TrailingMaps &maps, const float *H, const floa
                             const float *tau, int *status, int64_t batch, int m, int hcols, int k,
                             int c_begin, int c_end, bool apply_t, cudaStream_t st);
 // batch_all: the whole call's batch (the launch covers `batch` of them); the
-// static plan splits each tile's rows over two CTAs when the call's tiles
-// fit one CTA per SM.
+// static plan splits each tile's rows over a cluster of 2, 4 or 8 CTAs when
+// the call's tiles fit one CTA per SM.
 cudaError_t launch_trailing_tc(const TrailingMaps &maps, float *H, const float *Sws, int64_t s_stride,
                                const float *tau, int *status, int64_t batch, int64_t batch_all, int m, int n, int k,
                                cudaStream_t st);
@@ -111,7 +111,7 @@ cudaError_t launch_inblock(float *H, const float *tau, float *S64, int64_t s_str
 // Rank-64 tensor-core trailing update of columns k+64 .. n-1 with the 64
 // reflectors of columns k .. k+63 (S64 complete) and tau.  batch_all: the
 // whole call's batch (the launch covers `batch` of them), which the static
-// plan uses to decide whether two CTAs share each tile's rows.
+// plan uses to decide how many CTAs (1, 2, 4 or 8) share each tile's rows.
 cudaError_t launch_trailing64_tc(const TrailingMaps &maps, float *H, const float *S64, int64_t s_stride,
                                  const float *tau, int *status, int64_t batch, int64_t batch_all, int m, int n,
                                  int k, cudaStream_t st);
