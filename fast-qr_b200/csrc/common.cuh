@@ -42,7 +42,10 @@ struct Reflector {
 // far from unit scale.  The fast path is therefore taken only when
 //   sigma in [1e-20, 1e20]  (||x|| in [1e-10, 1e10]) and |alpha| <= 1e15,
 // and, checked after the reduction, every d_j is finite and not in the
-// denormal-product regime (0 < |d_j| < 1e-30).  Otherwise the column is redone
+// denormal-product regime (0 < |d_j| < 1e-30); the panel kernel checks the
+// stricter |d_j| <= 1e17 and |a(k,j)| <= 1e27 instead, which bound w_j
+// without the reflector (|scale| <= 1e10 in the envelope), so its vote
+// overlaps the reflector's computation.  Otherwise the column is redone
 // in LAPACK order: sigma in double, v = x / (alpha - beta), then w_j = v^T a_j.
 constexpr float kSigmaLo = 1e-20f;
 constexpr float kSigmaHi = 1e20f;

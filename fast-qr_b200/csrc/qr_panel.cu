@@ -188,14 +188,18 @@ panel_kernel(float *__restrict__ H, float *__restrict__ tau, float *__restrict__
                 for (int qr = 0; qr < ncl; ++qr) f += xch[par][qr][lane];
                 rc = xch[par][0][32 + lane];
             }
+            // safety of the fast path, voted before the reflector (the vote
+            // overlaps its chain): within the fast envelope |scale| <= 1e10,
+            // so |d| <= 1e17 and |a(c, l)| <= 1e27 keep w_l finite
+            const bool early_vote = __any_sync(kFull, !(fabsf(f) <= 1e17f) || (f != 0.0f && fabsf(f) < kDotTiny) ||
+                                                          !(fabsf(rc) <= 1e27f));
             const float alpha = __shfl_sync(kFull, rc, c);
             const float sg = __shfl_sync(kFull, f, c);
             // sigma == 0 (an exactly zero tail, or one whose squares
             // underflow) also goes to the robust path, which sorts the two out
-            bool fast = reflector_fast_ok(alpha, sg);
+            bool fast = reflector_fast_ok(alpha, sg) && !early_vote;
             Reflector r = fast ? reflector_from_float(alpha, sg) : reflector_identity(alpha);
             float wl = rc + r.scale * f;
-            if (fast) fast = !__any_sync(kFull, dot_unsafe(f, wl));
 
             if (!fast) {
                 // Robust path, LAPACK order (uniform across the CTA and the
