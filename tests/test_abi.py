@@ -75,15 +75,18 @@ def test_workspace_and_plan_depend_on_shape_only():
     with pytest.raises(fastqr.FastQRError):
         fastqr.plan(1, 10000)
     assert fastqr.launch_count(1024, 32) == 1
-    # two parts of a batch on two streams, each copy-in + 8 panels + 7 trailing
-    assert fastqr.launch_count(256, 256) == 2 * (1 + 8 + 7)
+    # copy-in + 8 panels + 7 trailing; a batch runs as one part up to 26M
+    # matrix elements (n < 2048), else as two parts on two streams
+    assert fastqr.launch_count(256, 256) == 1 + 8 + 7
     assert fastqr.launch_count(1, 256) == 1 + 8 + 7
+    assert fastqr.launch_count(512, 256) == 2 * (1 + 8 + 7)
     # n >= 2048: rank-64 blocks (panel, in-block update, panel, then Gram
     # block + trailing update for all but the last block); four parts for
-    # n >= 2048: 32 blocks each
+    # n >= 2048 above 140M elements (one part up to that): 32 blocks each
     assert "rank 64" in fastqr.plan(16, 4096) and "rank 32" in fastqr.plan(64, 1024)
-    assert fastqr.launch_count(16, 2048) == 4 * (1 + 32 * 3 + 31 * 2)
-    assert fastqr.launch_count(3, 2048) == 3 * (1 + 32 * 3 + 31 * 2)
+    assert fastqr.launch_count(16, 2048) == 1 + 32 * 3 + 31 * 2
+    assert fastqr.launch_count(3, 2048) == 1 + 32 * 3 + 31 * 2
+    assert fastqr.launch_count(40, 2048) == 4 * (1 + 32 * 3 + 31 * 2)
     assert fastqr.launch_count(64, 1024) == 2 * (1 + 32 + 31)
     # 2100 = 32 blocks of 64 + a 32- and a 20-column panel (every block has a
     # trailing update, the first rank-32 panel too)

@@ -71,8 +71,9 @@ def test_rect_large_gates(m, n, dev):
 
 
 def test_rect_batch_split_and_strides(dev):
-    """Batches of two or more run as two halves on two streams; a
-    column-major input takes the strided copy-in; results equal per matrix."""
+    """A matrix factored within a batch and on its own gives bitwise the same
+    result (large batches run as parts on several streams); a column-major
+    input takes the strided copy-in."""
     a = tall(5, 300, 200, 9).to(dev)
     h, t = fastqr.geqrf(a)
     h1, t1 = fastqr.geqrf(a[3:4])
