@@ -27,20 +27,22 @@ namespace {
 
 using fqr::kWsAlign;
 
-// Streams a batch is split over (static plan by batch and n, through the
-// call's element count batch * n^2).  Parts on concurrent streams fill the
-// SMs one part's chain leaves idle, but a small batch leaves SMs idle either
-// way and then one chain of launches is shorter: one part up to 26M elements
-// (n < 2048) or 140M (n >= 2048), else two (n < 2048) or four.  Measured
-// against the earlier fixed two / four parts: 256 x 256^2 -5.7%, 32 x 256^2
-// -9%, 64 x 512^2 -6.6%, 8 x 1024^2 -8.6%, 2 and 4 x 4096^2 -5% and -8.4%;
-// 512 x 256^2 (33.5M elements) was 12.8% slower with one part.  Three parts
-// at n < 2048 measured +4% to +18%.
+// Streams a batch is split over (static plan by batch and n).  Parts on
+// concurrent streams fill the SMs one part's chain leaves idle, but a small
+// batch leaves SMs idle either way and one chain of launches is shorter (half
+// the launches to enqueue, too).  One part up to 64 matrices and 17M matrix
+// elements (n < 2048) or up to 140M elements (n >= 2048), else two (n < 2048)
+// or four (64 x 1024^2 was 16% slower with one part).  Measured
+// against the earlier fixed two / four parts, steps back to back: 32 and
+// 64 x 256^2 -2.7% and -2.0%, 8 x 1024^2 -0.6%, 2 and 4 x 4096^2 -1.2% and
+// -0.4% (per call with a synchronize after each: -9%, -8.6%, -5%, -8.4%);
+// 128 x 256^2 was 2.7% slower with one part.  Three parts at n < 2048
+// measured +4% to +18%.
 constexpr int kMaxSplitParts = 4;
 int split_parts(int64_t batch, int64_t n)
 {
     const double elems = (double)batch * (double)n * (double)n;
-    const int want = n >= 2048 ? (elems <= 140e6 ? 1 : 4) : (elems <= 26e6 ? 1 : 2);
+    const int want = n >= 2048 ? (elems <= 140e6 ? 1 : 4) : (batch <= 64 && elems <= 17e6 ? 1 : 2);
     return batch < want ? (int)batch : want;
 }
 

@@ -75,11 +75,11 @@ def test_workspace_and_plan_depend_on_shape_only():
     with pytest.raises(fastqr.FastQRError):
         fastqr.plan(1, 10000)
     assert fastqr.launch_count(1024, 32) == 1
-    # copy-in + 8 panels + 7 trailing; a batch runs as one part up to 26M
-    # matrix elements (n < 2048), else as two parts on two streams
-    assert fastqr.launch_count(256, 256) == 1 + 8 + 7
+    # copy-in + 8 panels + 7 trailing; a batch runs as one part up to 64
+    # matrices (n < 2048), else as two parts on two streams
+    assert fastqr.launch_count(256, 256) == 2 * (1 + 8 + 7)
+    assert fastqr.launch_count(64, 256) == 1 + 8 + 7
     assert fastqr.launch_count(1, 256) == 1 + 8 + 7
-    assert fastqr.launch_count(512, 256) == 2 * (1 + 8 + 7)
     # n >= 2048: rank-64 blocks (panel, in-block update, panel, then Gram
     # block + trailing update for all but the last block); four parts for
     # n >= 2048 above 140M elements (one part up to that): 32 blocks each
