@@ -1,20 +1,17 @@
 // fqr_geqrf_f32_host: batched QR of matrices held in HOST memory.
 //
-// The batch is cut into up to 18 chunks, run as a three-stage pipeline:
-// every upload goes on one copy stream in chunk order, each chunk is factored
-// on its own internal stream (its own device staging slot) as soon as its
-// upload has landed, and every download goes on a second copy stream in
-// chunk order.  Uploads therefore reach the device one chunk after the other
-// at the full host-to-device rate (copies issued on many streams at once share
-// the link and all finish late), chunk i is factored while chunk i+1 uploads,
-// and the downloads use the other direction of the link.  A call made
+// The batch is cut into up to 16 chunks.  Each chunk is copied host->device,
+// factored and copied back device->host on its own internal stream with its
+// own device staging slot, so that the uploads run back to back while earlier
+// chunks are factored and downloaded (the two copy directions use separate
+// copy engines).  A call made
 // through the device-pointer entry point pays the two transfers one after the
 // other and after the kernels; here the whole call costs about one transfer
 // plus the factorisation and download of a single chunk.
 //
 // Ordering with the caller: an event recorded on `stream` is waited on by
-// both copy streams before their first copy, and `stream` waits on an event
-// recorded at the end of every internal stream, so the call behaves like any
+// every internal stream before its first copy, and `stream` waits on an event
+// recorded at the end of each internal stream, so the call behaves like any
 // other asynchronous work on `stream`.  The host buffers must stay valid and
 // unmodified until `stream` has passed the call.  Copies overlap only when the
 // host buffers are page-locked (cudaHostAlloc / cudaHostRegister); pageable
@@ -30,8 +27,8 @@
 // The internal streams and events are created once per device, on the first
 // call made with that device current, and live until the process exits.
 // The enqueue sequence of a call holds a per-device mutex (the events are
-// shared), so concurrent calls on one device share the copy streams and run
-// one after the other.
+// shared); kernels of concurrent calls still overlap on the GPU when their
+// workspaces differ.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -45,33 +42,18 @@ using fqr::kWsAlign;
 
 // Every chunk gets its own staging slot and stream: a slot reused by a later
 // chunk would hold that chunk's upload until the earlier chunk's
-// factorisation (a per-matrix latency chain of ~0.3 ms at n = 256, whatever
+// factorisation (a per-matrix latency chain of ~0.35 ms at n = 256, whatever
 // the chunk's size) and download are done.
-//
-// The first and the last chunk are small ("edge" chunks, 1/8 of a body chunk):
-// the downloads cannot start before the first chunk is factored, and the call
-// cannot end before the last chunk is factored and downloaded, so both ends
-// of the pipeline cost one factorisation latency plus the copy of an edge
-// chunk instead of a body chunk.  A device-side timeline of a 256 x 256^2
-// call (64 MiB each way) shows what remains: the factorisations hide behind
-// the copies, and the call is bound by the link, whose two directions carry
-// ~37 GB/s each while both are busy (the uploads end at 1.85 ms, the last
-// download 0.27 ms later).
 constexpr int kMaxSlots = 16;
-constexpr int kMaxBody = 16;                // body chunks at most
-constexpr int kMaxChunks = kMaxBody + 2;    // plus the two edge chunks
-constexpr int kTaper = 8;                   // edge chunk = body chunk / kTaper (at least 1)
-constexpr size_t kMinChunkBytes = size_t(1) << 20;  // 1 MiB of input per body chunk at least
+constexpr int kMaxChunks = 16;
+constexpr size_t kMinChunkBytes = size_t(1) << 20;  // 1 MiB of input per chunk at least
 constexpr int kMaxDevices = 64;
 
 constexpr size_t align_up(size_t x) { return (x + kWsAlign - 1) / kWsAlign * kWsAlign; }
 
 // Chunking plan: a function of (batch, n) only.
 struct HostPlan {
-    int64_t batch;
-    int64_t chunk;     // matrices per slot (the largest chunk: a body chunk)
-    int64_t edge;      // matrices in the first and the last chunk (0: all chunks are body chunks)
-    int64_t body;      // matrices per body chunk (the last body chunk may be shorter)
+    int64_t chunk;     // matrices per chunk (the last one may be shorter)
     int64_t nchunks;
     int slots;         // staging slots = internal streams used
     size_t off_a, off_h, off_tau, off_ws, ws_bytes, slot_bytes;
@@ -84,28 +66,16 @@ bool host_plan(int64_t batch, int64_t n, HostPlan *p)
     if (batch <= 0 || n <= 0 || n > FQR_MAX_N) return false;
     const size_t mat = (size_t)n * (size_t)n * sizeof(float);
     const size_t all = mat * (size_t)batch;
-    size_t target = all / kMaxBody;
+    size_t target = all / kMaxChunks;
     if (target < kMinChunkBytes) target = kMinChunkBytes;
     int64_t chunk = (int64_t)((target + mat - 1) / mat);
-    const int64_t min_chunk = (batch + kMaxBody - 1) / kMaxBody;  // at most kMaxBody body chunks
+    const int64_t min_chunk = (batch + kMaxChunks - 1) / kMaxChunks;  // at most kMaxChunks chunks
     if (chunk < min_chunk) chunk = min_chunk;
     if (chunk > batch) chunk = batch;
     if (chunk < 1) chunk = 1;
-    int64_t edge = chunk >= 2 ? (chunk / kTaper > 1 ? chunk / kTaper : 1) : 0;
-    if (batch < 2 * edge + chunk) edge = 0;
-    const int64_t rest = batch - 2 * edge;
-    const int64_t nbody = (rest + chunk - 1) / chunk;
-    p->batch = batch;
-    p->edge = edge;
-    p->body = (rest + nbody - 1) / nbody;  // even split, <= chunk, >= edge
-    p->chunk = p->body;                    // a slot holds the largest chunk
-    chunk = p->body;
-    p->nchunks = nbody + (edge ? 2 : 0);
-    // the two edge chunks share one slot when every chunk could have its own
-    // (the last one reuses the first one's, long downloaded)
-    int64_t slots = p->nchunks < kMaxSlots ? p->nchunks : kMaxSlots;
-    if (edge && slots > nbody + 1) slots = nbody + 1;
-    p->slots = (int)slots;
+    p->chunk = chunk;
+    p->nchunks = (batch + chunk - 1) / chunk;
+    p->slots = (int)(p->nchunks < kMaxSlots ? p->nchunks : kMaxSlots);
     p->ws_bytes = fqr_workspace_bytes(chunk, n);
     p->off_a = 0;
     p->off_h = align_up((size_t)chunk * mat);
@@ -115,23 +85,6 @@ bool host_plan(int64_t batch, int64_t n, HostPlan *p)
     p->status_bytes = align_up((size_t)p->nchunks * sizeof(int));
     p->total = p->status_bytes + (size_t)p->slots * p->slot_bytes;
     return true;
-}
-
-// First matrix and size of chunk c: [edge | body, body, ..., body' | edge].
-void chunk_range(const HostPlan &p, int64_t c, int64_t *b0, int64_t *cb)
-{
-    if (p.edge && c == 0) {
-        *b0 = 0;
-        *cb = p.edge;
-    } else if (p.edge && c == p.nchunks - 1) {
-        *b0 = p.batch - p.edge;
-        *cb = p.edge;
-    } else {
-        const int64_t i = p.edge ? c - 1 : c;
-        const int64_t end = p.batch - p.edge;
-        *b0 = p.edge + i * p.body;
-        *cb = (*b0 + p.body <= end) ? p.body : end - *b0;
-    }
 }
 
 // One call's arguments: the key of its cached graph.
@@ -165,11 +118,9 @@ struct CachedGraph {
 struct DeviceStreams {
     bool ready = false;
     cudaStream_t origin = nullptr;  // root of a captured call
-    cudaStream_t up = nullptr, down = nullptr;  // uploads / downloads, in chunk order
-    cudaStream_t st[kMaxSlots] = {};            // factorisation, one stream per slot
+    cudaStream_t st[kMaxSlots] = {};
     cudaEvent_t fork = nullptr;
-    cudaEvent_t uploaded[kMaxChunks] = {}, factored[kMaxChunks] = {}, downloaded[kMaxChunks] = {};
-    cudaEvent_t done[kMaxSlots + 2] = {};  // end of every internal stream (joined into the caller)
+    cudaEvent_t done[kMaxSlots] = {};
     CachedGraph graphs[kGraphCache];
     uint64_t tick = 0;
     std::mutex mu;
@@ -185,19 +136,13 @@ int device_streams(DeviceStreams **out)
     *out = &d;
     if (d.ready) return FQR_OK;
     if (cudaEventCreateWithFlags(&d.fork, cudaEventDisableTiming) != cudaSuccess ||
-        cudaStreamCreateWithFlags(&d.origin, cudaStreamNonBlocking) != cudaSuccess ||
-        cudaStreamCreateWithFlags(&d.up, cudaStreamNonBlocking) != cudaSuccess ||
-        cudaStreamCreateWithFlags(&d.down, cudaStreamNonBlocking) != cudaSuccess)
+        cudaStreamCreateWithFlags(&d.origin, cudaStreamNonBlocking) != cudaSuccess)
         return FQR_ECUDA;
-    for (int s = 0; s < kMaxSlots; ++s)
-        if (cudaStreamCreateWithFlags(&d.st[s], cudaStreamNonBlocking) != cudaSuccess) return FQR_ECUDA;
-    for (int s = 0; s < kMaxSlots + 2; ++s)
-        if (cudaEventCreateWithFlags(&d.done[s], cudaEventDisableTiming) != cudaSuccess) return FQR_ECUDA;
-    for (int c = 0; c < kMaxChunks; ++c)
-        if (cudaEventCreateWithFlags(&d.uploaded[c], cudaEventDisableTiming) != cudaSuccess ||
-            cudaEventCreateWithFlags(&d.factored[c], cudaEventDisableTiming) != cudaSuccess ||
-            cudaEventCreateWithFlags(&d.downloaded[c], cudaEventDisableTiming) != cudaSuccess)
+    for (int s = 0; s < kMaxSlots; ++s) {
+        if (cudaStreamCreateWithFlags(&d.st[s], cudaStreamNonBlocking) != cudaSuccess ||
+            cudaEventCreateWithFlags(&d.done[s], cudaEventDisableTiming) != cudaSuccess)
             return FQR_ECUDA;
+    }
     d.ready = true;
     return FQR_OK;
 }
@@ -207,7 +152,7 @@ int device_streams(DeviceStreams **out)
 int enqueue_host(const HostCall &c, const HostPlan &p, DeviceStreams *d, cudaStream_t caller)
 {
     const float *A = c.A;
-    const int64_t n = c.n, a_bstride = c.a_bstride;
+    const int64_t batch = c.batch, n = c.n, a_bstride = c.a_bstride;
     float *H = c.H, *tau = c.tau;
     const bool colmajor = c.a_rstride == 1 && c.a_cstride == n && n > 1;
     int rc = FQR_OK;
@@ -219,20 +164,15 @@ int enqueue_host(const HostCall &c, const HostPlan &p, DeviceStreams *d, cudaStr
     const int64_t d_rs = colmajor ? 1 : n, d_cs = colmajor ? n : 1;
 
     if (cudaMemsetAsync(status, 0, p.status_bytes, caller) != cudaSuccess) return FQR_ECUDA;
-    if (cudaEventRecord(d->fork, caller) != cudaSuccess ||
-        cudaStreamWaitEvent(d->up, d->fork, 0) != cudaSuccess ||
-        cudaStreamWaitEvent(d->down, d->fork, 0) != cudaSuccess)
-        return FQR_ECUDA;
+    if (cudaEventRecord(d->fork, caller) != cudaSuccess) return FQR_ECUDA;
+    for (int s = 0; s < p.slots; ++s)
+        if (cudaStreamWaitEvent(d->st[s], d->fork, 0) != cudaSuccess) return FQR_ECUDA;
 
     for (int64_t c = 0; c < p.nchunks; ++c) {
         const int s = (int)(c % p.slots);
         cudaStream_t st = d->st[s];
-        // a slot's next upload overwrites its input only after the chunk that
-        // used it last has been downloaded (and so factored)
-        if (c >= p.slots && cudaStreamWaitEvent(d->up, d->downloaded[c - p.slots], 0) != cudaSuccess)
-            return FQR_ECUDA;
-        int64_t b0 = 0, cb = 0;
-        chunk_range(p, c, &b0, &cb);
+        const int64_t b0 = c * p.chunk;
+        const int64_t cb = (b0 + p.chunk <= batch) ? p.chunk : batch - b0;
         unsigned char *slot = ws + p.status_bytes + (size_t)s * p.slot_bytes;
         float *dA = (float *)(slot + p.off_a);
         float *dH = (float *)(slot + p.off_h);
@@ -241,46 +181,35 @@ int enqueue_host(const HostCall &c, const HostPlan &p, DeviceStreams *d, cudaStr
         const float *hA = A + b0 * a_bstride;
         cudaError_t e;
         if (a_bstride == (int64_t)mat_elems || cb == 1) {
-            e = cudaMemcpyAsync(dA, hA, (size_t)cb * mat_bytes, cudaMemcpyHostToDevice, d->up);
+            e = cudaMemcpyAsync(dA, hA, (size_t)cb * mat_bytes, cudaMemcpyHostToDevice, st);
         } else {
             // gapped batch: one strided copy, or one copy per matrix where the
             // pitch is beyond what a strided copy accepts
             e = cudaMemcpy2DAsync(dA, mat_bytes, hA, (size_t)a_bstride * sizeof(float), mat_bytes,
-                                  (size_t)cb, cudaMemcpyHostToDevice, d->up);
+                                  (size_t)cb, cudaMemcpyHostToDevice, st);
             if (e != cudaSuccess) {
                 cudaGetLastError();
                 e = cudaSuccess;
                 for (int64_t i = 0; i < cb && e == cudaSuccess; ++i)
                     e = cudaMemcpyAsync(dA + (size_t)i * mat_elems, hA + i * a_bstride, mat_bytes,
-                                        cudaMemcpyHostToDevice, d->up);
+                                        cudaMemcpyHostToDevice, st);
             }
         }
-        if (e != cudaSuccess || cudaEventRecord(d->uploaded[c], d->up) != cudaSuccess ||
-            cudaStreamWaitEvent(st, d->uploaded[c], 0) != cudaSuccess)
-            return FQR_ECUDA;
+        if (e != cudaSuccess) return FQR_ECUDA;
         rc = fqr::geqrf_enqueue_status(dA, cb, n, (int64_t)mat_elems, d_rs, d_cs, dH, dT, dW,
                                        p.ws_bytes, status + c, st);
         if (rc != FQR_OK) return rc;
-        if (cudaEventRecord(d->factored[c], st) != cudaSuccess ||
-            cudaStreamWaitEvent(d->down, d->factored[c], 0) != cudaSuccess ||
-            cudaMemcpyAsync(H + (size_t)b0 * mat_elems, dH, (size_t)cb * mat_bytes,
-                            cudaMemcpyDeviceToHost, d->down) != cudaSuccess ||
+        if (cudaMemcpyAsync(H + (size_t)b0 * mat_elems, dH, (size_t)cb * mat_bytes,
+                            cudaMemcpyDeviceToHost, st) != cudaSuccess ||
             cudaMemcpyAsync(tau + (size_t)b0 * (size_t)n, dT, (size_t)cb * (size_t)n * sizeof(float),
-                            cudaMemcpyDeviceToHost, d->down) != cudaSuccess ||
-            cudaEventRecord(d->downloaded[c], d->down) != cudaSuccess)
+                            cudaMemcpyDeviceToHost, st) != cudaSuccess)
             return FQR_ECUDA;
     }
-    // join every internal stream back into the caller (a captured graph needs
-    // each forked stream joined)
-    cudaStream_t used[kMaxSlots + 2];
-    int nused = 0;
-    used[nused++] = d->up;
-    used[nused++] = d->down;
-    for (int s = 0; s < p.slots; ++s) used[nused++] = d->st[s];
-    for (int i = 0; i < nused; ++i)
-        if (cudaEventRecord(d->done[i], used[i]) != cudaSuccess ||
-            cudaStreamWaitEvent(caller, d->done[i], 0) != cudaSuccess)
+    for (int s = 0; s < p.slots; ++s) {
+        if (cudaEventRecord(d->done[s], d->st[s]) != cudaSuccess ||
+            cudaStreamWaitEvent(caller, d->done[s], 0) != cudaSuccess)
             return FQR_ECUDA;
+    }
     return FQR_OK;
 }
 

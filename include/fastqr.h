@@ -140,10 +140,9 @@ int fqr_noalloc_check_status(void *stream);
  * Batched QR of matrices in HOST memory: the same result as fqr_geqrf_f32,
  * with A, H and tau host pointers (page-locked memory, from cudaHostAlloc or
  * cudaHostRegister, lets the copies overlap; pageable memory works, slower).
- * The batch is cut into chunks, run as a pipeline on internal streams with
- * separate device staging: uploads in chunk order on one copy stream, each
- * chunk's factorisation on its own stream, downloads in chunk order on a
- * second copy stream.  So copies in both directions overlap the kernels.  Asynchronous on `stream` like
+ * The batch is cut into chunks that are uploaded, factored and downloaded on
+ * internal streams with separate device staging, so that copies in both
+ * directions overlap the kernels.  Asynchronous on `stream` like
  * fqr_geqrf_f32: H and tau are complete, and A may be reused, once `stream`
  * has passed the call.
  * A: each matrix one dense n x n block, row-major (a_rstride = n,

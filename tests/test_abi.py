@@ -123,9 +123,8 @@ def test_host_entry_validation_without_gpu():
 
 
 def test_host_workspace_plan():
-    # at most 16 staging slots, each holding one body chunk (>= 1 MiB of input
-    # or 1/16 of the batch; the two edge chunks are smaller); sizes depend on
-    # (batch, n) only
+    # one staging slot per chunk, at most 16 chunks, each >= 1 MiB of input
+    # or 1/16 of the batch; sizes depend on (batch, n) only
     for batch, n in [(1024, 32), (256, 256), (512, 512), (64, 1024), (16, 4096), (1, 8), (3, 100)]:
         mat = n * n * 4
         need = fastqr.host_workspace_bytes(batch, n)
