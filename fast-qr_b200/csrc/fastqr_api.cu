@@ -349,7 +349,8 @@ int enqueue_blocked_split(const float *A, int64_t batch, int m, int n, int64_t a
 // through the rectangular entry, with tau [batch][n]).
 int run_geqrf(const float *A, int64_t batch, int64_t m, int64_t n, int64_t a_bstride, int64_t a_rstride,
               int64_t a_cstride, float *H, float *tau, void *workspace, size_t workspace_bytes,
-              cudaStream_t st, StageTimer *tm, int *status_word = nullptr, bool split = true)
+              cudaStream_t st, StageTimer *tm, int *status_word = nullptr, bool split = true,
+              int64_t batch_in_flight = 0)
 {
     if (batch < 0 || n < 0 || m < 0) return FQR_EINVAL;
     if (batch == 0 || n == 0) return FQR_OK;
@@ -387,7 +388,8 @@ int run_geqrf(const float *A, int64_t batch, int64_t m, int64_t n, int64_t a_bst
                                      tc, st);
     // an own status word (host entry, one per chunk) or both words of the
     // workspace's status block
-    return enqueue_blocked(A, batch, batch, mi, ni, a_bstride, a_rstride, a_cstride, H, tau, Sws, status, 0,
+    return enqueue_blocked(A, batch, batch_in_flight > batch ? batch_in_flight : batch, mi, ni, a_bstride,
+                           a_rstride, a_cstride, H, tau, Sws, status, 0,
                            status_word ? 1u : (1u << kSplitParts) - 1u, tc, st, tm);
 }
 
@@ -404,10 +406,10 @@ int fqr::geqrf_enqueue(const float *A, int64_t batch, int64_t n, int64_t a_bstri
 int fqr::geqrf_enqueue_status(const float *A, int64_t batch, int64_t n, int64_t a_bstride,
                               int64_t a_rstride, int64_t a_cstride, float *H, float *tau,
                               void *workspace, size_t workspace_bytes, int *status_word,
-                              cudaStream_t st)
+                              int64_t batch_in_flight, cudaStream_t st)
 {
     return run_geqrf(A, batch, n, n, a_bstride, a_rstride, a_cstride, H, tau, workspace,
-                     workspace_bytes, st, nullptr, status_word, false);
+                     workspace_bytes, st, nullptr, status_word, false, batch_in_flight);
 }
 
 extern "C" {

@@ -196,8 +196,21 @@ int enqueue_host(const HostCall &c, const HostPlan &p, DeviceStreams *d, cudaStr
             }
         }
         if (e != cudaSuccess) return FQR_ECUDA;
+        // Each chunk is planned as if it ran alone, so its trailing updates
+        // split rows over more CTAs to shorten its chain, except for large
+        // matrices (n >= 3584, rank-64 plan: one matrix per chunk, whose
+        // factorisation outlasts many uploads) when the call's trailing tiles
+        // together fill two CTAs per SM (296): those chunks run side by side
+        // and are planned for the whole batch, which trades the last chunk's
+        // longer chain for the throughput of unsplit tiles.  Measured (ms per
+        // call, whole batch / alone): 16 x 4096^2 42.2 / 48.1, 24 x 4096^2
+        // 56.9 / 65.0, 10 x 4096^2 32.1 / 33.2; where it lost: 4 x 4096^2
+        // 19.4 / 18.7, 16 x 3072^2 27.2 / 24.2, 32 x 2048^2 17.6 / 16.8,
+        // 16 x 2048^2 12.1 / 11.0, and C4's rank-32 chunks 8.0 / 7.6.
+        const int64_t tiles = (n - fqr::kOuter + 127) / 128;  // trailing tiles of the first rank-64 update
+        const int64_t in_flight = fqr::use_outer64(n, n) && n >= 3584 && tiles * batch >= 296 ? batch : cb;
         rc = fqr::geqrf_enqueue_status(dA, cb, n, (int64_t)mat_elems, d_rs, d_cs, dH, dT, dW,
-                                       p.ws_bytes, status + c, st);
+                                       p.ws_bytes, status + c, in_flight, st);
         if (rc != FQR_OK) return rc;
         if (cudaMemcpyAsync(H + (size_t)b0 * mat_elems, dH, (size_t)cb * mat_bytes,
                             cudaMemcpyDeviceToHost, st) != cudaSuccess ||

@@ -140,11 +140,14 @@ int geqrf_enqueue(const float *A, int64_t batch, int64_t n, int64_t a_bstride, i
                   int64_t a_cstride, float *H, float *tau, void *workspace, size_t workspace_bytes,
                   cudaStream_t st);
 // The same with the bounded-wait status word at `status_word` instead of
-// inside the workspace (the first kernel of the call clears it).
+// inside the workspace (the first kernel of the call clears it), in one part
+// on `st`.  batch_in_flight: how many matrices of the caller's work run on
+// the device at once (>= batch); the plan sizes its grids for that many, so a
+// chunk that runs beside others does not split rows as if it were alone.
 int geqrf_enqueue_status(const float *A, int64_t batch, int64_t n, int64_t a_bstride,
                          int64_t a_rstride, int64_t a_cstride, float *H, float *tau,
                          void *workspace, size_t workspace_bytes, int *status_word,
-                         cudaStream_t st);
+                         int64_t batch_in_flight, cudaStream_t st);
 
 // Launch with programmatic dependent launch: the kernel may be scheduled
 // while the previous kernel on `st` is still running (once every CTA of that

@@ -1,7 +1,9 @@
 """GPU: the host-buffer entry point (fqr_geqrf_f32_host) gives bitwise the
-same H and tau as the device entry point on the same matrices -- both run the
-same kernels, chunked over the batch -- for every layout it accepts, with
-page-locked and pageable buffers, and composes with the caller's stream."""
+same H and tau as the device entry point on the same matrices up to n = 1024
+-- both run the same kernels and plans, chunked over the batch -- for every
+layout it accepts, with page-locked and pageable buffers, and composes with
+the caller's stream.  For the rank-64 plan (n >= 2048) the two entries agree
+to rounding (the last test)."""
 import pytest
 import torch
 
@@ -115,3 +117,19 @@ def test_host_replayed_call_sees_new_data(dev):
             hd, td = device_result(a, dev)
             assert torch.equal(h, hd) and torch.equal(t, td), (pinned, seed)
             fastqr.host_check_status(ws, batch, n)  # raises if a bounded wait gave up
+
+
+def test_host_large_chunks_planned_for_the_batch(dev):
+    """10 x 4096^2: n >= 3584 and the call's trailing tiles fill two CTAs per
+    SM, so the one-matrix chunks are planned for the whole batch (unsplit
+    rank-64 tiles), as the device entry plans its parts.  The in-block steps
+    size their clusters by each launch's own batch (one matrix per chunk here,
+    two or three per part there), so the two entries agree to rounding, within
+    the per-column 1e-3 that the parity tests allow against float64."""
+    n, batch = 4096, 10
+    a = torch.randn(batch, n, n, generator=torch.Generator().manual_seed(11)).pin_memory()
+    h, t = fastqr.geqrf_host(a, device=dev)
+    hd, td = device_result(a, dev)
+    col = (h - hd).abs().amax(dim=1) / hd.abs().amax(dim=1).clamp_min(1e-30)  # per column of H
+    assert col.max().item() <= 1e-3
+    assert ((t - td).abs() <= 1e-3 * td.abs() + 1e-6).all()
