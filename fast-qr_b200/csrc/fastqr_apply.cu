@@ -119,6 +119,118 @@ __global__ void __launch_bounds__(256) apply_small_kernel(const float *__restric
     }
 }
 
+// Blocked path without the tensor cores (n > 512 where the tensor-core path
+// cannot run: n % 4 != 0, or H or C not 16-byte aligned).  Applies panel k's
+// block reflector to a 32-column tile of C (rows k .. n-1, columns c0 ..):
+// QT: C := (I - V T V^T)^T C = (I - V T^T V^T) C, Y = T^T W by forward
+// substitution (the geqrf trailing update); otherwise C := (I - V T V^T) C,
+// Y = T W = D (I + S D)^-1 W by backward substitution,
+//   Y(c) = tau_c (W(c) - sum_{l > c} S(c, l) Y(l)).
+// A last panel of w < 32 reflectors has zero columns w .. 31 (tau 0).
+template <bool QT>
+__global__ void __launch_bounds__(256) apply_simt_kernel(const float *__restrict__ H, const float *__restrict__ S,
+                                                         int64_t s_stride, const float *__restrict__ tau, int n,
+                                                         int k, float *__restrict__ C, int64_t ncols,
+                                                         int64_t c_begin, int64_t c_end)
+{
+    __shared__ float Vs[32][33];
+    __shared__ float Cs[32][33];
+    __shared__ float Ws[32][33];
+    __shared__ float Ts[32][33];
+    const int lane = threadIdx.x & 31, tg = threadIdx.x >> 5;
+    const int64_t mat = blockIdx.y;
+    const int64_t c0 = c_begin + (int64_t)blockIdx.x * 32;
+    const int nct = (int)((c_end - c0) < 32 ? (c_end - c0) : 32);
+    const int m = n - k;
+    const int w = m < kPanel ? m : kPanel;
+    const float *Hm = H + mat * (int64_t)n * n;
+    float *Cm = C + mat * (int64_t)n * ncols;
+
+    // chunk of 32 rows: V (unit lower, columns >= w zero) and the C tile
+    auto load_chunk = [&](int r0) {
+        const int rr = r0 + lane;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int j = tg + 8 * i;
+            float v = 0.0f;
+            if (rr < m && j < w) v = rr > j ? Hm[(int64_t)(k + j) * n + k + rr] : (rr == j ? 1.0f : 0.0f);
+            Vs[lane][j] = v;
+            Cs[lane][j] = (rr < m && j < nct) ? Cm[(c0 + j) * n + k + rr] : 0.0f;
+        }
+    };
+
+    // W = V^T C : thread (c = lane, j = 4tg..4tg+3)
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int r0 = 0; r0 < m; r0 += 32) {
+        load_chunk(r0);
+        __syncthreads();
+#pragma unroll 8
+        for (int r = 0; r < 32; ++r) {
+            const float cv = Cs[r][lane];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) acc[q] = fmaf(Vs[r][4 * tg + q], cv, acc[q]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) Ws[4 * tg + q][lane] = acc[q];
+    const float *Sm = S + mat * s_stride;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int cc = tg + 8 * i;
+        Ts[lane][cc] = Sm[cc * kPanel + lane];  // S(lane, cc), column-major source
+    }
+    __syncthreads();
+    if (tg == 0) {
+        float y[32];
+        if constexpr (QT) {
+#pragma unroll
+            for (int c = 0; c < 32; ++c) {
+                float a = Ws[c][lane];
+#pragma unroll
+                for (int l = 0; l < c; ++l) a = fmaf(-Ts[l][c], y[l], a);
+                y[c] = (c < w ? tau[mat * n + k + c] : 0.0f) * a;
+            }
+        } else {
+#pragma unroll
+            for (int c = 31; c >= 0; --c) {
+                float a = Ws[c][lane];
+#pragma unroll
+                for (int l = c + 1; l < 32; ++l) a = fmaf(-Ts[c][l], y[l], a);
+                y[c] = (c < w ? tau[mat * n + k + c] : 0.0f) * a;
+            }
+        }
+#pragma unroll
+        for (int c = 0; c < 32; ++c) Ws[c][lane] = y[c];
+    }
+    __syncthreads();
+    float yreg[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) yreg[j] = Ws[j][lane];
+
+    // C -= V Y : staged per 32-row chunk, thread (c = lane, rows tg + 8i)
+    for (int r0 = 0; r0 < m; r0 += 32) {
+        load_chunk(r0);
+        __syncthreads();
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int r = tg + 8 * i;
+            float a = Cs[r][lane];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) a = fmaf(-Vs[r][j], yreg[j], a);
+            Cs[r][lane] = a;
+        }
+        __syncthreads();
+        const int rr = r0 + lane;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int j = tg + 8 * i;
+            if (rr < m && j < nct) Cm[(c0 + j) * n + k + rr] = Cs[lane][j];
+        }
+        __syncthreads();
+    }
+}
+
 bool apply_tc_ok(int64_t n, const void *H, const void *C)
 {
     return trailing_tc_supported((int)n) && ((uintptr_t)H % 16) == 0 && ((uintptr_t)C % 16) == 0;
@@ -143,11 +255,13 @@ int run_apply(const float *H, const float *tau, int64_t batch, int64_t n, float 
     if (!H || !tau || !C) return FQR_EINVAL;
     const int ni = (int)n;
     const bool tc = apply_tc_ok(n, H, C);
+    // n > 512 off the tensor-core path: the same blocked order with the SIMT
+    // update (apply_simt_kernel); smaller such n: one reflector at a time
+    const bool blocked = tc || n > kSmallMaxN;
     const size_t need = apply_ws_bytes(batch, n);
     // every argument check before the first CUDA call
-    if (!tc && n > kSmallMaxN) return FQR_EUNSUPPORTED;
-    if (tc && (!ws || ws_bytes < need)) return FQR_EWORKSPACE;
-    if (tc && ((uintptr_t)ws) % kWsAlign) return FQR_EINVAL;
+    if (blocked && (!ws || ws_bytes < need)) return FQR_EWORKSPACE;
+    if (blocked && ((uintptr_t)ws) % kWsAlign) return FQR_EINVAL;
     cudaError_t e;
     if (mode == 0) {
         const int64_t total = batch * n * n;
@@ -155,7 +269,7 @@ int run_apply(const float *H, const float *tau, int64_t batch, int64_t n, float 
         identity_kernel<<<(unsigned)blocks, 256, 0, st>>>(C, total, ni);
         if ((e = cudaGetLastError()) != cudaSuccess) return status_of(e);
     }
-    if (!tc) {
+    if (!blocked) {
         const int pitch = (ni + 31) / 32 * 32 + 4;
         const size_t smem = (size_t)kSmallCols * pitch * sizeof(float);
         if (smem > 48 * 1024 &&
@@ -181,9 +295,30 @@ int run_apply(const float *H, const float *tau, int64_t batch, int64_t n, float 
                                                                          S + b0 * panels * kPanel * kPanel);
         if ((e = cudaGetLastError()) != cudaSuccess) return status_of(e);
     }
+    const int64_t s_stride = (int64_t)panels * kPanel * kPanel;
+    if (!tc) {
+        for (int s = 0; s < panels; ++s) {
+            const int p = mode == 1 ? s : panels - 1 - s;
+            const int k = p * kPanel;
+            const int64_t cb = mode == 0 ? k : 0, ce = mode == 0 ? n : ncols;
+            for (int64_t b0 = 0; b0 < batch; b0 += 65535) {
+                const int64_t nb = (batch - b0) < 65535 ? (batch - b0) : 65535;
+                const dim3 grid((unsigned)((ce - cb + 31) / 32), (unsigned)nb);
+                const float *Sp = S + b0 * s_stride + (int64_t)p * kPanel * kPanel;
+                float *Cb = C + b0 * n * (mode == 0 ? n : ncols);
+                if (mode == 1)
+                    apply_simt_kernel<true><<<grid, 256, 0, st>>>(H + b0 * n * n, Sp, s_stride, tau + b0 * n, ni, k,
+                                                                  Cb, mode == 0 ? n : ncols, cb, ce);
+                else
+                    apply_simt_kernel<false><<<grid, 256, 0, st>>>(H + b0 * n * n, Sp, s_stride, tau + b0 * n, ni,
+                                                                   k, Cb, mode == 0 ? n : ncols, cb, ce);
+                if ((e = cudaGetLastError()) != cudaSuccess) return status_of(e);
+            }
+        }
+        return FQR_OK;
+    }
     TrailingMaps maps;
     if (prepare_apply_maps(H, ni, ni, C, mode == 0 ? n : ncols, batch, &maps) != cudaSuccess) return FQR_ECUDA;
-    const int64_t s_stride = (int64_t)panels * kPanel * kPanel;
     for (int s = 0; s < panels; ++s) {
         const int p = mode == 1 ? s : panels - 1 - s;
         const int k = p * kPanel;
@@ -202,7 +337,8 @@ extern "C" {
 
 size_t fqr_orgqr_workspace_bytes(int64_t batch, int64_t n)
 {
-    if (batch <= 0 || n <= 0 || n > FQR_MAX_N || !fqr::trailing_tc_supported((int)n)) return 0;
+    if (batch <= 0 || n <= 0 || n > FQR_MAX_N) return 0;
+    if (!fqr::trailing_tc_supported((int)n) && n <= fqr::kSmallMaxN) return 0;
     return fqr::apply_ws_bytes(batch, n);
 }
 

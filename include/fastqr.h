@@ -171,8 +171,10 @@ int fqr_host_check_status(const void *workspace, size_t workspace_bytes, int64_t
  * H, unit diagonal implied).  H and tau as fqr_geqrf_f32 returns them (device
  * pointers; H column-major per matrix, tau [batch][n]); Q: batch x n x n,
  * column-major like H.  workspace: fqr_orgqr_workspace_bytes(batch, n) bytes
- * (0 when n % 4 != 0 or n < 128: those sizes, up to n = 512, take a
- * reflector-by-reflector kernel; larger such n return FQR_EUNSUPPORTED).
+ * (0 for n <= 512 with n % 4 != 0 or n < 128: those sizes take a
+ * reflector-by-reflector kernel).  Larger n run panel by panel: on the tensor
+ * cores when n % 4 == 0 and H and Q (C) are 16-byte aligned, else with an
+ * FP32 SIMT update.
  * Replaces the reference's use of torch.linalg.householder_product in its
  * checker (official/reference.py:199).
  */

@@ -151,9 +151,12 @@ def test_orgqr_ormqr_validation_without_gpu():
     assert lib.fqr_orgqr_f32(None, None, -1, 8, None, None, 0, None) == 1
     assert lib.fqr_orgqr_f32(None, None, 0, 8, None, None, 0, None) == 0
     assert lib.fqr_orgqr_f32(dummy, dummy, 1, 8193, dummy, None, 0, None) == 2
-    # tensor-core sizes need the S workspace; odd sizes above 512 are unsupported
+    # blocked sizes (tensor-core ones, and every n above 512) need the S
+    # workspace; sizes up to 512 off the tensor-core path need none
     assert lib.fqr_orgqr_f32(dummy, dummy, 2, 256, dummy, None, 0, None) == 5
-    assert lib.fqr_orgqr_f32(dummy, dummy, 2, 514, dummy, None, 0, None) == 2
+    assert lib.fqr_orgqr_f32(dummy, dummy, 2, 514, dummy, None, 0, None) == 5
+    assert fastqr.orgqr_workspace_bytes(2, 514) == 2 * 17 * 32 * 32 * 4 + 256
+    assert fastqr.orgqr_workspace_bytes(2, 510) == 0
     assert lib.fqr_ormqr_f32(dummy, dummy, 2, 256, dummy, 10, 1, None, 0, None) == 5
     assert lib.fqr_ormqr_f32(None, dummy, 2, 256, dummy, 10, 1, None, 0, None) == 1
     # one 32 x 32 S block per panel per matrix + a status block

@@ -18,8 +18,9 @@ from fastqr import inputs
 
 pytestmark = pytest.mark.gpu
 
-# small path (n % 4 != 0 or n < 128) and tensor-core path sizes
-SIZES = [1, 8, 33, 64, 100, 130, 128, 256, 260, 384, 512]
+# small path (n % 4 != 0 or n < 128, up to 512), tensor-core path sizes, and
+# the blocked SIMT path (n > 512 off the tensor-core path: 514, 601)
+SIZES = [1, 8, 33, 64, 100, 130, 128, 256, 260, 384, 512, 514, 601]
 
 
 @pytest.fixture(scope="module")
@@ -65,7 +66,7 @@ def test_q_is_orthogonal_and_reconstructs(dev, n, batch):
     assert float(rec.max()) <= 1e-4
 
 
-@pytest.mark.parametrize("n,ncols", [(64, 7), (130, 1), (256, 64), (256, 300), (512, 129)])
+@pytest.mark.parametrize("n,ncols", [(64, 7), (130, 1), (256, 64), (256, 300), (512, 129), (514, 200), (601, 37)])
 @pytest.mark.parametrize("transpose", [True, False])
 def test_ormqr_matches_oracle(dev, n, ncols, transpose):
     a, h, tau = factor(2, n, 1, 40 + n, dev)
@@ -106,9 +107,9 @@ def test_row_major_factors_and_errors(dev):
     q1 = fastqr.householder_product(h, tau)
     q2 = fastqr.householder_product(h.contiguous(), tau)  # row-major copy of H
     assert torch.equal(q1, q2)
-    with pytest.raises(fastqr.FastQRError):
-        hb = torch.zeros(1, 514, 514, device=dev)
-        fastqr.householder_product(hb, torch.zeros(1, 514, device=dev))
+    with pytest.raises(fastqr.FastQRError):  # n above FQR_MAX_N
+        hb = torch.zeros(1, 8200, 8200, device=dev)
+        fastqr.householder_product(hb, torch.zeros(1, 8200, device=dev))
     with pytest.raises(ValueError):
         fastqr.ormqr(h, tau, torch.zeros(2, 127, 3, device=dev))
 
@@ -125,7 +126,7 @@ def test_column_range_update_leaves_other_columns(dev):
     assert frob(out.cpu().double().numpy() - want) / frob(want) <= 1e-5
 
 
-@pytest.mark.parametrize("n", [64, 100, 256, 384])
+@pytest.mark.parametrize("n", [64, 100, 256, 384, 601])
 @pytest.mark.parametrize("mrows", [1, 50, 256])
 @pytest.mark.parametrize("transpose", [False, True])
 def test_ormqr_right_side_matches_torch_float64(dev, n, mrows, transpose):
@@ -145,3 +146,28 @@ def test_ormqr_right_side_matches_torch_float64(dev, n, mrows, transpose):
     assert back.data_ptr() == out.data_ptr()
     rt = ((back.double() - c.double()).flatten(1).norm(dim=1) / c.double().flatten(1).norm(dim=1)).max()
     assert float(rt) <= 1e-5, float(rt)
+
+
+def test_unaligned_factors_take_the_simt_blocked_path(dev):
+    """n = 640 with H and C one float off 16-byte alignment: the tensor-core
+    update cannot take them, so Q, Q^T C and Q C come from the blocked SIMT
+    path; they agree with the aligned (tensor-core) results to 1e-5."""
+    n, batch = 640, 2
+    a, h, tau = factor(batch, n, 0, 17, dev)
+    buf = torch.empty(batch * n * n + 1, device=dev)
+    hs = buf[1:].as_strided((batch, n, n), (n * n, 1, n))
+    hs.copy_(h)
+    assert hs.data_ptr() % 16 != 0
+    q = fastqr.householder_product(h, tau)
+    qs = fastqr.householder_product(hs, tau)
+    assert float((qs - q).abs().max()) <= 1e-5
+    c = torch.randn(batch, n, 70, device=dev)
+    cbuf = torch.empty(batch * n * 70 + 1, device=dev)
+    cs = cbuf[1:].as_strided((batch, n, 70), (n * 70, 1, n))
+    for transpose in (True, False):
+        want = fastqr.ormqr(h, tau, c, transpose=transpose)
+        cs.copy_(c)
+        got = fastqr.ormqr(hs, tau, cs, transpose=transpose, out=cs)
+        assert got.data_ptr() % 16 != 0
+        err = torch.linalg.matrix_norm(got - want) / torch.linalg.matrix_norm(want)
+        assert float(err.max()) <= 1e-5, float(err.max())
