@@ -6,7 +6,9 @@ at most 65,535 matrices.  A batch of two or more runs as two stream parts at
 n < 2048, so a part passes that limit only beyond 131,070 matrices: 140,000
 matrices here, at n = 100 (the SIMT update) and n = 128 (the tensor-core
 update).  Matrices on both sides of every boundary (piece and part) are
-checked with the official gates and against the same matrix factored alone.
+checked with the official gates and against the same matrix factored alone,
+and Q formed for the whole batch (fastqr.householder_product, whose
+launchers cut batches the same way) against Q of the matrix alone.
 """
 import pytest
 import torch
@@ -43,3 +45,9 @@ def test_batch_beyond_the_grid_limit(dev, n):
         err = float((h1[0] - h_s[j]).abs().max() / h1[0].abs().max().clamp_min(1e-30))
         assert err <= 1e-5, (i, err)
         assert float((t1[0] - t_s[j]).abs().max()) <= 1e-5, i
+    del a
+    q = fastqr.householder_product(h, tau)
+    torch.cuda.synchronize()
+    for i in picks:
+        q1 = fastqr.householder_product(h[i : i + 1], tau[i : i + 1])
+        assert float((q1[0] - q[i]).abs().max()) <= 1e-5, i
